@@ -1,0 +1,177 @@
+/*
+ * phew_b200.h — C ABI of the B200 execution backend for phew's
+ * candidate-evaluation path.
+ *
+ * The reference reaches its device through MLX: `mx.fast.metal_kernel`
+ * objects built from generated MSL, the `mx.fast.*` primitives that the
+ * primitive-substitution pass emits, `a @ b`, `mx.softmax`, and the
+ * numpy comparison loop of its equivalence checker.  Each entry point below
+ * replaces one of those call sites; the comment on each names the reference
+ * file:line it stands in for (paths relative to the phew project root).
+ *
+ * Conventions
+ *   - Every function returns an int status: PHEW_OK (0) or a PHEW_ERR_* code.
+ *     phew_last_error() returns the message of the last failure on the
+ *     calling thread.
+ *   - Pointers named x/y/q/k/v/... are DEVICE pointers of the current CUDA
+ *     device (in practice `torch.Tensor.data_ptr()`).  The library never
+ *     frees memory it did not allocate.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ *     stream).  All work is asynchronous on that stream.
+ *   - dtype codes: PHEW_F32, PHEW_F16, PHEW_BF16 (phew.ir.dtype.Dtype
+ *     float32 / float16 / bfloat16, ir/dtype.py:6-9).
+ *   - Shapes are row-major and contiguous unless strides are given.
+ */
+#ifndef PHEW_B200_H
+#define PHEW_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define PHEW_OK 0
+#define PHEW_ERR_INVALID 1     /* bad argument (null pointer, bad shape, bad dtype) */
+#define PHEW_ERR_CUDA 2        /* a CUDA runtime call failed */
+#define PHEW_ERR_COMPILE 3     /* NVRTC compilation failed; log in phew_last_error */
+#define PHEW_ERR_UNSUPPORTED 4 /* valid request this build does not implement */
+#define PHEW_ERR_TIMEOUT 5     /* a bounded device-side wait gave up */
+#define PHEW_ERR_NOT_FOUND 6   /* unknown kernel handle or symbol */
+
+/* ---- dtype codes ------------------------------------------------------- */
+#define PHEW_F32 0
+#define PHEW_F16 1
+#define PHEW_BF16 2
+
+/* ---- reduction op codes (phew.ir.ops.Reduce.op, ir/ops.py:43-52) -------- */
+#define PHEW_REDUCE_SUM 0
+#define PHEW_REDUCE_MEAN 1
+#define PHEW_REDUCE_MAX 2
+#define PHEW_REDUCE_MIN 3
+#define PHEW_REDUCE_PROD 4
+
+/* ---- library / device -------------------------------------------------- */
+
+/* ABI version of this library (bumped on any signature change). */
+int phew_abi_version(void);
+
+/* Copies the calling thread's last error message into buf (NUL-terminated,
+ * truncated to len).  Returns the length of the full message. */
+int phew_last_error(char* buf, size_t len);
+
+/* Selects `device` for the calling thread and caches its properties.
+ * Replaces the implicit MLX device setup behind `mx.metal.is_available()` /
+ * `mx.device_info()` (optimizer.py:114-116). */
+int phew_init(int device);
+
+typedef struct phew_device_info {
+  int sm_count;
+  int cc_major;
+  int cc_minor;
+  int max_smem_per_block_optin;
+  int64_t l2_bytes;
+  int64_t hbm_bytes;
+  char name[128];
+} phew_device_info;
+
+int phew_device_query(int device, phew_device_info* out);
+
+/* ---- runtime-compiled kernels (NVRTC, sm_100a) ------------------------- */
+
+/* Compiles CUDA C++ `source` with NVRTC for sm_100a and loads kernel
+ * `kernel_name` (an extern "C" __global__ symbol of the source).  Results are
+ * cached by a hash of (source, kernel_name); *handle identifies the kernel.
+ * On PHEW_ERR_COMPILE the NVRTC log is available from phew_last_error().
+ * Replaces `mx.fast.metal_kernel(name, input_names, output_names, source,
+ * header)` kernel construction (ir/importer.py:55-94, emit/codegen.py:488-495),
+ * whose MSL MLX JIT-compiles on first call. */
+int phew_compile(const char* source, const char* kernel_name, uint64_t* handle);
+
+/* Launches a compiled kernel.  `args` holds `nargs` pointers to the argument
+ * values (cudaLaunchKernel convention).  grid/block are in blocks/threads.
+ * Replaces the call of a metal_kernel object (emit/codegen.py:584-592). */
+int phew_launch(uint64_t handle, void** args, int nargs,
+                unsigned grid_x, unsigned grid_y, unsigned grid_z,
+                unsigned block_x, unsigned block_y, unsigned block_z,
+                size_t dynamic_smem, void* stream);
+
+/* Number of kernels currently held in the compile cache. */
+int phew_compile_cache_size(void);
+
+/* ---- hand-written primitives ------------------------------------------- */
+
+/* y[r, :] = w * cast(x[r, :] * rsqrt(mean(x[r, :]^2) + eps)); w may be NULL
+ * (no weight).  Sum of squares in fp32.  x, w, y share `dtype`.
+ * Replaces `mx.fast.rms_norm(x, w, eps)` (emit/codegen.py:401-404, node
+ * FastRMSNorm ir/ops.py:156-161 from rules/primitive_subst.py:63-145). */
+int phew_rms_norm(const void* x, const void* w, void* y, int64_t rows,
+                  int64_t cols, float eps, int dtype, void* stream);
+
+/* Row softmax over the last axis, fp32 internally, result in `dtype`.
+ * Replaces `mx.softmax(x, axis=-1)` (emit/codegen.py:147-150; Reduce op
+ * "softmax" recorded at ir/importer.py:494-506). */
+int phew_softmax(const void* x, void* y, int64_t rows, int64_t cols,
+                 int dtype, void* stream);
+
+/* Reduction of x viewed as [outer, red, inner] over the middle axis into
+ * y[outer, inner].  fp32 accumulation; y has the dtype of x.
+ * Replaces mx.sum/mean/max/min/prod (emit/codegen.py:94-146). */
+int phew_reduce(int op, const void* x, void* y, int64_t outer, int64_t red,
+                int64_t inner, int dtype, void* stream);
+
+/* dst (contiguous) = src viewed with `shape` and element `src_strides`
+ * (ndim <= 8).  Materialises Transpose / non-contiguous views
+ * (emit/codegen.py:312-317 `mx.transpose`). */
+int phew_copy_strided(const void* src, void* dst, int ndim,
+                      const int64_t* shape, const int64_t* src_strides,
+                      int elem_bytes, void* stream);
+
+/* Writes `bytes` bytes of `buf` so that the L2 holds none of the caller's
+ * data afterwards (buf must be larger than the L2).  Used between timed
+ * iterations; replaces nothing in the reference (bench/harness.py:28-90
+ * times warm caches). */
+int phew_l2_flush(void* buf, size_t bytes, void* stream);
+
+/* ---- equivalence comparison -------------------------------------------- */
+
+/* Result of one baseline/candidate comparison, written to DEVICE memory. */
+typedef struct phew_compare_stats {
+  double sum_abs_base;      /* sum |b| over all elements (fp64, fixed order)   */
+  double mean_abs_base;     /* sum_abs_base / n                                */
+  double max_abs_diff;      /* max |b - c| over pairs where both are finite    */
+  double atol_used;         /* tolerance actually applied (after bf16 relax)   */
+  double rtol_used;
+  int64_t n;                /* elements compared                               */
+  int64_t n_nonfinite_base; /* count of NaN/Inf in the baseline               */
+  int64_t n_mismatch;       /* elements failing the allclose rule              */
+  int64_t n_nan_any;        /* elements where b or c is NaN                    */
+  int32_t skipped;          /* 1 = comparison skipped (non-finite baseline, or
+                               bf16 with mean|b| > 1e10)                        */
+  int32_t passed;           /* 1 = the allclose rule held (or skipped)         */
+} phew_compare_stats;
+
+/* Bytes of scratch phew_compare needs for n elements. */
+size_t phew_compare_scratch_bytes(int64_t n);
+
+/* Compares baseline `b` against candidate `c` (n elements of `dtype`) with
+ * the rule of the reference's equivalence checker (verify/checker.py:144-209
+ * and _allclose :220-233): skip when the baseline holds a non-finite value;
+ * for bf16, skip when mean|b| > 1e10, else relax to atol = max(atol,
+ * mean|b| * f), rtol = max(rtol, f) with f = 0.30 if mean|b| > 1e6 else 0.05;
+ * pass iff NaN positions agree and |b - c| <= atol + rtol * |c| (or b == c),
+ * evaluated in the arithmetic numpy uses for that dtype (fp16 math for fp16
+ * outputs, fp32 otherwise).  `scratch` (device, phew_compare_scratch_bytes(n)
+ * bytes, caller-owned) holds per-block partial results.  `out` is a device
+ * pointer.  Deterministic: the same inputs give the same bits on any GPU. */
+int phew_compare(const void* b, const void* c, int64_t n, int dtype,
+                 double atol, double rtol, void* scratch, size_t scratch_bytes,
+                 phew_compare_stats* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PHEW_B200_H */

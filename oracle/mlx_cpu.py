@@ -1,0 +1,568 @@
+"""ORACLE -- test infrastructure only.
+
+A CPU restatement of the MLX-CPU evaluation that phew's candidate path is
+checked against.  Only ``tests/``, ``__graft_entry__.smoke()`` and
+``bench.py``'s CPU-baseline leg (``cpu_baseline`` / ``--impl reference``)
+may import it, and only as the checker or the timed CPU baseline -- never as
+part of the product path.
+
+Parity status
+-------------
+* Numerics: PARITY UNPINNED.  The reference evaluates through MLX 0.31.2 /
+  mlx-metal 0.31.2 (phew ``uv.lock:399-400,434-435``), which is not
+  installed here, and the reference's tests pin no numeric results at that
+  boundary.  This module restates MLX's op semantics from the reference's
+  call sites: op order from ``emit/codegen.py:94-476``, fused-kernel
+  arithmetic from ``emit/msl_codegen.py:184-330`` (every node rounded to its
+  dtype), ``FastRMSNorm`` eps default from ``ir/ops.py:156-161``, SDPA scale
+  from ``rules/primitive_subst.py:457-472`` with the mask dropped
+  (``:490-495``).
+* Verdict logic (``oracle/verdict.py``): PINNED against the reference's own
+  ``EquivalenceChecker._allclose``, ``TOLERANCES`` and bench ``compare`` /
+  ``check_convergence`` via committed golden fixtures
+  (``tests/golden/make_golden.py``).
+
+Semantics restated here (MLX-CPU):
+* elementwise ops compute in fp32 and round the result to the node dtype;
+* Python scalars are weak (take the array's dtype; ``_TracedArray._binop``,
+  ``ir/importer.py:171-186``, records them as Constants of that dtype);
+* reductions, softmax, rms_norm and SDPA accumulate in float64 and round
+  once to the output dtype; matmul accumulates in fp32 (BLAS sgemm);
+* ``fast.rms_norm``: y = w * T(x * rsqrt(mean(x^2) + eps)).
+"""
+
+from __future__ import annotations
+
+import math
+import types
+from typing import Any
+
+import ml_dtypes
+import numpy as np
+from scipy import special as _sp
+
+BF16 = np.dtype(ml_dtypes.bfloat16)
+
+_NP = {
+    "float32": np.dtype(np.float32),
+    "float16": np.dtype(np.float16),
+    "bfloat16": BF16,
+    "int8": np.dtype(np.int8),
+    "int16": np.dtype(np.int16),
+    "int32": np.dtype(np.int32),
+    "int64": np.dtype(np.int64),
+    "uint8": np.dtype(np.uint8),
+    "uint16": np.dtype(np.uint16),
+    "uint32": np.dtype(np.uint32),
+    "uint64": np.dtype(np.uint64),
+    "bool": np.dtype(np.bool_),
+}
+
+
+class Dtype:
+    def __init__(self, name: str) -> None:
+        self.name = name
+        self.np = _NP[name]
+        self.size = self.np.itemsize
+        self.kind = "f" if name in ("float32", "float16", "bfloat16") else (
+            "b" if name == "bool" else ("u" if name.startswith("uint") else "i"))
+
+    @property
+    def value(self) -> str:
+        return self.name
+
+    def __repr__(self) -> str:
+        return f"oracle.{self.name}"
+
+
+float32, float16, bfloat16 = Dtype("float32"), Dtype("float16"), Dtype("bfloat16")
+int8, int16, int32, int64 = Dtype("int8"), Dtype("int16"), Dtype("int32"), Dtype("int64")
+uint8, uint16, uint32, uint64 = Dtype("uint8"), Dtype("uint16"), Dtype("uint32"), Dtype("uint64")
+bool_ = Dtype("bool")
+_BY_NAME = {d.name: d for d in (float32, float16, bfloat16, int8, int16, int32, int64, uint8,
+                                uint16, uint32, uint64, bool_)}
+_BY_NAME["bool_"] = bool_
+
+
+def as_dtype(d: Any) -> Dtype:
+    if isinstance(d, Dtype):
+        return d
+    v = getattr(d, "value", None) or getattr(d, "name", None)
+    if isinstance(v, str) and v in _BY_NAME:
+        return _BY_NAME[v]
+    if isinstance(d, str):
+        return _BY_NAME[d]
+    nd = np.dtype(d)
+    if nd == BF16:
+        return bfloat16
+    if nd == np.float64:
+        return float32
+    return _BY_NAME["bool" if nd == np.bool_ else nd.name]
+
+
+def round_to(x: np.ndarray, d: Dtype) -> np.ndarray:
+    """Round values (any float array) to dtype `d`, returned in dtype `d`."""
+    if d.kind == "f":
+        return np.asarray(x, dtype=np.float32).astype(d.np)
+    return np.asarray(x).astype(d.np)
+
+
+def f32(x: np.ndarray) -> np.ndarray:
+    return np.asarray(x).astype(np.float32)
+
+
+def _promote(a: Dtype, b: Dtype) -> Dtype:
+    if a is b:
+        return a
+    if a.kind == "f" and b.kind == "f":
+        if {a.name, b.name} == {"float16", "bfloat16"}:
+            return float32
+        rank = {"float16": 1, "bfloat16": 1, "float32": 2}
+        return a if rank[a.name] >= rank[b.name] else b
+    if a.kind == "f":
+        return a
+    if b.kind == "f":
+        return b
+    if a.kind == "b":
+        return b
+    if b.kind == "b":
+        return a
+    return a if a.size >= b.size else b
+
+
+class array:
+    """Host array with an MLX dtype; values stored in that dtype."""
+
+    __array_priority__ = 100
+
+    def __init__(self, val: Any, dtype: Any = None) -> None:
+        if isinstance(val, array):
+            v = val.v if dtype is None else round_to(f32(val.v) if val.dtype.kind == "f" else val.v, as_dtype(dtype))
+            self.v = v
+            self.dtype = val.dtype if dtype is None else as_dtype(dtype)
+            return
+        a = np.asarray(val)
+        if dtype is None:
+            if a.dtype == np.float64:
+                d = float32
+            elif a.dtype == np.int64 and not isinstance(val, np.ndarray):
+                d = int32
+            else:
+                d = as_dtype(a.dtype)
+        else:
+            d = as_dtype(dtype)
+        self.dtype = d
+        self.v = round_to(a.astype(np.float64) if d.kind == "f" and a.dtype.kind != "V" and a.dtype != BF16 else a, d)
+
+    @classmethod
+    def wrap(cls, v: np.ndarray, d: Dtype) -> "array":
+        a = object.__new__(cls)
+        a.v = v
+        a.dtype = d
+        return a
+
+    @property
+    def shape(self):
+        return tuple(self.v.shape)
+
+    @property
+    def size(self):
+        return int(self.v.size)
+
+    @property
+    def ndim(self):
+        return self.v.ndim
+
+    def __array__(self, dtype=None, copy=None):
+        out = self.v
+        return out.astype(dtype) if dtype is not None else out
+
+    def astype(self, d):
+        return astype(self, d)
+
+    @property
+    def T(self):
+        return transpose(self)
+
+    def transpose(self, *axes):
+        if len(axes) == 1 and isinstance(axes[0], (list, tuple)):
+            axes = tuple(axes[0])
+        return transpose(self, axes or None)
+
+    def reshape(self, *shape):
+        if len(shape) == 1 and isinstance(shape[0], (list, tuple)):
+            shape = tuple(shape[0])
+        return array.wrap(self.v.reshape(shape), self.dtype)
+
+    def swapaxes(self, a, b):
+        return array.wrap(np.swapaxes(self.v, a, b), self.dtype)
+
+    def __getitem__(self, idx):
+        return array.wrap(self.v[idx], self.dtype)
+
+    def sum(self, axis=None, keepdims=False):
+        return sum(self, axis, keepdims)
+
+    def mean(self, axis=None, keepdims=False):
+        return mean(self, axis, keepdims)
+
+    def max(self, axis=None, keepdims=False):
+        return max(self, axis, keepdims)
+
+    def __add__(self, o):
+        return _ew("add", self, o)
+
+    def __radd__(self, o):
+        return _ew("add", o, self)
+
+    def __sub__(self, o):
+        return _ew("sub", self, o)
+
+    def __rsub__(self, o):
+        return _ew("sub", o, self)
+
+    def __mul__(self, o):
+        return _ew("mul", self, o)
+
+    def __rmul__(self, o):
+        return _ew("mul", o, self)
+
+    def __truediv__(self, o):
+        return _ew("div", self, o)
+
+    def __rtruediv__(self, o):
+        return _ew("div", o, self)
+
+    def __neg__(self):
+        return _ew("negative", self)
+
+    def __matmul__(self, o):
+        return matmul(self, o)
+
+
+# ---------------------------------------------------------------------------
+# elementwise (fp32 compute, result rounded to the node dtype)
+# ---------------------------------------------------------------------------
+
+
+def _sigmoid(a):
+    with np.errstate(over="ignore"):
+        return np.float32(1.0) / (np.float32(1.0) + np.exp(-a))
+
+
+def _maximum(a, b):
+    return np.maximum(a, b)
+
+
+def _remainder(a, b):
+    return np.remainder(a, b)
+
+
+FLOAT_OPS = {
+    "add": lambda a, b: a + b,
+    "sub": lambda a, b: a - b,
+    "mul": lambda a, b: a * b,
+    "div": lambda a, b: a / b,
+    "negative": lambda a: -a,
+    "abs": np.abs,
+    "exp": np.exp,
+    "log": np.log,
+    "sqrt": np.sqrt,
+    "rsqrt": lambda a: np.float32(1.0) / np.sqrt(a),
+    "sigmoid": _sigmoid,
+    "tanh": np.tanh,
+    "relu": lambda a: np.maximum(a, np.float32(0.0)),
+    "gelu": lambda a: (a * np.float32(0.5)) * (np.float32(1.0) + _sp.erf(a * np.float32(0.70710678118654752))).astype(np.float32),
+    "silu": lambda a: a / (np.float32(1.0) + np.exp(-a)),
+    "cos": np.cos,
+    "sin": np.sin,
+    "tan": np.tan,
+    "arctan": np.arctan,
+    "arcsin": np.arcsin,
+    "arccos": np.arccos,
+    "arctanh": np.arctanh,
+    "arcsinh": np.arcsinh,
+    "arccosh": np.arccosh,
+    "cosh": np.cosh,
+    "sinh": np.sinh,
+    "degrees": lambda a: a * np.float32(57.295779513082320876),
+    "radians": lambda a: a * np.float32(0.017453292519943295769),
+    "square": lambda a: a * a,
+    "maximum": _maximum,
+    "minimum": np.minimum,
+    "logaddexp": np.logaddexp,
+    "ceil": np.ceil,
+    "floor": np.floor,
+    "round": np.rint,
+    "sign": np.sign,
+    "reciprocal": lambda a: np.float32(1.0) / a,
+    "erf": lambda a: _sp.erf(a).astype(np.float32),
+    "erfinv": lambda a: _sp.erfinv(a).astype(np.float32),
+    "expm1": np.expm1,
+    "log1p": np.log1p,
+    "log2": np.log2,
+    "log10": np.log10,
+    "floor_divide": lambda a, b: np.floor(a / b),
+    "remainder": _remainder,
+    "power": np.power,
+    "arctan2": np.arctan2,
+}
+ALIASES = {"multiply": "mul", "subtract": "sub", "divide": "div", "neg": "negative"}
+COMPARE = {"eq": np.equal, "ne": np.not_equal, "gt": np.greater, "ge": np.greater_equal,
+           "lt": np.less, "le": np.less_equal}
+
+
+def _operand(x, d: Dtype):
+    if isinstance(x, array):
+        return x.v
+    return round_to(np.asarray(x, dtype=np.float64 if d.kind == "f" else None), d)
+
+
+def apply_op(op: str, args: list[np.ndarray], out: Dtype) -> np.ndarray:
+    """One elementwise node: inputs already in their node dtypes."""
+    op = ALIASES.get(op, op)
+    if op in COMPARE:
+        r = COMPARE[op](*[f32(a) if out.kind == "f" or a.dtype.kind == "f" else a for a in args])
+        return round_to(r, out)
+    if op == "where":
+        return round_to(np.where(args[0].astype(bool), f32(args[1]), f32(args[2])), out)
+    if op == "logical_not":
+        return round_to(np.logical_not(args[0]), out)
+    if op in ("logical_and", "logical_or"):
+        f = np.logical_and if op == "logical_and" else np.logical_or
+        return round_to(f(args[0], args[1]), out)
+    if out.kind != "f":
+        f = {"add": np.add, "sub": np.subtract, "mul": np.multiply, "negative": np.negative,
+             "abs": np.abs, "maximum": np.maximum, "minimum": np.minimum,
+             "floor_divide": np.floor_divide, "remainder": np.remainder, "square": np.square,
+             "sign": np.sign}[op]
+        return f(*[a.astype(out.np) for a in args]).astype(out.np)
+    with np.errstate(all="ignore"):
+        r = FLOAT_OPS[op](*[f32(a) for a in args])
+    return round_to(np.asarray(r, dtype=np.float32), out)
+
+
+def _ew(op: str, *operands) -> array:
+    arrays = [x for x in operands if isinstance(x, array)]
+    res = arrays[0].dtype
+    for a in arrays[1:]:
+        res = _promote(res, a.dtype)
+    for x in operands:
+        if not isinstance(x, array) and isinstance(x, float) and res.kind != "f":
+            res = float32
+    args = []
+    for x in operands:
+        if isinstance(x, array):
+            args.append(x.v if x.dtype is res else round_to(f32(x.v) if x.dtype.kind == "f" else x.v, res))
+        else:
+            args.append(_operand(x, res))
+    return array.wrap(apply_op(op, args, res), res)
+
+
+def _unary_fn(op):
+    return lambda x, *_, **__: _ew(op, x)
+
+
+for _op in ("exp", "log", "sqrt", "rsqrt", "sigmoid", "tanh", "abs", "negative", "square", "sin",
+            "cos", "erf", "erfinv", "expm1", "log1p", "log2", "log10", "ceil", "floor", "round",
+            "sign", "reciprocal", "arctan", "arcsin", "arccos", "sinh", "cosh", "relu", "gelu",
+            "silu"):
+    globals()[_op] = _unary_fn(_op)
+
+maximum = lambda a, b: _ew("maximum", a, b)  # noqa: E731
+minimum = lambda a, b: _ew("minimum", a, b)  # noqa: E731
+power = lambda a, b: _ew("power", a, b)  # noqa: E731
+add = lambda a, b: _ew("add", a, b)  # noqa: E731
+multiply = lambda a, b: _ew("mul", a, b)  # noqa: E731
+subtract = lambda a, b: _ew("sub", a, b)  # noqa: E731
+divide = lambda a, b: _ew("div", a, b)  # noqa: E731
+
+
+def astype(a: array, d) -> array:
+    d = as_dtype(d)
+    if a.dtype is d:
+        return a
+    if d.kind == "f":
+        return array.wrap(round_to(f32(a.v), d), d)
+    if a.dtype.kind == "f":
+        return array.wrap(np.trunc(f32(a.v)).astype(d.np), d)
+    return array.wrap(a.v.astype(d.np), d)
+
+
+def where(c, a, b):
+    cv = c.v if isinstance(c, array) else np.asarray(c)
+    res = a.dtype if isinstance(a, array) else b.dtype
+    av = _operand(a, res) if not isinstance(a, array) else astype(a, res).v
+    bv = _operand(b, res) if not isinstance(b, array) else astype(b, res).v
+    return array.wrap(round_to(np.where(cv.astype(bool), f32(av), f32(bv)), res), res)
+
+
+# ---------------------------------------------------------------------------
+# reductions, softmax, matmul, fast.*
+# ---------------------------------------------------------------------------
+
+
+def _axes(a: array, axis):
+    if axis is None:
+        return tuple(range(a.ndim))
+    if isinstance(axis, (list, tuple)):
+        return tuple(int(x) % a.ndim for x in axis)
+    return (int(axis) % a.ndim,)
+
+
+def _reduce(fn, a: array, axis, keepdims) -> array:
+    ax = _axes(a, axis)
+    with np.errstate(all="ignore"):
+        r = fn(a.v.astype(np.float64), axis=ax, keepdims=keepdims)
+    return array.wrap(round_to(r, a.dtype), a.dtype)
+
+
+def sum(a, axis=None, keepdims=False, **_):  # noqa: A001
+    return _reduce(np.sum, a, axis, keepdims)
+
+
+def mean(a, axis=None, keepdims=False, **_):
+    return _reduce(np.mean, a, axis, keepdims)
+
+
+def max(a, axis=None, keepdims=False, **_):  # noqa: A001
+    return _reduce(np.max, a, axis, keepdims)
+
+
+def min(a, axis=None, keepdims=False, **_):  # noqa: A001
+    return _reduce(np.min, a, axis, keepdims)
+
+
+def _softmax64(x: np.ndarray, axis: int) -> np.ndarray:
+    with np.errstate(all="ignore"):
+        m = np.max(x, axis=axis, keepdims=True)
+        e = np.exp(x - m)
+        return e / np.sum(e, axis=axis, keepdims=True)
+
+
+def softmax(a, axis=-1, **_):
+    if isinstance(axis, (list, tuple)):
+        axis = axis[0]
+    return array.wrap(round_to(_softmax64(a.v.astype(np.float64), int(axis)), a.dtype), a.dtype)
+
+
+def matmul(a, b):
+    res = _promote(a.dtype, b.dtype)
+    r = np.matmul(f32(a.v), f32(b.v))
+    return array.wrap(round_to(r, res), res)
+
+
+def transpose(a, axes=None):
+    return array.wrap(np.transpose(a.v, axes), a.dtype)
+
+
+def swapaxes(a, x, y):
+    return array.wrap(np.swapaxes(a.v, x, y), a.dtype)
+
+
+def reshape(a, shape):
+    return array.wrap(a.v.reshape(shape), a.dtype)
+
+
+def zeros_like(a):
+    return array.wrap(np.zeros(a.shape, a.dtype.np), a.dtype)
+
+
+def zeros(shape, dtype=float32):
+    d = as_dtype(dtype)
+    return array.wrap(np.zeros(shape, d.np), d)
+
+
+def ones(shape, dtype=float32):
+    d = as_dtype(dtype)
+    return array.wrap(np.ones(shape, d.np), d)
+
+
+def eval(*_):  # noqa: A001
+    return None
+
+
+def synchronize(*_):
+    return None
+
+
+def compile(fn=None, **_):  # noqa: A001
+    return fn if fn is not None else (lambda f: f)
+
+
+def rms_norm(x: array, weight: array | None = None, eps: float = 1e-5) -> array:
+    """fast.rms_norm: fp32 mean of squares, then y = w * T(x * r)."""
+    xv = f32(x.v)
+    ms = np.float32(np.mean(xv.astype(np.float64) ** 2, axis=-1, keepdims=True))
+    r = (np.float32(1.0) / np.sqrt(ms + np.float32(eps))).astype(np.float32)
+    n = round_to(xv * r, x.dtype)
+    if weight is None:
+        return array.wrap(n, x.dtype)
+    return array.wrap(round_to(f32(weight.v) * f32(n), x.dtype), x.dtype)
+
+
+def sdpa(q: array, k: array, v: array, scale: float, mask: Any = None) -> array:
+    """softmax(q k^T * scale [+ mask]) v, fp32 matmuls, float64 softmax."""
+    s = np.matmul(f32(q.v), np.swapaxes(f32(k.v), -1, -2)) * np.float32(scale)
+    s = s.astype(np.float64)
+    if isinstance(mask, str) and mask == "causal":
+        L, S = s.shape[-2], s.shape[-1]
+        s = np.where(np.tril(np.ones((L, S), dtype=bool), k=S - L), s, -np.inf)
+    elif mask is not None:
+        s = s + f32(mask.v if isinstance(mask, array) else mask)
+    p = _softmax64(s, -1).astype(np.float32)
+    o = np.matmul(p, f32(v.v))
+    return array.wrap(round_to(o, q.dtype), q.dtype)
+
+
+fast = types.SimpleNamespace(
+    rms_norm=rms_norm,
+    scaled_dot_product_attention=lambda q, k, v, *, scale=1.0, mask=None, **_: sdpa(q, k, v, scale, mask),
+)
+
+
+# ---------------------------------------------------------------------------
+# fused-chain evaluation (node by node, each rounded to its dtype)
+# ---------------------------------------------------------------------------
+
+
+def _kind(n) -> str:
+    return getattr(n, "kind", None) or type(n).__name__
+
+
+def _dname(d) -> str:
+    v = getattr(d, "value", None)
+    if isinstance(v, str):
+        d = v
+    d = str(d)
+    return "bool" if d == "bool_" else d
+
+
+def eval_chain(nodes, ext_inputs, ext_outputs, values: list[np.ndarray]) -> list[np.ndarray]:
+    """Evaluate an Elementwise/Cast/Constant chain the way the MSL kernel and
+    MLX's op-by-op evaluation do (``msl_codegen.py:184-330``)."""
+    env: dict[int, np.ndarray] = {}
+    out_shape = tuple(ext_outputs[0].shape)
+    for node, v in zip(ext_inputs, values):
+        env[node.id] = np.asarray(v)
+    for node in nodes:
+        kind = _kind(node)
+        d = as_dtype(_dname(node.dtype))
+        if kind == "Constant":
+            env[node.id] = round_to(np.asarray(float(np.float32(node.value)) if d.kind == "f" else node.value), d)
+        elif kind == "Cast":
+            t = as_dtype(_dname(getattr(node, "target_dtype", node.dtype)))
+            env[node.id] = astype(array.wrap(env[node.inputs[0]], as_dtype(env[node.inputs[0]].dtype)), t).v
+        else:
+            args = [env[i] for i in node.inputs]
+            env[node.id] = apply_op(node.op, args, d)
+    return [np.broadcast_to(env[o.id], out_shape).copy() for o in ext_outputs]
+
+
+def to_float(x) -> np.ndarray:
+    """Values of an oracle/device/numpy array as float32 numpy."""
+    v = x.v if isinstance(x, array) else np.asarray(x)
+    return v.astype(np.float32)
+
+
+__all__ = [n for n in dir() if not n.startswith("_")]

@@ -1,0 +1,168 @@
+"""ctypes binding of ``libphew_b200.so`` (declared in ``include/phew_b200.h``).
+
+The library is the only way this package reaches the GPU: there is no
+Python or CPU fallback.  Loading fails loudly when the library is missing.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libphew_b200.so"
+
+PHEW_OK = 0
+PHEW_ERR_INVALID = 1
+PHEW_ERR_CUDA = 2
+PHEW_ERR_COMPILE = 3
+PHEW_ERR_UNSUPPORTED = 4
+PHEW_ERR_TIMEOUT = 5
+PHEW_ERR_NOT_FOUND = 6
+
+PHEW_F32 = 0
+PHEW_F16 = 1
+PHEW_BF16 = 2
+
+REDUCE_OPS = {"sum": 0, "mean": 1, "max": 2, "min": 3, "prod": 4}
+
+# Every symbol the header declares; tests check that each one is exported.
+EXPORTED_SYMBOLS = (
+    "phew_abi_version",
+    "phew_last_error",
+    "phew_init",
+    "phew_device_query",
+    "phew_compile",
+    "phew_launch",
+    "phew_compile_cache_size",
+    "phew_rms_norm",
+    "phew_softmax",
+    "phew_reduce",
+    "phew_copy_strided",
+    "phew_l2_flush",
+    "phew_compare_scratch_bytes",
+    "phew_compare",
+)
+
+
+class PhewError(RuntimeError):
+    """A native call returned a non-zero status."""
+
+    def __init__(self, status: int, message: str) -> None:
+        super().__init__(f"[phew status {status}] {message}")
+        self.status = status
+
+
+class PhewCompileError(PhewError):
+    """NVRTC rejected an emitted or user-supplied kernel source."""
+
+
+class DeviceInfo(ctypes.Structure):
+    _fields_ = [
+        ("sm_count", ctypes.c_int),
+        ("cc_major", ctypes.c_int),
+        ("cc_minor", ctypes.c_int),
+        ("max_smem_per_block_optin", ctypes.c_int),
+        ("l2_bytes", ctypes.c_int64),
+        ("hbm_bytes", ctypes.c_int64),
+        ("name", ctypes.c_char * 128),
+    ]
+
+
+class CompareStats(ctypes.Structure):
+    _fields_ = [
+        ("sum_abs_base", ctypes.c_double),
+        ("mean_abs_base", ctypes.c_double),
+        ("max_abs_diff", ctypes.c_double),
+        ("atol_used", ctypes.c_double),
+        ("rtol_used", ctypes.c_double),
+        ("n", ctypes.c_int64),
+        ("n_nonfinite_base", ctypes.c_int64),
+        ("n_mismatch", ctypes.c_int64),
+        ("n_nan_any", ctypes.c_int64),
+        ("skipped", ctypes.c_int32),
+        ("passed", ctypes.c_int32),
+    ]
+
+
+_lib = None
+_lock = threading.Lock()
+
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+
+_SIGNATURES = {
+    "phew_abi_version": ([], _int),
+    "phew_last_error": ([ctypes.c_char_p, ctypes.c_size_t], _int),
+    "phew_init": ([_int], _int),
+    "phew_device_query": ([_int, ctypes.POINTER(DeviceInfo)], _int),
+    "phew_compile": ([ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint64)], _int),
+    "phew_launch": (
+        [ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p), _int]
+        + [ctypes.c_uint] * 6
+        + [ctypes.c_size_t, _vp],
+        _int,
+    ),
+    "phew_compile_cache_size": ([], _int),
+    "phew_rms_norm": ([_vp, _vp, _vp, _i64, _i64, ctypes.c_float, _int, _vp], _int),
+    "phew_softmax": ([_vp, _vp, _i64, _i64, _int, _vp], _int),
+    "phew_reduce": ([_int, _vp, _vp, _i64, _i64, _i64, _int, _vp], _int),
+    "phew_copy_strided": (
+        [_vp, _vp, _int, ctypes.POINTER(_i64), ctypes.POINTER(_i64), _int, _vp],
+        _int,
+    ),
+    "phew_l2_flush": ([_vp, ctypes.c_size_t, _vp], _int),
+    "phew_compare_scratch_bytes": ([_i64], ctypes.c_size_t),
+    "phew_compare": (
+        [_vp, _vp, _i64, _int, ctypes.c_double, ctypes.c_double, _vp, ctypes.c_size_t, _vp, _vp],
+        _int,
+    ),
+}
+
+
+def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
+    """Load (once) and return the native library.  Raises if it is missing."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        p = Path(path) if path else LIB_PATH
+        if not p.exists():
+            raise ImportError(
+                f"phew_b200 native library not found at {p}; build it with "
+                "`python -m phew_b200.build` (there is no CPU fallback)"
+            )
+        lib = ctypes.CDLL(str(p))
+        for name, (argtypes, restype) in _SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = argtypes
+            fn.restype = restype
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    lib = load()
+    buf = ctypes.create_string_buffer(8192)
+    lib.phew_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def check(status: int, what: str = "") -> None:
+    """Raise PhewError (or PhewCompileError) for a non-zero status."""
+    if status == PHEW_OK:
+        return
+    msg = last_error()
+    if what:
+        msg = f"{what}: {msg}"
+    if status == PHEW_ERR_COMPILE:
+        raise PhewCompileError(status, msg)
+    raise PhewError(status, msg)
+
+
+def call(name: str, *args):
+    """Call a status-returning entry point and raise on failure."""
+    lib = load()
+    check(getattr(lib, name)(*args), name)

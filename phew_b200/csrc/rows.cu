@@ -1,0 +1,402 @@
+// Row-wise primitives: rms_norm, softmax and axis reductions.
+//
+// Layout: the reduced axis is the innermost, contiguous one ([rows, cols],
+// row-major) except for phew_reduce's strided form ([outer, red, inner]).
+// Each CTA row group keeps its row in registers (up to 8 16-byte vectors per
+// thread), so a row is read from HBM once and written once: these kernels are
+// HBM-bound at 2 * rows * cols * sizeof(T) bytes.
+#include <math.h>
+
+#include "common.cuh"
+
+namespace phew {
+namespace {
+
+constexpr int kMaxVPT = 8;  // 16-byte vectors held per thread
+
+template <typename T> struct Vec {
+  static constexpr int E = 16 / sizeof(T);  // elements per 16-byte vector
+};
+
+// Loads 16 bytes at p (E elements of T) into fp32 registers.
+template <typename T>
+__device__ __forceinline__ void load_vec(const T* p, float* out) {
+  const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p));
+  const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+  for (int i = 0; i < Vec<T>::E; ++i) out[i] = to_f32(e[i]);
+}
+
+template <typename T>
+__device__ __forceinline__ void store_vec(T* p, const float* in) {
+  uint4 raw;
+  T* e = reinterpret_cast<T*>(&raw);
+#pragma unroll
+  for (int i = 0; i < Vec<T>::E; ++i) e[i] = from_f32<T>(in[i]);
+  *reinterpret_cast<uint4*>(p) = raw;
+}
+
+// Block-wide reduction of one value per row group.  Threads of a row are
+// threadIdx.x in [0, blockDim.x); rows of the block are threadIdx.y.
+template <bool IS_MAX>
+__device__ __forceinline__ float row_allreduce(float v, float* smem) {
+  v = IS_MAX ? warp_max(v) : warp_sum(v);
+  const int warps_per_row = blockDim.x / 32;
+  if (warps_per_row == 1) return v;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float* row_smem = smem + threadIdx.y * 32;
+  __syncthreads();
+  if (lane == 0) row_smem[warp] = v;
+  __syncthreads();
+  float r = lane < warps_per_row ? row_smem[lane] : (IS_MAX ? -INFINITY : 0.f);
+  r = IS_MAX ? warp_max(r) : warp_sum(r);
+  return r;
+}
+
+// ---------------------------------------------------------------------------
+// rms_norm: y = w * T(x * rsqrt(mean(x^2) + eps))
+// ---------------------------------------------------------------------------
+template <typename T, int VPT>
+__global__ void rms_norm_vec_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                    T* __restrict__ y, int64_t rows, int64_t cols, float eps) {
+  __shared__ float smem[32 * 32];
+  constexpr int E = Vec<T>::E;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.y + threadIdx.y;
+  const bool active = row < rows;
+  const int64_t nvec = cols / E;
+  const T* xr = x + row * cols;
+  float v[VPT][E];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t vi = threadIdx.x + static_cast<int64_t>(j) * blockDim.x;
+    if (active && vi < nvec) {
+      load_vec<T>(xr + vi * E, v[j]);
+#pragma unroll
+      for (int i = 0; i < E; ++i) ss = fmaf(v[j][i], v[j][i], ss);
+    }
+  }
+  const float total = row_allreduce<false>(ss, smem);
+  const float r = 1.0f / sqrtf(total / static_cast<float>(cols) + eps);
+  if (!active) return;
+  T* yr = y + row * cols;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t vi = threadIdx.x + static_cast<int64_t>(j) * blockDim.x;
+    if (vi < nvec) {
+      float o[E];
+      if (w != nullptr) {
+        float wv[E];
+        load_vec<T>(w + vi * E, wv);
+#pragma unroll
+        for (int i = 0; i < E; ++i) o[i] = __fmul_rn(wv[i], round_to<T>(__fmul_rn(v[j][i], r)));
+      } else {
+#pragma unroll
+        for (int i = 0; i < E; ++i) o[i] = __fmul_rn(v[j][i], r);
+      }
+      store_vec<T>(yr + vi * E, o);
+    }
+  }
+}
+
+// Scalar two-pass form for unaligned rows or rows too long for registers.
+template <typename T>
+__global__ void rms_norm_loop_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                     T* __restrict__ y, int64_t rows, int64_t cols, float eps) {
+  __shared__ float smem[32 * 32];
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.y + threadIdx.y;
+  const bool active = row < rows;
+  const T* xr = x + row * cols;
+  float ss = 0.f;
+  if (active)
+    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+      const float a = to_f32(xr[c]);
+      ss = fmaf(a, a, ss);
+    }
+  const float total = row_allreduce<false>(ss, smem);
+  const float r = 1.0f / sqrtf(total / static_cast<float>(cols) + eps);
+  if (!active) return;
+  T* yr = y + row * cols;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+    const float n = __fmul_rn(to_f32(xr[c]), r);
+    yr[c] = from_f32<T>(w != nullptr ? __fmul_rn(to_f32(w[c]), round_to<T>(n)) : n);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// softmax over the last axis: y = exp(x - max) / sum(exp(x - max))
+// ---------------------------------------------------------------------------
+template <typename T, int VPT>
+__global__ void softmax_vec_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t rows,
+                                   int64_t cols) {
+  __shared__ float smem[32 * 32];
+  constexpr int E = Vec<T>::E;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.y + threadIdx.y;
+  const bool active = row < rows;
+  const int64_t nvec = cols / E;
+  const T* xr = x + row * cols;
+  float v[VPT][E];
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t vi = threadIdx.x + static_cast<int64_t>(j) * blockDim.x;
+    if (active && vi < nvec) {
+      load_vec<T>(xr + vi * E, v[j]);
+#pragma unroll
+      for (int i = 0; i < E; ++i) m = fmaxf(m, v[j][i]);
+    }
+  }
+  m = row_allreduce<true>(m, smem);
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t vi = threadIdx.x + static_cast<int64_t>(j) * blockDim.x;
+    if (active && vi < nvec) {
+#pragma unroll
+      for (int i = 0; i < E; ++i) {
+        v[j][i] = expf(v[j][i] - m);
+        s += v[j][i];
+      }
+    }
+  }
+  s = row_allreduce<false>(s, smem);
+  if (!active) return;
+  T* yr = y + row * cols;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t vi = threadIdx.x + static_cast<int64_t>(j) * blockDim.x;
+    if (vi < nvec) {
+      float o[E];
+#pragma unroll
+      for (int i = 0; i < E; ++i) o[i] = __fdiv_rn(v[j][i], s);
+      store_vec<T>(yr + vi * E, o);
+    }
+  }
+}
+
+template <typename T>
+__global__ void softmax_loop_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t rows,
+                                    int64_t cols) {
+  __shared__ float smem[32 * 32];
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.y + threadIdx.y;
+  const bool active = row < rows;
+  const T* xr = x + row * cols;
+  float m = -INFINITY;
+  if (active)
+    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) m = fmaxf(m, to_f32(xr[c]));
+  m = row_allreduce<true>(m, smem);
+  float s = 0.f;
+  if (active)
+    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) s += expf(to_f32(xr[c]) - m);
+  s = row_allreduce<false>(s, smem);
+  if (!active) return;
+  T* yr = y + row * cols;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x)
+    yr[c] = from_f32<T>(__fdiv_rn(expf(to_f32(xr[c]) - m), s));
+}
+
+// ---------------------------------------------------------------------------
+// Reductions over the middle axis of [outer, red, inner]
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float combine(int op, float a, float b) {
+  switch (op) {
+    case PHEW_REDUCE_MAX: return (b > a || isnan(b)) && !isnan(a) ? b : a;
+    case PHEW_REDUCE_MIN: return (b < a || isnan(b)) && !isnan(a) ? b : a;
+    case PHEW_REDUCE_PROD: return a * b;
+    default: return a + b;
+  }
+}
+__device__ __forceinline__ float identity(int op) {
+  switch (op) {
+    case PHEW_REDUCE_MAX: return -INFINITY;
+    case PHEW_REDUCE_MIN: return INFINITY;
+    case PHEW_REDUCE_PROD: return 1.f;
+    default: return 0.f;
+  }
+}
+
+// inner == 1: one row group per reduced row.
+template <typename T>
+__global__ void reduce_rows_kernel(int op, const T* __restrict__ x, T* __restrict__ y,
+                                   int64_t rows, int64_t red) {
+  __shared__ float smem[32 * 32];
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.y + threadIdx.y;
+  const bool active = row < rows;
+  const T* xr = x + row * red;
+  float acc = identity(op);
+  if (active)
+    for (int64_t c = threadIdx.x; c < red; c += blockDim.x) acc = combine(op, acc, to_f32(xr[c]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc = combine(op, acc, __shfl_xor_sync(0xffffffffu, acc, o));
+  const int warps_per_row = blockDim.x / 32;
+  if (warps_per_row > 1) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float* row_smem = smem + threadIdx.y * 32;
+    __syncthreads();
+    if (lane == 0) row_smem[warp] = acc;
+    __syncthreads();
+    acc = lane < warps_per_row ? row_smem[lane] : identity(op);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc = combine(op, acc, __shfl_xor_sync(0xffffffffu, acc, o));
+  }
+  if (active && threadIdx.x == 0) {
+    if (op == PHEW_REDUCE_MEAN) acc = __fdiv_rn(acc, static_cast<float>(red));
+    y[row] = from_f32<T>(acc);
+  }
+}
+
+// inner > 1: one thread per (outer, inner) output, coalesced along inner.
+template <typename T>
+__global__ void reduce_cols_kernel(int op, const T* __restrict__ x, T* __restrict__ y,
+                                   int64_t outer, int64_t red, int64_t inner) {
+  const int64_t total = outer * inner;
+  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t o = idx / inner, i = idx % inner;
+    const T* p = x + o * red * inner + i;
+    float acc = identity(op);
+    for (int64_t r = 0; r < red; ++r) acc = combine(op, acc, to_f32(p[r * inner]));
+    if (op == PHEW_REDUCE_MEAN) acc = __fdiv_rn(acc, static_cast<float>(red));
+    y[idx] = from_f32<T>(acc);
+  }
+}
+
+// Chooses threads-per-row (multiple of 32) and rows-per-block for a row of
+// `nvec` vectors so that each thread holds about 4 vectors.
+struct RowLaunch {
+  int tpr, rpb, vpt;
+};
+RowLaunch plan_rows(int64_t nvec) {
+  int tpr = static_cast<int>(((nvec + 3) / 4 + 31) / 32 * 32);
+  if (tpr < 32) tpr = 32;
+  if (tpr > 1024) tpr = 1024;
+  int vpt = static_cast<int>((nvec + tpr - 1) / tpr);
+  int rpb = tpr >= 128 ? 1 : 128 / tpr;
+  return {tpr, rpb, vpt};
+}
+
+template <typename T>
+int rms_norm_typed(const void* x, const void* w, void* y, int64_t rows, int64_t cols, float eps,
+                   cudaStream_t st) {
+  constexpr int E = Vec<T>::E;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
+                         reinterpret_cast<uintptr_t>(w)) & 15) == 0;
+  const int64_t nvec = cols / E;
+  const T* xp = static_cast<const T*>(x);
+  const T* wp = static_cast<const T*>(w);
+  T* yp = static_cast<T*>(y);
+  if (aligned && cols % E == 0 && nvec <= 1024LL * kMaxVPT) {
+    RowLaunch L = plan_rows(nvec);
+    dim3 block(L.tpr, L.rpb), grid(static_cast<unsigned>((rows + L.rpb - 1) / L.rpb));
+    switch (L.vpt) {
+#define PHEW_CASE(N) \
+  case N: rms_norm_vec_kernel<T, N><<<grid, block, 0, st>>>(xp, wp, yp, rows, cols, eps); break;
+      PHEW_CASE(1) PHEW_CASE(2) PHEW_CASE(3) PHEW_CASE(4)
+      PHEW_CASE(5) PHEW_CASE(6) PHEW_CASE(7) PHEW_CASE(8)
+#undef PHEW_CASE
+      default: return set_error(PHEW_ERR_INVALID, "rms_norm: bad plan");
+    }
+    return launch_status("rms_norm_vec_kernel");
+  }
+  const int tpr = cols >= 1024 ? 256 : 32;
+  const int rpb = tpr == 32 ? 4 : 1;
+  dim3 block(tpr, rpb), grid(static_cast<unsigned>((rows + rpb - 1) / rpb));
+  rms_norm_loop_kernel<T><<<grid, block, 0, st>>>(xp, wp, yp, rows, cols, eps);
+  return launch_status("rms_norm_loop_kernel");
+}
+
+template <typename T>
+int softmax_typed(const void* x, void* y, int64_t rows, int64_t cols, cudaStream_t st) {
+  constexpr int E = Vec<T>::E;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+  const int64_t nvec = cols / E;
+  const T* xp = static_cast<const T*>(x);
+  T* yp = static_cast<T*>(y);
+  if (aligned && cols % E == 0 && nvec <= 1024LL * kMaxVPT) {
+    RowLaunch L = plan_rows(nvec);
+    dim3 block(L.tpr, L.rpb), grid(static_cast<unsigned>((rows + L.rpb - 1) / L.rpb));
+    switch (L.vpt) {
+#define PHEW_CASE(N) \
+  case N: softmax_vec_kernel<T, N><<<grid, block, 0, st>>>(xp, yp, rows, cols); break;
+      PHEW_CASE(1) PHEW_CASE(2) PHEW_CASE(3) PHEW_CASE(4)
+      PHEW_CASE(5) PHEW_CASE(6) PHEW_CASE(7) PHEW_CASE(8)
+#undef PHEW_CASE
+      default: return set_error(PHEW_ERR_INVALID, "softmax: bad plan");
+    }
+    return launch_status("softmax_vec_kernel");
+  }
+  const int tpr = cols >= 1024 ? 256 : 32;
+  const int rpb = tpr == 32 ? 4 : 1;
+  dim3 block(tpr, rpb), grid(static_cast<unsigned>((rows + rpb - 1) / rpb));
+  softmax_loop_kernel<T><<<grid, block, 0, st>>>(xp, yp, rows, cols);
+  return launch_status("softmax_loop_kernel");
+}
+
+template <typename T>
+int reduce_typed(int op, const void* x, void* y, int64_t outer, int64_t red, int64_t inner,
+                 cudaStream_t st) {
+  const T* xp = static_cast<const T*>(x);
+  T* yp = static_cast<T*>(y);
+  if (inner == 1) {
+    const int tpr = red >= 1024 ? 256 : 32;
+    const int rpb = tpr == 32 ? 4 : 1;
+    dim3 block(tpr, rpb), grid(static_cast<unsigned>((outer + rpb - 1) / rpb));
+    reduce_rows_kernel<T><<<grid, block, 0, st>>>(op, xp, yp, outer, red);
+    return launch_status("reduce_rows_kernel");
+  }
+  const int64_t total = outer * inner;
+  int64_t blocks = (total + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(sm_count_current()) * 16;
+  if (blocks > cap) blocks = cap;
+  reduce_cols_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, st>>>(op, xp, yp, outer, red, inner);
+  return launch_status("reduce_cols_kernel");
+}
+
+}  // namespace
+}  // namespace phew
+
+using namespace phew;
+
+extern "C" int phew_rms_norm(const void* x, const void* w, void* y, int64_t rows, int64_t cols,
+                             float eps, int dtype, void* stream) {
+  PHEW_REQUIRE(x && y, "phew_rms_norm: null pointer");
+  PHEW_REQUIRE(rows >= 0 && cols > 0, "phew_rms_norm: bad shape");
+  PHEW_REQUIRE(rows < (1LL << 31) * 1024, "phew_rms_norm: too many rows");
+  if (rows == 0) return PHEW_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case PHEW_F32: return rms_norm_typed<float>(x, w, y, rows, cols, eps, st);
+    case PHEW_F16: return rms_norm_typed<f16>(x, w, y, rows, cols, eps, st);
+    case PHEW_BF16: return rms_norm_typed<bf16>(x, w, y, rows, cols, eps, st);
+    default: return set_error(PHEW_ERR_INVALID, "phew_rms_norm: bad dtype");
+  }
+}
+
+extern "C" int phew_softmax(const void* x, void* y, int64_t rows, int64_t cols, int dtype,
+                            void* stream) {
+  PHEW_REQUIRE(x && y, "phew_softmax: null pointer");
+  PHEW_REQUIRE(rows >= 0 && cols > 0, "phew_softmax: bad shape");
+  if (rows == 0) return PHEW_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case PHEW_F32: return softmax_typed<float>(x, y, rows, cols, st);
+    case PHEW_F16: return softmax_typed<f16>(x, y, rows, cols, st);
+    case PHEW_BF16: return softmax_typed<bf16>(x, y, rows, cols, st);
+    default: return set_error(PHEW_ERR_INVALID, "phew_softmax: bad dtype");
+  }
+}
+
+extern "C" int phew_reduce(int op, const void* x, void* y, int64_t outer, int64_t red,
+                           int64_t inner, int dtype, void* stream) {
+  PHEW_REQUIRE(x && y, "phew_reduce: null pointer");
+  PHEW_REQUIRE(outer >= 0 && red > 0 && inner > 0, "phew_reduce: bad shape");
+  PHEW_REQUIRE(op >= PHEW_REDUCE_SUM && op <= PHEW_REDUCE_PROD, "phew_reduce: bad op");
+  if (outer == 0) return PHEW_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case PHEW_F32: return reduce_typed<float>(op, x, y, outer, red, inner, st);
+    case PHEW_F16: return reduce_typed<f16>(op, x, y, outer, red, inner, st);
+    case PHEW_BF16: return reduce_typed<bf16>(op, x, y, outer, red, inner, st);
+    default: return set_error(PHEW_ERR_INVALID, "phew_reduce: bad dtype");
+  }
+}

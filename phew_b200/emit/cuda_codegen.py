@@ -1,0 +1,798 @@
+"""CUDA C++ source generator for fused elementwise subgraphs (NVRTC, sm_100a).
+
+Stands in for ``SubgraphMSLCodegen`` (phew ``emit/msl_codegen.py:125-330``)
+with the same call shape::
+
+    source, input_names, output_names = SubgraphCUDACodegen().emit(
+        subgraph_nodes, external_inputs, external_outputs)
+
+``source`` is a kernel *body* for :func:`phew_b200.mx.fast.cuda_kernel` (the
+``mx.fast.metal_kernel`` analogue), which wraps it in an ``extern "C"``
+signature built from ``input_names`` / ``output_names`` and the dtypes of
+the arrays it is called with.
+
+Semantics (what the kernel computes) follow the reference emitter and the
+MLX evaluation of the unfused graph:
+
+* every node's result is rounded to that node's dtype, as the MSL kernel
+  does by holding each value in a variable of the node's type
+  (``msl_codegen.py:184-199``) and as MLX does between separate ops;
+* add / sub / mul / div / sqrt use the IEEE round-to-nearest intrinsics
+  (``__fadd_rn`` ...), so no multiply-add contraction changes a result;
+* constants are inlined, rounded to their node's dtype
+  (``msl_codegen.py:55-67, 189-191``);
+* broadcast inputs are indexed from the flat output index
+  (``msl_codegen.py:70-107``).
+
+Layout and launch (the B200 part): the body is a grid-stride loop that moves
+one 16-byte vector per array per iteration (8 x 16-bit or 4 x 32-bit
+elements), with row-broadcast inputs (``elem % inner``) read as vectors too
+and column-broadcast ones read once per vector.  Chains whose arrays are all
+of one 16-bit float type compute in packed pairs (``add.rn.f16x2`` ...),
+which give the same bits as fp32-then-round for add/sub/mul.  A scalar loop
+handles the tail, unaligned pointers and general broadcasts.
+
+Nodes are read by duck typing: the class name (or a ``kind`` attribute)
+selects Elementwise / Cast / Constant, and the fields used are ``id``,
+``shape``, ``dtype`` (an enum with ``.value`` or a plain string),
+``inputs``, ``op``, ``value`` and ``target_dtype`` -- the fields of
+``phew.ir.ops`` (``ir/ops.py:28-64,82-86``).
+"""
+
+from __future__ import annotations
+
+import math
+import struct
+from typing import Any, Iterable
+
+import numpy as np
+
+try:  # bf16 rounding of constants
+    import ml_dtypes as _mld
+except ImportError:  # pragma: no cover - ml_dtypes ships with the image
+    _mld = None
+
+# ---------------------------------------------------------------------------
+# dtype tables
+# ---------------------------------------------------------------------------
+
+FLOAT_TYPES = ("float32", "float16", "bfloat16")
+HALF_TYPES = ("float16", "bfloat16")
+
+CTYPE = {
+    "float32": "float",
+    "float16": "phew_f16",
+    "bfloat16": "phew_bf16",
+    "int8": "signed char",
+    "int16": "short",
+    "int32": "int",
+    "int64": "long long",
+    "uint8": "unsigned char",
+    "uint16": "unsigned short",
+    "uint32": "unsigned int",
+    "uint64": "unsigned long long",
+    "bool": "bool",
+}
+
+ITEMSIZE = {
+    "float32": 4,
+    "float16": 2,
+    "bfloat16": 2,
+    "int8": 1,
+    "int16": 2,
+    "int32": 4,
+    "int64": 8,
+    "uint8": 1,
+    "uint16": 2,
+    "uint32": 4,
+    "uint64": 8,
+    "bool": 1,
+}
+
+# Value type that holds a node's result inside the kernel.
+VALUE_CTYPE = dict(CTYPE, float16="float", bfloat16="float")
+
+
+def dtype_name(d: Any) -> str:
+    """Normalise a dtype (phew Dtype enum, our mx Dtype, numpy dtype, str)."""
+    if d is None:
+        return "float32"
+    for attr in ("value", "name"):
+        v = getattr(d, attr, None)
+        if isinstance(v, str):
+            d = v
+            break
+    d = str(d)
+    if d in ("bool_", "bool"):
+        return "bool"
+    return d
+
+
+def node_kind(node: Any) -> str:
+    return getattr(node, "kind", None) or type(node).__name__
+
+
+def _numel(shape: Iterable[int]) -> int:
+    n = 1
+    for s in shape:
+        n *= int(s)
+    return n
+
+
+# ---------------------------------------------------------------------------
+# literals
+# ---------------------------------------------------------------------------
+
+
+def _round_value(value: float, dt: str) -> float:
+    """Round a Python float the way an inlined literal of dtype `dt` is."""
+    f = float(np.float32(value))
+    if dt == "float16":
+        return float(np.float16(f))
+    if dt == "bfloat16":
+        if _mld is None:
+            raise ValueError("bfloat16 constants need ml_dtypes")
+        return float(np.asarray(f, dtype=np.float32).astype(_mld.bfloat16).astype(np.float32))
+    return f
+
+
+def float_literal(value: float) -> str:
+    """An exact fp32 C literal for `value` (already representable in fp32)."""
+    f = float(np.float32(value))
+    if math.isnan(f):
+        return "__int_as_float(0x7fc00000)"
+    if math.isinf(f):
+        return "__int_as_float(0x7f800000)" if f > 0 else "__int_as_float(0xff800000)"
+    bits = struct.unpack("<I", struct.pack("<f", f))[0]
+    return f"__int_as_float(0x{bits:08x}) /* {f!r} */"
+
+
+def half_bits(value: float, dt: str) -> int:
+    """Raw 16-bit pattern of `value` rounded to dtype `dt`."""
+    v = _round_value(value, dt)
+    if dt == "float16":
+        return int(np.asarray(v, dtype=np.float16).view(np.uint16))
+    return int(np.asarray(v, dtype=np.float32).view(np.uint32)) >> 16
+
+
+def _const_literal(value: Any, dt: str) -> str:
+    if isinstance(value, (list, tuple, np.ndarray)) and np.ndim(value) > 0:
+        raise ValueError("cuda_codegen: non-scalar Constant cannot be inlined")
+    if dt in FLOAT_TYPES:
+        return float_literal(_round_value(float(value), dt))
+    if dt == "bool":
+        return "true" if bool(value) else "false"
+    iv = int(value)
+    if dt in ("int64",):
+        return f"{iv}LL"
+    if dt in ("uint64",):
+        return f"{iv}ULL"
+    if dt.startswith("uint"):
+        return f"{iv}u"
+    return str(iv)
+
+
+# ---------------------------------------------------------------------------
+# op table: expression builders in the fp32 value domain
+# ---------------------------------------------------------------------------
+
+ALIASES = {
+    "multiply": "mul",
+    "subtract": "sub",
+    "divide": "div",
+    "neg": "negative",
+    "equal": "eq",
+    "not_equal": "ne",
+    "greater": "gt",
+    "greater_equal": "ge",
+    "less": "lt",
+    "less_equal": "le",
+    "pow": "power",
+    "atan2": "arctan2",
+}
+
+_UNARY_F = {
+    "abs": "fabsf({a})",
+    "log": "logf({a})",
+    "sqrt": "__fsqrt_rn({a})",
+    "rsqrt": "__fdiv_rn(1.0f, __fsqrt_rn({a}))",
+    "relu": "phew_maximum({a}, 0.0f)",
+    "gelu": "__fmul_rn(__fmul_rn({a}, 0.5f), __fadd_rn(1.0f, erff(__fmul_rn({a}, 0.70710678118654752f))))",
+    "cos": "cosf({a})",
+    "sin": "sinf({a})",
+    "tan": "tanf({a})",
+    "arctan": "atanf({a})",
+    "arcsin": "asinf({a})",
+    "arccos": "acosf({a})",
+    "arctanh": "atanhf({a})",
+    "arcsinh": "asinhf({a})",
+    "arccosh": "acoshf({a})",
+    "cosh": "coshf({a})",
+    "sinh": "sinhf({a})",
+    "degrees": "__fmul_rn({a}, 57.295779513082320876f)",
+    "radians": "__fmul_rn({a}, 0.017453292519943295769f)",
+    "square": "__fmul_rn({a}, {a})",
+    "ceil": "ceilf({a})",
+    "floor": "floorf({a})",
+    "round": "rintf({a})",
+    "sign": "phew_sign({a})",
+    "reciprocal": "__fdiv_rn(1.0f, {a})",
+    "erf": "erff({a})",
+    "erfinv": "erfinvf({a})",
+    "expm1": "expm1f({a})",
+    "log1p": "log1pf({a})",
+    "log2": "log2f({a})",
+    "log10": "log10f({a})",
+    "negative": "(-{a})",
+}
+
+# Transcendentals with a 16-bit-precision variant (used when the node's dtype
+# is float16/bfloat16, whose result is rounded to 11/8 significant bits).
+_UNARY_F_PRECISE = {
+    "exp": "expf({a})",
+    "sigmoid": "__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-({a}))))",
+    "tanh": "tanhf({a})",
+    "silu": "__fdiv_rn({a}, __fadd_rn(1.0f, expf(-({a}))))",
+}
+_UNARY_F_HALF = {
+    "exp": "phew_exp16({a})",
+    "sigmoid": "phew_sigmoid16({a})",
+    "tanh": "phew_tanh16({a})",
+    "silu": "__fmul_rn({a}, phew_sigmoid16({a}))",
+}
+
+_BINARY_F = {
+    "add": "__fadd_rn({a}, {b})",
+    "sub": "__fsub_rn({a}, {b})",
+    "mul": "__fmul_rn({a}, {b})",
+    "div": "__fdiv_rn({a}, {b})",
+    "maximum": "phew_maximum({a}, {b})",
+    "minimum": "phew_minimum({a}, {b})",
+    "logaddexp": "phew_logaddexp({a}, {b})",
+    "floor_divide": "floorf(__fdiv_rn({a}, {b}))",
+    "remainder": "phew_remainder({a}, {b})",
+    "power": "powf({a}, {b})",
+    "arctan2": "atan2f({a}, {b})",
+}
+
+_COMPARE = {"eq": "==", "ne": "!=", "gt": ">", "ge": ">=", "lt": "<", "le": "<="}
+_LOGICAL = {"logical_and": "&&", "logical_or": "||"}
+
+_INT_BINARY = {"add": "+", "sub": "-", "mul": "*"}
+
+SUPPORTED_OPS = (
+    set(_UNARY_F)
+    | set(_UNARY_F_PRECISE)
+    | set(_BINARY_F)
+    | set(_COMPARE)
+    | set(_LOGICAL)
+    | {"logical_not", "where"}
+    | set(ALIASES)
+)
+
+# Ops computed natively on packed 16-bit pairs.
+_PACKED_NATIVE = {"add": "add", "sub": "sub", "mul": "mul", "square": "sq", "negative": "neg", "abs": "abs"}
+
+
+def canonical_op(op: str) -> str:
+    return ALIASES.get(op, op)
+
+
+def _round_expr(expr: str, dt: str) -> str:
+    if dt == "float16":
+        return f"phew_rnd_f16({expr})"
+    if dt == "bfloat16":
+        return f"phew_rnd_bf16({expr})"
+    return expr
+
+
+def _to_float(v: str, dt: str) -> str:
+    return v if dt in FLOAT_TYPES else f"(float)({v})"
+
+
+def scalar_expr(
+    op: str, args: list[str], arg_dtypes: list[str], out_dt: str, round_result: bool = True
+) -> str:
+    """C expression computing `op` on value variables, typed for `out_dt`.
+
+    Float results are rounded to `out_dt` (unless `round_result` is False,
+    for callers that round while packing); integer and bool results use C
+    semantics of the node's C type.
+    """
+    op = canonical_op(op)
+    if out_dt in FLOAT_TYPES:
+        fa = [_to_float(a, d) for a, d in zip(args, arg_dtypes)]
+        half = out_dt in HALF_TYPES
+        if op in _COMPARE:
+            expr = f"(({fa[0]} {_COMPARE[op]} {fa[1]}) ? 1.0f : 0.0f)"
+        elif op in _LOGICAL:
+            expr = f"(((({fa[0]}) != 0.0f) {_LOGICAL[op]} (({fa[1]}) != 0.0f)) ? 1.0f : 0.0f)"
+        elif op == "logical_not":
+            expr = f"(({fa[0]}) == 0.0f ? 1.0f : 0.0f)"
+        elif op == "where":
+            cond = args[0] if arg_dtypes[0] == "bool" else f"({fa[0]} != 0.0f)"
+            expr = f"({cond} ? {fa[1]} : {fa[2]})"
+        elif op in _UNARY_F and len(fa) >= 1:
+            expr = _UNARY_F[op].format(a=fa[0])
+        elif op in _UNARY_F_PRECISE and len(fa) >= 1:
+            table = _UNARY_F_HALF if half else _UNARY_F_PRECISE
+            expr = table[op].format(a=fa[0])
+        elif op in _BINARY_F and len(fa) == 2:
+            expr = _BINARY_F[op].format(a=fa[0], b=fa[1])
+        else:
+            raise ValueError(f"cuda_codegen: unhandled op {op!r}")
+        return _round_expr(expr, out_dt) if round_result else expr
+    ct = VALUE_CTYPE[out_dt]
+    if op in _COMPARE:
+        return f"(({ct})({args[0]} {_COMPARE[op]} {args[1]}))"
+    if op in _LOGICAL:
+        return f"(({ct})({args[0]} {_LOGICAL[op]} {args[1]}))"
+    if op == "logical_not":
+        return f"(({ct})(!{args[0]}))"
+    if op == "where":
+        return f"(({ct})({args[0]} ? {args[1]} : {args[2]}))"
+    if out_dt == "bool":
+        raise ValueError(f"cuda_codegen: unhandled bool op {op!r}")
+    if op in _INT_BINARY and len(args) == 2:
+        return f"(({ct})({args[0]} {_INT_BINARY[op]} {args[1]}))"
+    if op == "negative":
+        return f"(({ct})(-{args[0]}))"
+    if op == "abs":
+        return f"(({ct})({args[0]} < 0 ? -{args[0]} : {args[0]}))"
+    if op == "square":
+        return f"(({ct})({args[0]} * {args[0]}))"
+    if op == "maximum":
+        return f"(({ct})({args[0]} > {args[1]} ? {args[0]} : {args[1]}))"
+    if op == "minimum":
+        return f"(({ct})({args[0]} < {args[1]} ? {args[0]} : {args[1]}))"
+    if op == "floor_divide":
+        return f"phew_floordiv_i({args[0]}, {args[1]})"
+    if op == "remainder":
+        return f"phew_remainder_i({args[0]}, {args[1]})"
+    if op == "sign":
+        return f"(({ct})(({args[0]} > 0) - ({args[0]} < 0)))"
+    raise ValueError(f"cuda_codegen: unhandled integer op {op!r}")
+
+
+def cast_expr(v: str, src_dt: str, dst_dt: str) -> str:
+    """Value-domain conversion for a Cast node (MLX astype semantics)."""
+    if dst_dt in FLOAT_TYPES:
+        return _round_expr(_to_float(v, src_dt), dst_dt)
+    ct = VALUE_CTYPE[dst_dt]
+    if dst_dt == "bool":
+        return f"({v} != 0)"
+    if src_dt in FLOAT_TYPES:
+        return f"(({ct})truncf({v}))"
+    return f"(({ct})({v}))"
+
+
+# ---------------------------------------------------------------------------
+# broadcast classification
+# ---------------------------------------------------------------------------
+
+
+def broadcast_compatible(in_shape, out_shape) -> bool:
+    if len(in_shape) > len(out_shape):
+        return False
+    padded = (1,) * (len(out_shape) - len(in_shape)) + tuple(in_shape)
+    return all(i == 1 or i == o for i, o in zip(padded, out_shape))
+
+
+def classify_input(in_shape, out_shape) -> tuple[str, int]:
+    """Return (class, extent) of an input's broadcast pattern.
+
+    classes: "full" (same shape), "scalar" (one element), "suffix" (equals
+    the trailing dims: index ``elem % extent``), "prefix" (equals the leading
+    dims: index ``elem / extent``) and "general" (anything else).
+    """
+    in_shape = tuple(int(s) for s in in_shape)
+    out_shape = tuple(int(s) for s in out_shape)
+    if in_shape == out_shape:
+        return "full", 0
+    if _numel(in_shape) == 1:
+        return "scalar", 0
+    nd = len(out_shape)
+    padded = (1,) * (nd - len(in_shape)) + in_shape
+    for k in range(nd + 1):
+        if all(p == 1 for p in padded[:k]) and padded[k:] == out_shape[k:]:
+            return "suffix", _numel(out_shape[k:])
+    for k in range(nd + 1):
+        if padded[:k] == out_shape[:k] and all(p == 1 for p in padded[k:]):
+            return "prefix", _numel(out_shape[k:])
+    return "general", 0
+
+
+IO_TAG = "// phew-io:"
+
+
+def io_contract_line(classes, out_shape, in_shapes, it: str) -> str:
+    """Machine-readable launch contract checked by the kernel factory before
+    every launch, so a body specialised to traced shapes can never index
+    outside the arrays it is given (see ``kernel.check_io_contract``)."""
+    parts = ["idx32" if it == "unsigned int" else "idx64"]
+    parts.append("out=" + "x".join(str(int(s)) for s in out_shape))
+    for k, ((cls, ext), shp) in enumerate(zip(classes, in_shapes)):
+        if cls in ("suffix", "prefix"):
+            parts.append(f"inp{k}={cls}:{ext}")
+        elif cls == "general":
+            parts.append(f"inp{k}=general:" + "x".join(str(int(s)) for s in shp))
+        else:
+            parts.append(f"inp{k}={cls}")
+    return IO_TAG + " " + " ".join(parts)
+
+
+def general_index(elem: str, out_shape, in_shape, it: str) -> str:
+    """Flat input index of a general broadcast (restates msl_codegen.py:70-107)."""
+    ndim = len(out_shape)
+    padded = (1,) * (ndim - len(in_shape)) + tuple(in_shape)
+    out_strides, s = [], 1
+    for d in reversed(out_shape):
+        out_strides.insert(0, s)
+        s *= d
+    in_strides, s = [], 1
+    for d in reversed(padded):
+        in_strides.insert(0, s)
+        s *= d
+    terms = []
+    u = "u" if it == "unsigned int" else "ull"
+    for i in range(ndim):
+        if padded[i] == 1:
+            continue
+        coord = (
+            f"({elem} % {out_shape[i]}{u})"
+            if out_strides[i] == 1
+            else f"(({elem} / {out_strides[i]}{u}) % {out_shape[i]}{u})"
+        )
+        terms.append(coord if in_strides[i] == 1 else f"{coord} * {in_strides[i]}{u}")
+    return " + ".join(terms) if terms else "0"
+
+
+# ---------------------------------------------------------------------------
+# emitter
+# ---------------------------------------------------------------------------
+
+
+class SubgraphCUDACodegen:
+    """Emit a CUDA kernel body for a fuseable subgraph.
+
+    Parameters of :meth:`emit` mirror ``SubgraphMSLCodegen.emit``:
+    topologically ordered Elementwise/Cast/Constant nodes, the external
+    input nodes (become ``inp0, inp1, ...``) and the external output nodes
+    (become ``out0, out1, ...``).  Raises ``ValueError`` for anything it
+    cannot fuse; the fusion pass treats that as "leave the chain unfused"
+    (``rules/fusion.py:266-270``).
+    """
+
+    def emit(
+        self,
+        subgraph_nodes: list[Any],
+        external_inputs: list[Any],
+        external_outputs: list[Any],
+    ) -> tuple[str, list[str], list[str]]:
+        if not external_outputs:
+            raise ValueError("cuda_codegen: chain has no external output")
+        inp_names = [f"inp{i}" for i in range(len(external_inputs))]
+        out_names = [f"out{i}" for i in range(len(external_outputs))]
+        out_shape = tuple(int(s) for s in external_outputs[0].shape)
+        n = _numel(out_shape)
+        for o in external_outputs:
+            if tuple(int(s) for s in o.shape) != out_shape:
+                raise ValueError(
+                    "cuda_codegen: external outputs of different shapes cannot share one "
+                    "iteration space"
+                )
+        in_dts = [dtype_name(x.dtype) for x in external_inputs]
+        out_dts = [dtype_name(x.dtype) for x in external_outputs]
+        for d in in_dts + out_dts:
+            if d not in CTYPE:
+                raise ValueError(f"cuda_codegen: unsupported dtype {d!r}")
+        classes = []
+        for x in external_inputs:
+            shp = tuple(int(s) for s in x.shape)
+            if len(shp) > 0 and not broadcast_compatible(shp, out_shape):
+                raise ValueError("cuda_codegen: input not broadcast-compatible with output")
+            classes.append(classify_input(shp, out_shape))
+
+        # Resolve the chain into a statement plan (also validates every op).
+        plan = _Plan(subgraph_nodes, external_inputs, external_outputs)
+
+        # 32-bit indexing when the traced size leaves 2x headroom; the runtime
+        # factory refuses launches whose size would overflow it.
+        it = "unsigned int" if n < 2**30 else "unsigned long long"
+        u = "u" if it == "unsigned int" else "ull"
+        itemsizes = [ITEMSIZE[d] for d, (c, _) in zip(in_dts, classes) if c in ("full", "suffix")]
+        itemsizes += [ITEMSIZE[d] for d in out_dts]
+        V = max(1, min(8, 16 // min(itemsizes)))
+        half_t = plan.pure_half_type(in_dts, out_dts)
+        vec_ok_classes = all(
+            c in ("full", "scalar", "general")
+            or (c == "suffix" and ext % V == 0)
+            or (c == "prefix" and ext % V == 0)
+            for c, ext in classes
+        )
+
+        L: list[str] = []
+        L.append(
+            f"// fused elementwise chain: {len(plan.compute_nodes)} ops, "
+            f"{len(external_inputs)} inputs, {len(external_outputs)} outputs, {n} elements"
+        )
+        L.append(io_contract_line(classes, out_shape, [tuple(x.shape) for x in external_inputs], it))
+        # The element count comes from the launch (the output's size), so the
+        # kernel traced at one size also runs the other verification sizes.
+        L.append(f"const {it} phew_n = ({it}){out_names[0]}_size;")
+        L.append(f"const {it} phew_tid = ({it})blockIdx.x * blockDim.x + threadIdx.x;")
+        L.append(f"const {it} phew_nthreads = ({it})gridDim.x * blockDim.x;")
+        L.append(f"{it} phew_tail = 0;")
+        # Loop-invariant constants.
+        for line in plan.constant_lines(packed_type=half_t if (vec_ok_classes and V == 8) else None):
+            L.append(line)
+
+        if vec_ok_classes and n >= V:
+            ptrs = " | ".join(f"reinterpret_cast<phew_uptr>({nm})" for nm in inp_names + out_names)
+            L.append(f"if ((({ptrs}) & 15u) == 0u) {{")
+            L.append(f"  const {it} phew_nvec = phew_n / {V}{u};")
+            L.append(
+                f"  for ({it} phew_v = phew_tid; phew_v < phew_nvec; phew_v += phew_nthreads) {{"
+            )
+            L.append(f"    const {it} elem = phew_v * {V}{u};")
+            body = self._vector_body(
+                plan, external_inputs, inp_names, out_names, in_dts, out_dts, classes,
+                out_shape, V, it, u, half_t,
+            )
+            L.extend("    " + b for b in body)
+            L.append("  }")
+            L.append(f"  phew_tail = phew_nvec * {V}{u};")
+            L.append("}")
+
+        L.append(f"for ({it} elem = phew_tail + phew_tid; elem < phew_n; elem += phew_nthreads) {{")
+        scalar = self._scalar_body(
+            plan, external_inputs, inp_names, out_names, in_dts, out_dts, classes, out_shape, it, u
+        )
+        L.extend("  " + s for s in scalar)
+        L.append("}")
+        source = "\n".join(f"    {line}" if line else "" for line in L)
+        return source, inp_names, out_names
+
+    # -- per-element form -----------------------------------------------------
+
+    def _index(self, cls, ext, name, node, out_shape, it, u, elem="elem") -> str:
+        if cls == "full":
+            return elem
+        if cls == "scalar":
+            return "0"
+        if cls == "suffix":
+            return f"{elem} % {ext}{u}"
+        if cls == "prefix":
+            return f"{elem} / {ext}{u}"
+        return general_index(elem, out_shape, tuple(int(s) for s in node.shape), it)
+
+    def _scalar_body(self, plan, ext_in, inp_names, out_names, in_dts, out_dts, classes,
+                     out_shape, it, u) -> list[str]:
+        lines = []
+        env = {}
+        for node, nm, dt, (cls, ext) in zip(ext_in, inp_names, in_dts, classes):
+            v = plan.var(node)
+            idx = self._index(cls, ext, nm, node, out_shape, it, u)
+            lines.append(f"const {VALUE_CTYPE[dt]} {v} = phew_ld({nm}[{idx}]);")
+            env[node.id] = (v, dt)
+        lines += plan.scalar_lines(env)
+        for node, nm, dt in zip(plan.outputs, out_names, out_dts):
+            v, vdt = env[node.id]
+            lines.append(f"{nm}[elem] = phew_st_{_suffix(dt)}({_convert(v, vdt, dt)});")
+        return lines
+
+    # -- vector form ----------------------------------------------------------
+
+    def _vector_body(self, plan, ext_in, inp_names, out_names, in_dts, out_dts, classes,
+                     out_shape, V, it, u, half_t) -> list[str]:
+        lines = []
+        packed = half_t is not None and V == 8
+        # Loads.
+        for k, (node, nm, dt, (cls, ext)) in enumerate(zip(ext_in, inp_names, in_dts, classes)):
+            ct = CTYPE[dt]
+            if cls == "full":
+                lines.append(f"const phew_vec<{ct}, {V}> ld{k} = phew_ldv<{ct}, {V}>({nm} + elem);")
+            elif cls == "suffix":
+                lines.append(
+                    f"const phew_vec<{ct}, {V}> ld{k} = phew_ldv<{ct}, {V}>({nm} + elem % {ext}{u});"
+                )
+            elif cls in ("scalar", "prefix"):
+                idx = "0" if cls == "scalar" else f"elem / {ext}{u}"
+                lines.append(f"const {ct} ld{k} = {nm}[{idx}];")
+            else:
+                lines.append(f"phew_vec<{ct}, {V}> ld{k};")
+                lines.append("#pragma unroll")
+                lines.append(f"for (int l = 0; l < {V}; ++l) {{")
+                gi = general_index(f"(elem + l)", out_shape, tuple(int(s) for s in node.shape), it)
+                lines.append(f"  ld{k}.v[l] = {nm}[{gi}];")
+                lines.append("}")
+        for k, (nm, dt) in enumerate(zip(out_names, out_dts)):
+            lines.append(f"phew_vec<{CTYPE[dt]}, {V}> st{k};")
+        if packed:
+            P = V // 2
+            lines.append("#pragma unroll")
+            lines.append(f"for (int p = 0; p < {P}; ++p) {{")
+            env = {}
+            for k, (node, (cls, _)) in enumerate(zip(ext_in, classes)):
+                v = plan.var(node)
+                if cls in ("scalar", "prefix"):
+                    lines.append(f"  const phew_u32 {v} = phew_splat2(ld{k});")
+                else:
+                    lines.append(f"  const phew_u32 {v} = phew_pair(ld{k}, p);")
+                env[node.id] = v
+            lines += ["  " + s for s in plan.packed_lines(env, half_t)]
+            for k, node in enumerate(plan.outputs):
+                lines.append(f"  phew_set_pair(st{k}, p, {env[node.id]});")
+            lines.append("}")
+        else:
+            lines.append("#pragma unroll")
+            lines.append(f"for (int l = 0; l < {V}; ++l) {{")
+            env = {}
+            for k, (node, dt, (cls, _)) in enumerate(zip(ext_in, in_dts, classes)):
+                v = plan.var(node)
+                src = f"ld{k}" if cls in ("scalar", "prefix") else f"ld{k}.v[l]"
+                lines.append(f"  const {VALUE_CTYPE[dt]} {v} = phew_ld({src});")
+                env[node.id] = (v, dt)
+            lines += ["  " + s for s in plan.scalar_lines(env)]
+            for k, (node, dt) in enumerate(zip(plan.outputs, out_dts)):
+                v, vdt = env[node.id]
+                lines.append(f"  st{k}.v[l] = phew_st_{_suffix(dt)}({_convert(v, vdt, dt)});")
+            lines.append("}")
+        for k, (nm, dt) in enumerate(zip(out_names, out_dts)):
+            lines.append(f"phew_stv<{CTYPE[dt]}, {V}>({nm} + elem, st{k});")
+        return lines
+
+
+def _suffix(dt: str) -> str:
+    return {"float32": "f32", "float16": "f16", "bfloat16": "bf16"}.get(dt, "raw")
+
+
+def _convert(v: str, src: str, dst: str) -> str:
+    if src == dst:
+        return v
+    return cast_expr(v, src, dst)
+
+
+class _Plan:
+    """Resolved chain: variable names, node order and dtype bookkeeping."""
+
+    def __init__(self, nodes, ext_in, ext_out) -> None:
+        self.nodes = list(nodes)
+        self.ext_in = list(ext_in)
+        self.outputs = list(ext_out)
+        self._names: dict[int, str] = {}
+        self._ctr = 0
+        for x in self.ext_in:
+            self.var(x)
+        self.compute_nodes = []
+        self.constants = []
+        for node in self.nodes:
+            kind = node_kind(node)
+            dt = dtype_name(node.dtype)
+            if dt not in CTYPE:
+                raise ValueError(f"cuda_codegen: unsupported dtype {dt!r}")
+            if kind == "Constant":
+                _const_literal(getattr(node, "value", None), dt)  # validates
+                self.constants.append(node)
+            elif kind == "Cast":
+                tdt = dtype_name(getattr(node, "target_dtype", node.dtype))
+                if tdt not in CTYPE:
+                    raise ValueError(f"cuda_codegen: unsupported dtype {tdt!r}")
+                self.compute_nodes.append(node)
+            elif kind == "Elementwise":
+                op = canonical_op(node.op)
+                if op not in SUPPORTED_OPS and op not in ALIASES.values():
+                    raise ValueError(f"cuda_codegen: unhandled op {node.op!r}")
+                self.compute_nodes.append(node)
+            else:
+                raise ValueError(f"cuda_codegen: cannot fuse node kind {kind!r}")
+            self.var(node)
+        known = {x.id for x in self.ext_in} | {n.id for n in self.nodes}
+        for node in self.nodes:
+            for i in getattr(node, "inputs", []):
+                if i not in known:
+                    raise ValueError(f"cuda_codegen: input {i} of node {node.id} is not available")
+        # Validate ops and arities by generating the scalar form once.
+        env = {x.id: (self.var(x), dtype_name(x.dtype)) for x in self.ext_in}
+        self.scalar_lines(env)
+        for o in self.outputs:
+            if o.id not in env:
+                raise ValueError(f"cuda_codegen: output {o.id} is not computed by the chain")
+
+    def var(self, node) -> str:
+        if node.id not in self._names:
+            self._ctr += 1
+            self._names[node.id] = f"v{self._ctr}"
+        return self._names[node.id]
+
+    def pure_half_type(self, in_dts, out_dts) -> str | None:
+        dts = set(in_dts) | set(out_dts)
+        for node in self.nodes:
+            dts.add(dtype_name(node.dtype))
+            if node_kind(node) == "Cast":
+                dts.add(dtype_name(getattr(node, "target_dtype", node.dtype)))
+        if len(dts) == 1 and next(iter(dts)) in HALF_TYPES:
+            return next(iter(dts))
+        return None
+
+    def constant_lines(self, packed_type: str | None) -> list[str]:
+        lines = []
+        for node in self.constants:
+            dt = dtype_name(node.dtype)
+            v = self.var(node)
+            lit = _const_literal(node.value, dt)
+            lines.append(f"const {VALUE_CTYPE[dt]} {v} = {lit};")
+            if packed_type is not None and dt == packed_type:
+                bits = half_bits(float(node.value), dt)
+                lines.append(f"const phew_u32 {v}_x2 = 0x{bits:04x}{bits:04x}u;")
+        return lines
+
+    def scalar_lines(self, env: dict) -> list[str]:
+        lines = []
+        for node in self.constants:
+            env[node.id] = (self.var(node), dtype_name(node.dtype))
+        for node in self.compute_nodes:
+            kind = node_kind(node)
+            dt = dtype_name(node.dtype)
+            v = self.var(node)
+            args = [env[i] for i in node.inputs]
+            if kind == "Cast":
+                tdt = dtype_name(getattr(node, "target_dtype", node.dtype))
+                expr = cast_expr(args[0][0], args[0][1], tdt)
+                dt = tdt
+            else:
+                op = canonical_op(node.op)
+                _check_arity(op, len(args))
+                expr = scalar_expr(op, [a[0] for a in args], [a[1] for a in args], dt)
+            lines.append(f"const {VALUE_CTYPE[dt]} {v} = {expr};")
+            env[node.id] = (v, dt)
+        return lines
+
+    def packed_lines(self, env: dict, ht: str) -> list[str]:
+        """Statements on packed pairs (phew_u32 holding two `ht` values)."""
+        pfx = "phew_h2" if ht == "float16" else "phew_b2"
+        lines = []
+        for node in self.constants:
+            env[node.id] = f"{self.var(node)}_x2"
+        for node in self.compute_nodes:
+            v = self.var(node)
+            ins = [env[i] for i in node.inputs]
+            if node_kind(node) == "Cast":
+                lines.append(f"const phew_u32 {v} = {ins[0]};")
+                env[node.id] = v
+                continue
+            op = canonical_op(node.op)
+            _check_arity(op, len(ins))
+            if op in _PACKED_NATIVE:
+                nat = _PACKED_NATIVE[op]
+                if nat == "sq":
+                    lines.append(f"const phew_u32 {v} = {pfx}_mul({ins[0]}, {ins[0]});")
+                elif nat in ("neg", "abs"):
+                    lines.append(f"const phew_u32 {v} = {pfx}_{nat}({ins[0]});")
+                else:
+                    lines.append(f"const phew_u32 {v} = {pfx}_{nat}({ins[0]}, {ins[1]});")
+            else:
+                # Unpack, apply the scalar form to each half, repack.
+                lo = [f"{pfx}_lo({a})" for a in ins]
+                hi = [f"{pfx}_hi({a})" for a in ins]
+                dts = [ht] * len(ins)
+                # The pack conversion rounds each half to ht.
+                e_lo = scalar_expr(op, lo, dts, ht, round_result=False)
+                e_hi = scalar_expr(op, hi, dts, ht, round_result=False)
+                lines.append(f"const phew_u32 {v} = {pfx}_pack({e_lo}, {e_hi});")
+            env[node.id] = v
+        return lines
+
+
+_ARITY = {"where": 3}
+
+
+def _check_arity(op: str, n: int) -> None:
+    if op == "where":
+        if n != 3:
+            raise ValueError("cuda_codegen: where needs 3 inputs")
+    elif op in _BINARY_F or op in _COMPARE or op in _LOGICAL:
+        if n != 2:
+            raise ValueError(f"cuda_codegen: {op} needs 2 inputs, got {n}")
+    elif n != 1:
+        raise ValueError(f"cuda_codegen: {op} needs 1 input, got {n}")

@@ -1,0 +1,779 @@
+"""Arrays and ops of the ``phew_b200.mx`` namespace.
+
+This is the surface that phew's emitted ``output_source`` and a user's
+harness function call: the subset of ``mlx.core`` that the candidate path
+uses (phew ``emit/codegen.py:94-476``), executed eagerly on the current CUDA
+device by this package's kernels:
+
+* elementwise ops and casts -> one NVRTC kernel emitted by
+  ``SubgraphCUDACodegen`` per (op, shapes, dtypes), Python scalars inlined as
+  constants of the array's dtype (MLX weak scalars);
+* reductions, softmax, rms_norm, strided copies -> the hand-written kernels
+  of ``libphew_b200.so``;
+* ``@`` / ``matmul`` and SDPA -> the tcgen05 kernels (``phew_b200.ops``).
+
+PyTorch only allocates device memory (``torch.empty``) and provides the
+current stream; no torch compute kernel runs on these paths.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import functools
+import math
+import numbers
+import weakref
+from typing import Any, Sequence
+
+import numpy as np
+import torch
+
+from .. import _native
+from .. import dtypes as dt
+from ..dtypes import (  # noqa: F401  (re-exported as mx.float16 ...)
+    Dtype,
+    bfloat16,
+    bool_,
+    float16,
+    float32,
+    int8,
+    int16,
+    int32,
+    int64,
+    uint8,
+    uint16,
+    uint32,
+    uint64,
+)
+from ..emit.cuda_codegen import SubgraphCUDACodegen
+from ..graph import NodeSpec
+from ..kernel import CudaKernel
+
+_DEVICE: torch.device | None = None
+
+
+def device() -> torch.device:
+    global _DEVICE
+    if _DEVICE is None:
+        if not torch.cuda.is_available():
+            raise RuntimeError("phew_b200.mx needs a CUDA device (there is no CPU fallback)")
+        idx = torch.cuda.current_device()
+        _native.call("phew_init", idx)
+        _DEVICE = torch.device("cuda", idx)
+    return _DEVICE
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+@functools.lru_cache(maxsize=None)
+def sm_count() -> int:
+    info = _native.DeviceInfo()
+    _native.call("phew_device_query", torch.cuda.current_device(), ctypes.byref(info))
+    return int(info.sm_count)
+
+
+def elementwise_threads(numel: int) -> int:
+    """Total threads for an emitted grid-stride elementwise kernel.
+
+    One thread per 8 elements (one 16-byte vector of a 16-bit type), capped
+    at two full waves of 2048 threads on every SM; threads loop over the
+    rest.
+    """
+    want = max(1, -(-numel // 8))
+    cap = sm_count() * 2048 * 2
+    return min(want, cap)
+
+
+# ---------------------------------------------------------------------------
+# array
+# ---------------------------------------------------------------------------
+
+
+class array:
+    """A device array (storage: a CUDA torch tensor, possibly a strided view)."""
+
+    __slots__ = ("_t", "__weakref__")
+
+    def __init__(self, val: Any, dtype: Any = None) -> None:
+        if isinstance(val, array):
+            t = val._t if dtype is None else val.astype(dtype)._t
+        elif isinstance(val, torch.Tensor):
+            t = val if val.is_cuda else val.to(device())
+            if dtype is not None and dt.from_any(dtype).torch != t.dtype:
+                t = array(t).astype(dtype)._t
+        else:
+            t = _host_to_device(val, dtype)
+        object.__setattr__(self, "_t", t)
+
+    @classmethod
+    def _wrap(cls, t: torch.Tensor) -> "array":
+        a = object.__new__(cls)
+        object.__setattr__(a, "_t", t)
+        return a
+
+    # -- metadata ------------------------------------------------------------
+    @property
+    def shape(self) -> tuple:
+        return tuple(self._t.shape)
+
+    @property
+    def dtype(self) -> Dtype:
+        return dt.from_any(self._t.dtype)
+
+    @property
+    def size(self) -> int:
+        return self._t.numel()
+
+    @property
+    def ndim(self) -> int:
+        return self._t.dim()
+
+    @property
+    def itemsize(self) -> int:
+        return self._t.element_size()
+
+    @property
+    def nbytes(self) -> int:
+        return self.size * self.itemsize
+
+    def __len__(self) -> int:
+        if self.ndim == 0:
+            raise TypeError("len() of a 0-d array")
+        return self.shape[0]
+
+    def __repr__(self) -> str:
+        return f"array(shape={self.shape}, dtype={self.dtype!r})"
+
+    # -- host interop ----------------------------------------------------------
+    def __array__(self, dtype=None, copy=None):
+        out = to_numpy(self)
+        return out.astype(dtype) if dtype is not None else out
+
+    def item(self):
+        return to_numpy(self).reshape(()).item()
+
+    def tolist(self):
+        return to_numpy(self).tolist()
+
+    # -- views / layout ----------------------------------------------------------
+    @property
+    def T(self) -> "array":
+        return transpose(self)
+
+    def transpose(self, *axes) -> "array":
+        if len(axes) == 1 and isinstance(axes[0], (list, tuple)):
+            axes = tuple(axes[0])
+        return transpose(self, axes or None)
+
+    def swapaxes(self, a: int, b: int) -> "array":
+        return swapaxes(self, a, b)
+
+    def reshape(self, *shape) -> "array":
+        if len(shape) == 1 and isinstance(shape[0], (list, tuple)):
+            shape = tuple(shape[0])
+        return reshape(self, shape)
+
+    def flatten(self) -> "array":
+        return reshape(self, (-1,))
+
+    def astype(self, dtype) -> "array":
+        return astype(self, dtype)
+
+    def __getitem__(self, idx) -> "array":
+        return array._wrap(self._t[idx])
+
+    # -- reductions --------------------------------------------------------------
+    def sum(self, axis=None, keepdims=False):
+        return sum(self, axis=axis, keepdims=keepdims)
+
+    def mean(self, axis=None, keepdims=False):
+        return mean(self, axis=axis, keepdims=keepdims)
+
+    def max(self, axis=None, keepdims=False):
+        return max(self, axis=axis, keepdims=keepdims)
+
+    def min(self, axis=None, keepdims=False):
+        return min(self, axis=axis, keepdims=keepdims)
+
+    # -- operators ---------------------------------------------------------------
+    def __add__(self, o):
+        return _binary("add", self, o)
+
+    def __radd__(self, o):
+        return _binary("add", o, self)
+
+    def __sub__(self, o):
+        return _binary("sub", self, o)
+
+    def __rsub__(self, o):
+        return _binary("sub", o, self)
+
+    def __mul__(self, o):
+        return _binary("mul", self, o)
+
+    def __rmul__(self, o):
+        return _binary("mul", o, self)
+
+    def __truediv__(self, o):
+        return _binary("div", self, o)
+
+    def __rtruediv__(self, o):
+        return _binary("div", o, self)
+
+    def __floordiv__(self, o):
+        return _binary("floor_divide", self, o)
+
+    def __mod__(self, o):
+        return _binary("remainder", self, o)
+
+    def __pow__(self, o):
+        return _binary("power", self, o)
+
+    def __rpow__(self, o):
+        return _binary("power", o, self)
+
+    def __neg__(self):
+        return _unary("negative", self)
+
+    def __abs__(self):
+        return _unary("abs", self)
+
+    def __eq__(self, o):  # noqa: D105  (elementwise, as in MLX)
+        return _binary("eq", self, o, out_bool=True)
+
+    def __ne__(self, o):
+        return _binary("ne", self, o, out_bool=True)
+
+    def __lt__(self, o):
+        return _binary("lt", self, o, out_bool=True)
+
+    def __le__(self, o):
+        return _binary("le", self, o, out_bool=True)
+
+    def __gt__(self, o):
+        return _binary("gt", self, o, out_bool=True)
+
+    def __ge__(self, o):
+        return _binary("ge", self, o, out_bool=True)
+
+    __hash__ = object.__hash__
+
+    def __matmul__(self, o):
+        return matmul(self, o)
+
+    def __rmatmul__(self, o):
+        return matmul(o, self)
+
+
+# ---------------------------------------------------------------------------
+# host <-> device
+# ---------------------------------------------------------------------------
+
+_scalar_cache: dict[tuple, torch.Tensor] = {}
+
+
+def _host_to_device(val: Any, dtype: Any) -> torch.Tensor:
+    d = dt.from_any(dtype) if dtype is not None else None
+    if isinstance(val, (bool, numbers.Number)) and not isinstance(val, np.ndarray):
+        if d is None:
+            d = bool_ if isinstance(val, bool) else (int32 if isinstance(val, int) else float32)
+        key = (type(val).__name__, val if not (isinstance(val, float) and math.isnan(val)) else "nan", d.name)
+        t = _scalar_cache.get(key)
+        if t is None:
+            t = _from_numpy(np.asarray(val).astype(np.float64 if d.kind == "f" else None), d)
+            _scalar_cache[key] = t
+        return t
+    a = np.asarray(val)
+    if d is None:
+        if a.dtype == np.float64:
+            d = float32
+        elif a.dtype == np.int64 and not isinstance(val, np.ndarray):
+            d = int32
+        else:
+            d = dt.from_any(a.dtype)
+    return _from_numpy(a, d)
+
+
+def _from_numpy(a: np.ndarray, d: Dtype) -> torch.Tensor:
+    a = np.asarray(a)
+    if d.kind == "f" and a.dtype != d.np:
+        # float64 and other floats round through fp32, as inlined literals do
+        a = a.astype(np.float32) if a.dtype.kind == "f" or a.dtype == bfloat16.np else a
+    host = np.ascontiguousarray(a.astype(d.np))
+    if d is bfloat16:
+        t = torch.from_numpy(host.view(np.int16)).view(torch.bfloat16)
+    else:
+        t = torch.from_numpy(host)
+    return t.to(device(), non_blocking=False)
+
+
+def to_numpy(a: "array") -> np.ndarray:
+    t = a._t.detach()
+    if t.dtype == torch.bfloat16:
+        host = t.contiguous().cpu().view(torch.int16).numpy().view(bfloat16.np)
+        return host
+    return t.cpu().numpy()
+
+
+def asarray_device(x: Any, contiguous: bool = True) -> array:
+    """Coerce to an `array` on the device, materialising strided views."""
+    a = x if isinstance(x, array) else array(x)
+    if contiguous and not a._t.is_contiguous():
+        a = contiguous_copy(a)
+    return a
+
+
+def empty(shape: Sequence[int], dtype: Any) -> array:
+    d = dt.from_any(dtype)
+    return array._wrap(torch.empty(tuple(shape), dtype=d.torch, device=device()))
+
+
+def contiguous_copy(a: array) -> array:
+    """Materialise a strided view with the strided-copy kernel."""
+    t = a._t
+    out = torch.empty(t.shape, dtype=t.dtype, device=t.device)
+    if t.numel() == 0:
+        return array._wrap(out)
+    # Drop size-1 dims and merge nothing: the kernel takes up to 8 dims.
+    shape = [s for s in t.shape]
+    strides = list(t.stride())
+    if len(shape) == 0:
+        shape, strides = [1], [1]
+    if len(shape) > 8:
+        keep = [(s, st) for s, st in zip(shape, strides) if s != 1]
+        shape = [s for s, _ in keep] or [1]
+        strides = [st for _, st in keep] or [1]
+        if len(shape) > 8:
+            raise NotImplementedError("strided copy of more than 8 non-unit dims")
+    n = len(shape)
+    cs = (ctypes.c_int64 * n)(*shape)
+    cst = (ctypes.c_int64 * n)(*strides)
+    _native.call(
+        "phew_copy_strided",
+        ctypes.c_void_p(t.data_ptr()),
+        ctypes.c_void_p(out.data_ptr()),
+        n, cs, cst, t.element_size(), _stream(),
+    )
+    return array._wrap(out)
+
+
+# ---------------------------------------------------------------------------
+# elementwise ops through the fused-chain emitter
+# ---------------------------------------------------------------------------
+
+_kernel_cache: dict[tuple, tuple] = {}
+
+
+def _broadcast_shapes(*shapes) -> tuple:
+    nd = builtins_max((len(s) for s in shapes), default=0)
+    out = []
+    for i in range(nd):
+        d = 1
+        for s in shapes:
+            p = (1,) * (nd - len(s)) + tuple(s)
+            if p[i] != 1:
+                if d != 1 and d != p[i]:
+                    raise ValueError(f"shapes {shapes} cannot be broadcast")
+                d = p[i]
+        out.append(d)
+    return tuple(out)
+
+
+builtins_max = max  # shadowed below by mx.max
+builtins_min = min
+builtins_sum = sum
+
+
+def _elementwise(op: str, operands: list, out_dtype: Dtype | None = None,
+                 out_bool: bool = False) -> array:
+    """Run `op` over operands (arrays or Python scalars) with one emitted kernel."""
+    arrays = [x for x in operands if isinstance(x, array)]
+    if not arrays:
+        raise TypeError(f"{op}: needs at least one array operand")
+    # Result dtype: arrays promote; Python scalars are weak.
+    res = arrays[0].dtype
+    for a in arrays[1:]:
+        res = dt.promote(res, a.dtype)
+    for x in operands:
+        if not isinstance(x, array):
+            res = dt.scalar_dtype(x, res)
+    compute_dt = res
+    node_dt = bool_ if out_bool else (out_dtype or res)
+    shape = _broadcast_shapes(*[a.shape for a in arrays])
+    key_parts = []
+    for x in operands:
+        if isinstance(x, array):
+            key_parts.append(("a", x.shape, x.dtype.name))
+        else:
+            key_parts.append(("s", type(x).__name__, repr(x)))
+    key = (op, tuple(key_parts), compute_dt.name, node_dt.name)
+    entry = _kernel_cache.get(key)
+    if entry is None:
+        entry = _build_elementwise(op, operands, compute_dt, node_dt, shape)
+        _kernel_cache[key] = entry
+    kern, in_positions = entry
+    ins = [asarray_device(operands[i]) for i in in_positions]
+    out = kern(
+        inputs=ins,
+        output_shapes=[shape],
+        output_dtypes=[node_dt],
+        grid=(elementwise_threads(_numel(shape)), 1, 1),
+        threadgroup=(256, 1, 1),
+    )
+    return out[0]
+
+
+def _numel(shape) -> int:
+    n = 1
+    for s in shape:
+        n *= int(s)
+    return n
+
+
+def _build_elementwise(op, operands, compute_dt: Dtype, node_dt: Dtype, shape):
+    ext, chain, args, positions = [], [], [], []
+    for i, x in enumerate(operands):
+        if isinstance(x, array):
+            n = NodeSpec("Input", x.shape, x.dtype.name)
+            ext.append(n)
+            positions.append(i)
+            if x.dtype is not compute_dt and op not in ("where",):
+                c = NodeSpec("Cast", x.shape, compute_dt.name, inputs=[n.id],
+                             target_dtype=compute_dt.name)
+                chain.append(c)
+                n = c
+            args.append(n)
+        else:
+            c = NodeSpec("Constant", (), compute_dt.name, value=x)
+            chain.append(c)
+            args.append(c)
+    node = NodeSpec("Elementwise", shape, node_dt.name, inputs=[a.id for a in args], op=op)
+    chain.append(node)
+    src, in_names, out_names = SubgraphCUDACodegen().emit(chain, ext, [node])
+    kern = CudaKernel(f"phew_ew_{op}", in_names, out_names, src)
+    return kern, positions
+
+
+def _binary(op: str, a, b, out_bool: bool = False) -> array:
+    return _elementwise(op, [a, b], out_bool=out_bool)
+
+
+def _unary(op: str, a) -> array:
+    return _elementwise(op, [asarray_device(a, contiguous=False)])
+
+
+def _make_unary(op):
+    def f(x, *_, **__):
+        return _unary(op, x)
+
+    f.__name__ = op
+    return f
+
+
+for _op in (
+    "exp", "log", "sqrt", "rsqrt", "sigmoid", "tanh", "abs", "negative", "square", "sin",
+    "cos", "tan", "erf", "erfinv", "expm1", "log1p", "log2", "log10", "ceil", "floor",
+    "round", "sign", "reciprocal", "arcsin", "arccos", "arctan", "arcsinh", "arccosh",
+    "arctanh", "sinh", "cosh", "degrees", "radians", "logical_not",
+):
+    globals()[_op] = _make_unary(_op)
+
+
+def _make_binary(op, out_bool=False):
+    def f(a, b, *_, **__):
+        return _binary(op, a, b, out_bool=out_bool)
+
+    f.__name__ = op
+    return f
+
+
+add = _make_binary("add")
+subtract = _make_binary("sub")
+multiply = _make_binary("mul")
+divide = _make_binary("div")
+maximum = _make_binary("maximum")
+minimum = _make_binary("minimum")
+power = _make_binary("power")
+logaddexp = _make_binary("logaddexp")
+floor_divide = _make_binary("floor_divide")
+remainder = _make_binary("remainder")
+arctan2 = _make_binary("arctan2")
+equal = _make_binary("eq", True)
+not_equal = _make_binary("ne", True)
+greater = _make_binary("gt", True)
+greater_equal = _make_binary("ge", True)
+less = _make_binary("lt", True)
+less_equal = _make_binary("le", True)
+logical_and = _make_binary("logical_and", True)
+logical_or = _make_binary("logical_or", True)
+
+
+def where(cond, a, b) -> array:
+    c = cond if isinstance(cond, array) else array(cond)
+    vals = [x for x in (a, b) if isinstance(x, array)]
+    res = vals[0].dtype if vals else float32
+    for v in vals[1:]:
+        res = dt.promote(res, v.dtype)
+    a2 = a if not isinstance(a, array) or a.dtype is res else astype(a, res)
+    b2 = b if not isinstance(b, array) or b.dtype is res else astype(b, res)
+    return _elementwise("where", [c, a2, b2], out_dtype=res)
+
+
+def astype(a, dtype) -> array:
+    d = dt.from_any(dtype)
+    a = a if isinstance(a, array) else array(a)
+    if a.dtype is d:
+        return a
+    key = ("cast", a.shape, a.dtype.name, d.name)
+    entry = _kernel_cache.get(key)
+    if entry is None:
+        x = NodeSpec("Input", a.shape, a.dtype.name)
+        c = NodeSpec("Cast", a.shape, d.name, inputs=[x.id], target_dtype=d.name)
+        src, i, o = SubgraphCUDACodegen().emit([c], [x], [c])
+        entry = (CudaKernel("phew_cast", i, o, src), [0])
+        _kernel_cache[key] = entry
+    kern, _ = entry
+    return kern(inputs=[asarray_device(a)], output_shapes=[a.shape], output_dtypes=[d],
+                grid=(elementwise_threads(a.size), 1, 1), threadgroup=(256, 1, 1))[0]
+
+
+def silu(x):
+    return _unary("silu", x)
+
+
+def gelu(x):
+    return _unary("gelu", x)
+
+
+def relu(x):
+    return _unary("relu", x)
+
+
+# ---------------------------------------------------------------------------
+# layout
+# ---------------------------------------------------------------------------
+
+
+def transpose(a, axes=None) -> array:
+    a = a if isinstance(a, array) else array(a)
+    if axes is None:
+        axes = tuple(range(a.ndim - 1, -1, -1))
+    axes = tuple(int(x) % builtins_max(a.ndim, 1) for x in axes)
+    return array._wrap(a._t.permute(*axes))
+
+
+def swapaxes(a, x: int, y: int) -> array:
+    axes = list(range(a.ndim))
+    x, y = x % a.ndim, y % a.ndim
+    axes[x], axes[y] = axes[y], axes[x]
+    return transpose(a, axes)
+
+
+def reshape(a, shape) -> array:
+    a = a if isinstance(a, array) else array(a)
+    shape = tuple(int(s) for s in (shape if isinstance(shape, (list, tuple)) else (shape,)))
+    src = a if a._t.is_contiguous() else contiguous_copy(a)
+    return array._wrap(src._t.view(shape))
+
+
+def expand_dims(a, axis) -> array:
+    axes = axis if isinstance(axis, (list, tuple)) else [axis]
+    t = a._t
+    for ax in sorted(int(x) % (t.dim() + len(axes)) for x in axes):
+        t = t.unsqueeze(ax)
+    return array._wrap(t)
+
+
+def squeeze(a, axis=None) -> array:
+    t = a._t
+    if axis is None:
+        return array._wrap(t.squeeze())
+    axes = axis if isinstance(axis, (list, tuple)) else [axis]
+    for ax in sorted((int(x) % t.dim() for x in axes), reverse=True):
+        t = t.squeeze(ax)
+    return array._wrap(t)
+
+
+def broadcast_to(a, shape) -> array:
+    return array._wrap(a._t.expand(*shape))
+
+
+# ---------------------------------------------------------------------------
+# reductions
+# ---------------------------------------------------------------------------
+
+
+def _norm_axes(a: array, axis) -> tuple:
+    if axis is None:
+        return tuple(range(a.ndim))
+    if isinstance(axis, (list, tuple)):
+        return tuple(sorted(int(x) % a.ndim for x in axis))
+    return (int(axis) % a.ndim,)
+
+
+def _reduce(opname: str, a, axis=None, keepdims=False) -> array:
+    a = a if isinstance(a, array) else array(a)
+    if a.dtype.code is None:
+        raise NotImplementedError(f"{opname} over {a.dtype.name} arrays")
+    axes = _norm_axes(a, axis)
+    shape = a.shape
+    out_shape_keep = tuple(1 if i in axes else s for i, s in enumerate(shape))
+    out_shape = out_shape_keep if keepdims else tuple(s for i, s in enumerate(shape) if i not in axes)
+    if not axes:
+        return a
+    contiguous_block = axes == tuple(range(axes[0], axes[-1] + 1))
+    src = asarray_device(a)
+    if not contiguous_block:
+        rest = [i for i in range(a.ndim) if i not in axes]
+        src = contiguous_copy(transpose(src, rest + list(axes)))
+        shape = tuple(a.shape[i] for i in rest) + tuple(a.shape[i] for i in axes)
+        lo = len(rest)
+        axes = tuple(range(lo, a.ndim))
+    outer = _numel(shape[: axes[0]])
+    red = _numel(shape[axes[0] : axes[-1] + 1])
+    inner = _numel(shape[axes[-1] + 1 :])
+    out = empty(out_shape, a.dtype)
+    if out.size == 0:
+        return out
+    if red == 0:
+        fill = {"sum": 0.0, "mean": float("nan"), "prod": 1.0, "max": -math.inf, "min": math.inf}
+        out._t.fill_(fill[opname])
+        return out
+    _native.call(
+        "phew_reduce", _native.REDUCE_OPS[opname], ctypes.c_void_p(src._t.data_ptr()),
+        ctypes.c_void_p(out._t.data_ptr()), outer, red, inner, a.dtype.code, _stream(),
+    )
+    return out
+
+
+def sum(a, axis=None, keepdims=False, **_) -> array:  # noqa: A001
+    return _reduce("sum", a, axis, keepdims)
+
+
+def mean(a, axis=None, keepdims=False, **_) -> array:
+    return _reduce("mean", a, axis, keepdims)
+
+
+def max(a, axis=None, keepdims=False, **_) -> array:  # noqa: A001
+    return _reduce("max", a, axis, keepdims)
+
+
+def min(a, axis=None, keepdims=False, **_) -> array:  # noqa: A001
+    return _reduce("min", a, axis, keepdims)
+
+
+def prod(a, axis=None, keepdims=False, **_) -> array:
+    return _reduce("prod", a, axis, keepdims)
+
+
+def softmax(a, axis=-1, precise=False, **_) -> array:
+    a = a if isinstance(a, array) else array(a)
+    if a.dtype.code is None:
+        raise NotImplementedError(f"softmax over {a.dtype.name} arrays")
+    if isinstance(axis, (list, tuple)):
+        if len(axis) != 1:
+            raise NotImplementedError("softmax over several axes")
+        axis = axis[0]
+    ax = int(axis) % a.ndim
+    if ax != a.ndim - 1:
+        moved = swapaxes(a, ax, a.ndim - 1)
+        return swapaxes(softmax(moved, axis=-1), ax, a.ndim - 1)
+    src = asarray_device(a)
+    out = empty(a.shape, a.dtype)
+    cols = a.shape[-1] if a.ndim else 1
+    rows = a.size // builtins_max(cols, 1)
+    if a.size:
+        _native.call(
+            "phew_softmax", ctypes.c_void_p(src._t.data_ptr()), ctypes.c_void_p(out._t.data_ptr()),
+            rows, cols, a.dtype.code, _stream(),
+        )
+    return out
+
+
+# ---------------------------------------------------------------------------
+# constructors, evaluation and compile
+# ---------------------------------------------------------------------------
+
+
+def zeros(shape, dtype=float32) -> array:
+    d = dt.from_any(dtype)
+    shape = (shape,) if isinstance(shape, int) else tuple(shape)
+    return array._wrap(torch.zeros(shape, dtype=d.torch, device=device()))
+
+
+def ones(shape, dtype=float32) -> array:
+    d = dt.from_any(dtype)
+    shape = (shape,) if isinstance(shape, int) else tuple(shape)
+    return array._wrap(torch.ones(shape, dtype=d.torch, device=device()))
+
+
+def full(shape, value, dtype=None) -> array:
+    d = dt.from_any(dtype) if dtype is not None else (float32 if isinstance(value, float) else int32)
+    shape = (shape,) if isinstance(shape, int) else tuple(shape)
+    return array._wrap(torch.full(shape, value, dtype=d.torch, device=device()))
+
+
+def zeros_like(a) -> array:
+    return array._wrap(torch.zeros(a.shape, dtype=a._t.dtype, device=device()))
+
+
+def ones_like(a) -> array:
+    return array._wrap(torch.ones(a.shape, dtype=a._t.dtype, device=device()))
+
+
+def eval(*args) -> None:  # noqa: A001  (MLX name)
+    """Arrays are computed eagerly; nothing to force."""
+    return None
+
+
+def async_eval(*args) -> None:
+    return None
+
+
+def synchronize(stream=None) -> None:
+    torch.cuda.current_stream().synchronize()
+
+
+def matmul(a, b) -> array:
+    from ..ops import matmul as _mm
+
+    return _mm(a, b)
+
+
+def compile(fn=None, *, shapeless: bool = False, **_):  # noqa: A001  (MLX name)
+    """``@mx.compile``: see :mod:`phew_b200.graphs` for the CUDA-graph capture."""
+    from ..graphs import compile_function
+
+    if fn is None:
+        return lambda f: compile_function(f)
+    return compile_function(fn)
+
+
+class _Metal:
+    @staticmethod
+    def is_available() -> bool:
+        return False
+
+
+metal = _Metal()
+
+
+def is_available() -> bool:
+    return torch.cuda.is_available()
+
+
+def device_info() -> dict:
+    info = _native.DeviceInfo()
+    _native.call("phew_device_query", torch.cuda.current_device(), ctypes.byref(info))
+    return {
+        "device_name": info.name.decode(),
+        "architecture": f"sm_{info.cc_major}{info.cc_minor}",
+        "sm_count": info.sm_count,
+        "memory_size": info.hbm_bytes,
+        "l2_cache_size": info.l2_bytes,
+    }
+
+
+_live_arrays = weakref.WeakSet()

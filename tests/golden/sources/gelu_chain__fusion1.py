@@ -1,0 +1,90 @@
+import phew_b200.mx as mx
+from phew_b200.mx import fast
+
+@mx.compile
+def optimized(x, a, b, c, *_, **__):
+    _kernel_119 = mx.fast.cuda_kernel(
+        name="kernel_119",
+        input_names=['inp0', 'inp1', 'inp2', 'inp3'],
+        output_names=['out0'],
+        source="""    // fused elementwise chain: 14 ops, 4 inputs, 1 outputs, 33554432 elements
+    // phew-io: idx32 out=4096x8192 inp0=full inp1=suffix:8192 inp2=suffix:8192 inp3=full
+    const unsigned int phew_n = (unsigned int)out0_size;
+    const unsigned int phew_tid = (unsigned int)blockIdx.x * blockDim.x + threadIdx.x;
+    const unsigned int phew_nthreads = (unsigned int)gridDim.x * blockDim.x;
+    unsigned int phew_tail = 0;
+    const float v7 = __int_as_float(0x3f000000) /* 0.5 */;
+    const phew_u32 v7_x2 = 0x38003800u;
+    const float v11 = __int_as_float(0x3d372000) /* 0.044708251953125 */;
+    const phew_u32 v11_x2 = 0x29b929b9u;
+    const float v14 = __int_as_float(0x3f4c4000) /* 0.7978515625 */;
+    const phew_u32 v14_x2 = 0x3a623a62u;
+    const float v17 = __int_as_float(0x3f800000) /* 1.0 */;
+    const phew_u32 v17_x2 = 0x3c003c00u;
+    if (((reinterpret_cast<phew_uptr>(inp0) | reinterpret_cast<phew_uptr>(inp1) | reinterpret_cast<phew_uptr>(inp2) | reinterpret_cast<phew_uptr>(inp3) | reinterpret_cast<phew_uptr>(out0)) & 15u) == 0u) {
+      const unsigned int phew_nvec = phew_n / 8u;
+      for (unsigned int phew_v = phew_tid; phew_v < phew_nvec; phew_v += phew_nthreads) {
+        const unsigned int elem = phew_v * 8u;
+        const phew_vec<phew_f16, 8> ld0 = phew_ldv<phew_f16, 8>(inp0 + elem);
+        const phew_vec<phew_f16, 8> ld1 = phew_ldv<phew_f16, 8>(inp1 + elem % 8192u);
+        const phew_vec<phew_f16, 8> ld2 = phew_ldv<phew_f16, 8>(inp2 + elem % 8192u);
+        const phew_vec<phew_f16, 8> ld3 = phew_ldv<phew_f16, 8>(inp3 + elem);
+        phew_vec<phew_f16, 8> st0;
+        #pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const phew_u32 v1 = phew_pair(ld0, p);
+          const phew_u32 v2 = phew_pair(ld1, p);
+          const phew_u32 v3 = phew_pair(ld2, p);
+          const phew_u32 v4 = phew_pair(ld3, p);
+          const phew_u32 v5 = phew_h2_mul(v1, v2);
+          const phew_u32 v6 = phew_h2_add(v5, v3);
+          const phew_u32 v8 = phew_h2_mul(v6, v7_x2);
+          const phew_u32 v9 = phew_h2_mul(v6, v6);
+          const phew_u32 v10 = phew_h2_mul(v9, v6);
+          const phew_u32 v12 = phew_h2_mul(v10, v11_x2);
+          const phew_u32 v13 = phew_h2_add(v6, v12);
+          const phew_u32 v15 = phew_h2_mul(v13, v14_x2);
+          const phew_u32 v16 = phew_h2_pack(phew_tanh16(phew_h2_lo(v15)), phew_tanh16(phew_h2_hi(v15)));
+          const phew_u32 v18 = phew_h2_add(v16, v17_x2);
+          const phew_u32 v19 = phew_h2_mul(v8, v18);
+          const phew_u32 v20 = phew_h2_pack(phew_sigmoid16(phew_h2_lo(v4)), phew_sigmoid16(phew_h2_hi(v4)));
+          const phew_u32 v21 = phew_h2_mul(v19, v20);
+          const phew_u32 v22 = phew_h2_add(v21, v1);
+          phew_set_pair(st0, p, v22);
+        }
+        phew_stv<phew_f16, 8>(out0 + elem, st0);
+      }
+      phew_tail = phew_nvec * 8u;
+    }
+    for (unsigned int elem = phew_tail + phew_tid; elem < phew_n; elem += phew_nthreads) {
+      const float v1 = phew_ld(inp0[elem]);
+      const float v2 = phew_ld(inp1[elem % 8192u]);
+      const float v3 = phew_ld(inp2[elem % 8192u]);
+      const float v4 = phew_ld(inp3[elem]);
+      const float v5 = phew_rnd_f16(__fmul_rn(v1, v2));
+      const float v6 = phew_rnd_f16(__fadd_rn(v5, v3));
+      const float v8 = phew_rnd_f16(__fmul_rn(v6, v7));
+      const float v9 = phew_rnd_f16(__fmul_rn(v6, v6));
+      const float v10 = phew_rnd_f16(__fmul_rn(v9, v6));
+      const float v12 = phew_rnd_f16(__fmul_rn(v10, v11));
+      const float v13 = phew_rnd_f16(__fadd_rn(v6, v12));
+      const float v15 = phew_rnd_f16(__fmul_rn(v13, v14));
+      const float v16 = phew_rnd_f16(phew_tanh16(v15));
+      const float v18 = phew_rnd_f16(__fadd_rn(v16, v17));
+      const float v19 = phew_rnd_f16(__fmul_rn(v8, v18));
+      const float v20 = phew_rnd_f16(phew_sigmoid16(v4));
+      const float v21 = phew_rnd_f16(__fmul_rn(v19, v20));
+      const float v22 = phew_rnd_f16(__fadd_rn(v21, v1));
+      out0[elem] = phew_st_f16(v22);
+    }""",
+    )
+    kernel1_out = _kernel_119(
+        inputs=[x, a, b, c],
+        output_shapes=[x.shape],
+        output_dtypes=[mx.float16],
+        grid=(mx.elementwise_threads(x.size), 1, 1),
+        threadgroup=(256, 1, 1),
+        template=[],
+    )
+    kernel1 = kernel1_out[0]
+    return kernel1

@@ -1,0 +1,66 @@
+"""The C-ABI library loads without a GPU and exports every declared symbol."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADERS = sorted((ROOT / "include").glob("*.h"))
+DECL = re.compile(r"^\s*(?:int|size_t|void)\s+\*?\s*(phew_\w+)\s*\(", re.M)
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from phew_b200 import _native
+    from phew_b200.build import build
+
+    build()
+    return _native.load()
+
+
+def declared() -> set[str]:
+    names = set()
+    for h in HEADERS:
+        names |= set(DECL.findall(h.read_text()))
+    return names
+
+
+def test_header_declares_entry_points():
+    names = declared()
+    for required in ("phew_compile", "phew_launch", "phew_rms_norm", "phew_softmax",
+                     "phew_compare", "phew_last_error"):
+        assert required in names
+
+
+def test_every_declared_symbol_is_exported(lib):
+    for name in declared():
+        assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+
+
+def test_binding_covers_header():
+    from phew_b200 import _native
+
+    assert declared() == set(_native.EXPORTED_SYMBOLS)
+
+
+def test_abi_version_and_error_path(lib):
+    from phew_b200 import _native
+
+    assert lib.phew_abi_version() >= 1
+    # Invalid arguments are rejected on the host before any CUDA call.
+    st = lib.phew_rms_norm(None, None, None, 4, 4, ctypes.c_float(1e-5), 0, None)
+    assert st == _native.PHEW_ERR_INVALID
+    assert "null pointer" in _native.last_error()
+    st = lib.phew_copy_strided(None, None, 1, None, None, 4, None)
+    assert st == _native.PHEW_ERR_INVALID
+
+
+def test_compare_scratch_is_bounded(lib):
+    lib.phew_compare_scratch_bytes.restype = ctypes.c_size_t
+    small = lib.phew_compare_scratch_bytes(ctypes.c_int64(10))
+    big = lib.phew_compare_scratch_bytes(ctypes.c_int64(1 << 40))
+    assert 0 < small == big <= 1 << 20

@@ -135,6 +135,30 @@ int phew_copy_strided(const void* src, void* dst, int ndim,
  * times warm caches). */
 int phew_l2_flush(void* buf, size_t bytes, void* stream);
 
+/* ---- tensor-core GEMM -------------------------------------------------- */
+
+/* C[b] = A[b] @ B[b] (+ optional fused row scale), fp32 accumulation on the
+ * tcgen05 tensor cores with TMA-fed, 128B-swizzled shared-memory tiles.
+ *   A: [M, K] rows of stride lda (elements), K contiguous.
+ *   B: b_layout 0 -> [K, N] rows of stride ldb, N contiguous
+ *      b_layout 1 -> [N, K] rows of stride ldb, K contiguous (e.g. k.T)
+ *   C: [M, N] rows of stride ldc, dtype out_dtype.
+ *   stride_a / stride_b / stride_c: element strides between batches; 0 on an
+ *   operand broadcasts it over the batch.
+ *   row_scale = 1 multiplies row m of the product by
+ *   rsqrt(mean_k(A[m, k]^2) + eps), computed inside the kernel from the A tiles
+ *   it already loads (the normed matmul (x @ W) * rsqrt(mean(x^2) + eps)).
+ *   error_flag (device int, may be NULL) receives PHEW_ERR_TIMEOUT if a
+ *   bounded pipeline wait ran out.
+ * in_dtype bf16/f16 use the tensor cores when every row stride and base is
+ * 16-byte aligned; f32 and unaligned layouts use a SIMT kernel.
+ * Replaces `a @ b` (emit/codegen.py:129-133) and the normed-matmul rewrite
+ * rms_norm(x) @ W (rules/primitive_subst.py:156-240). */
+int phew_gemm(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+              int64_t batch, int64_t lda, int64_t ldb, int64_t ldc, int64_t stride_a,
+              int64_t stride_b, int64_t stride_c, int b_layout, int in_dtype, int out_dtype,
+              int row_scale, float eps, int* error_flag, void* stream);
+
 /* ---- equivalence comparison -------------------------------------------- */
 
 /* Result of one baseline/candidate comparison, written to DEVICE memory. */

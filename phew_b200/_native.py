@@ -41,6 +41,7 @@ EXPORTED_SYMBOLS = (
     "phew_reduce",
     "phew_copy_strided",
     "phew_l2_flush",
+    "phew_gemm",
     "phew_compare_scratch_bytes",
     "phew_compare",
 )
@@ -114,6 +115,10 @@ _SIGNATURES = {
         _int,
     ),
     "phew_l2_flush": ([_vp, ctypes.c_size_t, _vp], _int),
+    "phew_gemm": (
+        [_vp, _vp, _vp] + [_i64] * 10 + [_int, _int, _int, _int, ctypes.c_float, _vp, _vp],
+        _int,
+    ),
     "phew_compare_scratch_bytes": ([_i64], ctypes.c_size_t),
     "phew_compare": (
         [_vp, _vp, _i64, _int, ctypes.c_double, ctypes.c_double, _vp, ctypes.c_size_t, _vp, _vp],

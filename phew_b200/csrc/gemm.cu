@@ -1,0 +1,504 @@
+// Dense GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+//   C[b, m, n] = sum_k A[b, m, k] * B[b, k, n]      (bf16 or fp16 in, fp32 accumulate)
+//   optional fused row scale: C[b, m, :] *= rsqrt(mean_k(A[b, m, k]^2) + eps)
+//
+// Stands in for `a @ b` (phew emit/codegen.py:129-133, MatMul ir/ops.py:35-40)
+// and, with the row scale, for the normed matmul `(x @ W) * rsqrt(mean(x^2) + eps)`
+// that rules/primitive_subst.py:156-240 rewrites to rms_norm(x) @ W.
+//
+// Layout in HBM: A row-major [M, K] (K-major operand).  B either row-major
+// [K, N] (N contiguous: an MN-major operand, `b_layout = 0`) or row-major
+// [N, K] (K contiguous: a K-major operand, `b_layout = 1`, e.g. k.T in q @ k.T).
+// Batches are strided; a zero batch stride broadcasts the operand.
+//
+// One CTA computes one BM x BN tile (BM = 128, BN = 128 or 256):
+//   warp 0      TMA producer: 128B-swizzled tiles of A and B into a STAGES-deep
+//               shared-memory ring (no cluster multicast: these kernels also run
+//               in multi-GPU jobs)
+//   warp 1      allocates TMEM, one elected lane issues tcgen05.mma (M=128,
+//               N=BN, K=16) into a TMEM fp32 accumulator and commits each stage
+//               back to the producer
+//   warps 2-5   epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
+//               32*(w%4)..), scale, convert, store; with the fused row scale they
+//               also accumulate each row's sum of squares from the A tiles while
+//               the main loop runs, so the norm costs no extra HBM pass
+// Every mbarrier wait is bounded; a wait that runs out sets *error_flag and the
+// kernel winds down instead of spinning.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace phew {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 x 16-bit = one 128-byte swizzle row
+constexpr int kNumThreads = 192;
+constexpr uint32_t kSpinLimit = 1u << 26;
+
+template <int BN> struct Cfg {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int TMEM_COLS = BN;
+};
+
+struct Params {
+  int M, N, K;
+  int b_mn_major;  // 1: B is [K, N] (N contiguous)
+  int batch;
+  int a_batched, b_batched;
+  void* C;
+  long long ldc;
+  long long c_batch_stride;
+  int out_dtype;  // PHEW_F32 / PHEW_F16 / PHEW_BF16
+  int row_scale;  // 1: fused rsqrt(mean(A^2) + eps) per row
+  float eps;
+  int* error_flag;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Waits for the phase with `parity` to complete; false after kSpinLimit tries.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* tm, uint64_t* bar, int c0,
+                                            int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor for tcgen05 (SWIZZLE_128B, 1024-byte aligned tiles).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFF) >> 4);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFF) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFF) << 32;
+  d |= static_cast<uint64_t>(1) << 46;  // descriptor version for tcgen05
+  d |= static_cast<uint64_t>(2) << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulator, A/B bf16 or f16,
+// A K-major, B K- or MN-major, M = 128, N = BN.
+__host__ __device__ constexpr uint32_t instr_desc(int bf16, int b_mn_major, int n) {
+  return (1u << 4) | (static_cast<uint32_t>(bf16) << 7) | (static_cast<uint32_t>(bf16) << 10) |
+         (static_cast<uint32_t>(b_mn_major) << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                     uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <typename T>
+__device__ __forceinline__ void store_row32(T* dst, const float* v, int ncols) {
+  if (ncols >= 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+    constexpr int PER = 16 / sizeof(T);
+#pragma unroll
+    for (int c = 0; c < 32; c += PER) {
+      uint4 raw;
+      T* e = reinterpret_cast<T*>(&raw);
+#pragma unroll
+      for (int i = 0; i < PER; ++i) e[i] = from_f32<T>(v[c + i]);
+      *reinterpret_cast<uint4*>(dst + c) = raw;
+    }
+  } else {
+    for (int i = 0; i < 32 && i < ncols; ++i) dst[i] = from_f32<T>(v[i]);
+  }
+}
+
+template <int BN, bool BF16>
+__global__ void __launch_bounds__(kNumThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const Params p) {
+  using C = Cfg<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* accum_full = empty + C::STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_full + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN;
+  const int m0 = blockIdx.y * BM;
+  const int bz = blockIdx.z;
+  const int num_kb = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], p.row_scale ? 5 : 1);  // MMA commit (+ 4 epilogue warps)
+    }
+    mbar_init(accum_full, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(C::TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      const int ba = p.a_batched ? bz : 0;
+      const int bb = p.b_batched ? bz : 0;
+      for (int kb = 0; kb < num_kb && ok; ++kb) {
+        const int s = kb % C::STAGES;
+        const uint32_t ph = (kb / C::STAGES) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1)) {
+          ok = false;
+          break;
+        }
+        uint8_t* sa = smem + s * C::STAGE_BYTES;
+        uint8_t* sb = sa + C::A_BYTES;
+        mbar_expect_tx(&full[s], C::STAGE_BYTES);
+        tma_load_3d(sa, &tmA, &full[s], kb * BK, m0, ba);
+        if (p.b_mn_major) {
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j)
+            tma_load_3d(sb + j * (64 * BK * 2), &tmB, &full[s], n0 + j * 64, kb * BK, bb);
+        } else {
+          tma_load_3d(sb, &tmB, &full[s], kb * BK, n0, bb);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc(BF16 ? 1 : 0, 0, BN);
+      const uint32_t idesc_b = p.b_mn_major ? instr_desc(BF16 ? 1 : 0, 1, BN) : idesc;
+      for (int kb = 0; kb < num_kb && ok; ++kb) {
+        const int s = kb % C::STAGES;
+        const uint32_t ph = (kb / C::STAGES) & 1;
+        if (!mbar_wait(&full[s], ph)) {
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
+        const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint64_t ad = smem_desc(sa + kk * 32, 16, 1024);
+          const uint64_t bd = p.b_mn_major ? smem_desc(sb + kk * (16 * 128), 64 * BK * 2, 1024)
+                                           : smem_desc(sb + kk * 32, 16, 1024);
+          umma(tmem, ad, bd, idesc_b, (kb > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
+      }
+      if (ok) umma_commit(accum_full);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    float ss = 0.f;
+    if (p.row_scale) {
+      for (int kb = 0; kb < num_kb && ok; ++kb) {
+        const int s = kb % C::STAGES;
+        const uint32_t ph = (kb / C::STAGES) & 1;
+        if (!mbar_wait(&full[s], ph)) {
+          ok = false;
+          break;
+        }
+        // A row r occupies bytes [r*128, r*128+128) of the tile; the 128B
+        // swizzle only permutes 16-byte chunks within the row.
+        const uint4* row = reinterpret_cast<const uint4*>(smem + s * C::STAGE_BYTES + row_in_tile * 128);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 raw = row[c];
+          const uint16_t* h = reinterpret_cast<const uint16_t*>(&raw);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float x;
+            if (BF16) {
+              x = __uint_as_float(static_cast<uint32_t>(h[i]) << 16);
+            } else {
+              asm("cvt.f32.f16 %0, %1;" : "=f"(x) : "h"(h[i]));
+            }
+            ss = fmaf(x, x, ss);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      }
+    }
+    if (ok && !mbar_wait(accum_full, 0)) ok = false;
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (ok) {
+      const float scale = p.row_scale ? 1.0f / sqrtf(ss / static_cast<float>(p.K) + p.eps) : 1.0f;
+      const int row = m0 + row_in_tile;
+      const long long cbase = static_cast<long long>(bz) * p.c_batch_stride + static_cast<long long>(row) * p.ldc;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        tmem_ld32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + c, v);
+        if (row < p.M && n0 + c < p.N) {
+          if (p.row_scale) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] *= scale;
+          }
+          const int ncols = p.N - (n0 + c);
+          if (p.out_dtype == PHEW_BF16)
+            store_row32(static_cast<bf16*>(p.C) + cbase + n0 + c, v, ncols);
+          else if (p.out_dtype == PHEW_F16)
+            store_row32(static_cast<f16*>(p.C) + cbase + n0 + c, v, ncols);
+          else
+            store_row32(static_cast<float*>(p.C) + cbase + n0 + c, v, ncols);
+        }
+      }
+    }
+  }
+  if (!ok && p.error_flag) atomicExch(p.error_flag, PHEW_ERR_TIMEOUT);
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(C::TMEM_COLS));
+  }
+}
+
+// SIMT fallback for shapes the TMA path cannot describe (row strides that are
+// not multiples of 16 bytes): 16 x 16 output tiles, fp32 accumulation.
+template <typename T>
+__global__ void gemm_simt_kernel(const T* A, const T* B, Params p, long long lda, long long ldb,
+                                 long long sa, long long sb) {
+  __shared__ float ta[16][17];
+  __shared__ float tb[16][17];
+  const int bz = blockIdx.z;
+  const int row = blockIdx.y * 16 + threadIdx.y;
+  const int col = blockIdx.x * 16 + threadIdx.x;
+  const T* Ab = A + (p.a_batched ? bz * sa : 0);
+  const T* Bb = B + (p.b_batched ? bz * sb : 0);
+  float acc = 0.f;
+  for (int k0 = 0; k0 < p.K; k0 += 16) {
+    const int ka = k0 + threadIdx.x, kb = k0 + threadIdx.y;
+    ta[threadIdx.y][threadIdx.x] = (row < p.M && ka < p.K) ? to_f32(Ab[row * lda + ka]) : 0.f;
+    float bv = 0.f;
+    if (col < p.N && kb < p.K)
+      bv = p.b_mn_major ? to_f32(Bb[static_cast<long long>(kb) * ldb + col])
+                        : to_f32(Bb[static_cast<long long>(col) * ldb + kb]);
+    tb[threadIdx.y][threadIdx.x] = bv;
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 16; ++k) acc = fmaf(ta[threadIdx.y][k], tb[k][threadIdx.x], acc);
+    __syncthreads();
+  }
+  if (row < p.M && col < p.N) {
+    float scale = 1.f;
+    if (p.row_scale) {
+      float ss = 0.f;
+      for (int k = 0; k < p.K; ++k) {
+        const float x = to_f32(Ab[row * lda + k]);
+        ss = fmaf(x, x, ss);
+      }
+      scale = 1.0f / sqrtf(ss / static_cast<float>(p.K) + p.eps);
+    }
+    const long long o = static_cast<long long>(bz) * p.c_batch_stride + static_cast<long long>(row) * p.ldc + col;
+    const float v = acc * scale;
+    if (p.out_dtype == PHEW_BF16) static_cast<bf16*>(p.C)[o] = from_f32<bf16>(v);
+    else if (p.out_dtype == PHEW_F16) static_cast<f16*>(p.C)[o] = from_f32<f16>(v);
+    else static_cast<float*>(p.C)[o] = v;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+int make_map(CUtensorMap* tm, const void* base, CUtensorMapDataType dt, uint64_t d0, uint64_t d1,
+             uint64_t d2, uint64_t s1_bytes, uint64_t s2_bytes, uint32_t b0, uint32_t b1) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(PHEW_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {s1_bytes, s2_bytes};
+  cuuint32_t box[3] = {b0, b1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(tm, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(PHEW_ERR_INVALID, "cuTensorMapEncodeTiled rejected the operand layout (code " +
+                                           std::to_string(static_cast<int>(r)) + ")");
+  return PHEW_OK;
+}
+
+template <int BN, bool BF16>
+int launch_tc(const void* A, const void* B, const Params& p, long long lda, long long ldb,
+              long long sa, long long sb, cudaStream_t st) {
+  using C = Cfg<BN>;
+  const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap ta, tb;
+  const uint64_t nba = p.a_batched ? p.batch : 1, nbb = p.b_batched ? p.batch : 1;
+  int s = make_map(&ta, A, dt, p.K, p.M, nba, lda * 2, (p.a_batched ? sa : (long long)p.M * lda) * 2, BK, BM);
+  if (s) return s;
+  if (p.b_mn_major)
+    s = make_map(&tb, B, dt, p.N, p.K, nbb, ldb * 2, (p.b_batched ? sb : (long long)p.K * ldb) * 2, 64, BK);
+  else
+    s = make_map(&tb, B, dt, p.K, p.N, nbb, ldb * 2, (p.b_batched ? sb : (long long)p.N * ldb) * 2, BK, BN);
+  if (s) return s;
+  static bool attr_set = false;
+  if (!attr_set) {
+    PHEW_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, BF16>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    attr_set = true;
+  }
+  dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, p.batch);
+  gemm_tc_kernel<BN, BF16><<<grid, kNumThreads, C::SMEM, st>>>(ta, tb, p);
+  return launch_status("gemm_tc_kernel");
+}
+
+}  // namespace gemm
+}  // namespace phew
+
+using namespace phew;
+using namespace phew::gemm;
+
+extern "C" int phew_gemm(const void* A, const void* B, void* Cout, int64_t M, int64_t N, int64_t K,
+                         int64_t batch, int64_t lda, int64_t ldb, int64_t ldc, int64_t stride_a,
+                         int64_t stride_b, int64_t stride_c, int b_layout, int in_dtype,
+                         int out_dtype, int row_scale, float eps, int* error_flag, void* stream) {
+  PHEW_REQUIRE(A && B && Cout, "phew_gemm: null operand");
+  PHEW_REQUIRE(M >= 0 && N >= 0 && K >= 0 && batch >= 1, "phew_gemm: bad shape");
+  PHEW_REQUIRE(in_dtype == PHEW_BF16 || in_dtype == PHEW_F16 || in_dtype == PHEW_F32,
+               "phew_gemm: bad input dtype");
+  PHEW_REQUIRE(out_dtype == PHEW_BF16 || out_dtype == PHEW_F16 || out_dtype == PHEW_F32,
+               "phew_gemm: bad output dtype");
+  PHEW_REQUIRE(b_layout == 0 || b_layout == 1, "phew_gemm: b_layout must be 0 ([K,N]) or 1 ([N,K])");
+  PHEW_REQUIRE(M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31) && batch < 65536,
+               "phew_gemm: extent too large");
+  if (M == 0 || N == 0) return PHEW_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Params p;
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.b_mn_major = b_layout == 0 ? 1 : 0;
+  p.batch = static_cast<int>(batch);
+  p.a_batched = stride_a != 0;
+  p.b_batched = stride_b != 0;
+  p.C = Cout;
+  p.ldc = ldc;
+  p.c_batch_stride = stride_c;
+  p.out_dtype = out_dtype;
+  p.row_scale = row_scale;
+  p.eps = eps;
+  p.error_flag = error_flag;
+  const bool aligned16 =
+      ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) == 0 &&
+      (lda * 2) % 16 == 0 && (ldb * 2) % 16 == 0 && (stride_a * 2) % 16 == 0 &&
+      (stride_b * 2) % 16 == 0 && K > 0;
+  if (aligned16 && in_dtype != PHEW_F32) {
+    const bool bf = in_dtype == PHEW_BF16;
+    if (N <= 128) return bf ? launch_tc<128, true>(A, B, p, lda, ldb, stride_a, stride_b, st)
+                            : launch_tc<128, false>(A, B, p, lda, ldb, stride_a, stride_b, st);
+    return bf ? launch_tc<256, true>(A, B, p, lda, ldb, stride_a, stride_b, st)
+              : launch_tc<256, false>(A, B, p, lda, ldb, stride_a, stride_b, st);
+  }
+  dim3 grid(static_cast<unsigned>((N + 15) / 16), static_cast<unsigned>((M + 15) / 16),
+            static_cast<unsigned>(batch));
+  dim3 block(16, 16);
+  if (in_dtype == PHEW_F32)
+    gemm_simt_kernel<float><<<grid, block, 0, st>>>(static_cast<const float*>(A),
+                                                    static_cast<const float*>(B), p, lda, ldb,
+                                                    stride_a, stride_b);
+  else if (in_dtype == PHEW_BF16)
+    gemm_simt_kernel<bf16><<<grid, block, 0, st>>>(static_cast<const bf16*>(A),
+                                                   static_cast<const bf16*>(B), p, lda, ldb,
+                                                   stride_a, stride_b);
+  else
+    gemm_simt_kernel<f16><<<grid, block, 0, st>>>(static_cast<const f16*>(A),
+                                                  static_cast<const f16*>(B), p, lda, ldb,
+                                                  stride_a, stride_b);
+  return launch_status("gemm_simt_kernel");
+}

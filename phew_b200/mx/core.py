@@ -18,6 +18,7 @@ current stream; no torch compute kernel runs on these paths.
 
 from __future__ import annotations
 
+import builtins
 import ctypes
 import functools
 import math
@@ -81,9 +82,9 @@ def elementwise_threads(numel: int) -> int:
     at two full waves of 2048 threads on every SM; threads loop over the
     rest.
     """
-    want = max(1, -(-numel // 8))
+    want = builtins.max(1, -(-numel // 8))
     cap = sm_count() * 2048 * 2
-    return min(want, cap)
+    return builtins.min(want, cap)
 
 
 # ---------------------------------------------------------------------------

@@ -1,0 +1,115 @@
+"""tcgen05 GEMM parity against a float32 numpy product (the oracle's matmul),
+covering both B layouts, ragged edges, batching, broadcasting and the fused
+normed-matmul row scale."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import mlx_cpu
+
+pytestmark = pytest.mark.gpu
+
+BF16 = mlx_cpu.BF16
+
+
+def _rand(rng, shape, dtype, scale=1.0):
+    return (rng.standard_normal(shape).astype(np.float32) * scale).astype(dtype)
+
+
+def check(got, ref, dtype):
+    g = np.asarray(got).astype(np.float64)
+    r = np.asarray(ref).astype(np.float64)
+    assert g.shape == r.shape, (g.shape, r.shape)
+    scale = np.sqrt(np.mean(r * r)) + 1e-30
+    tol = 1e-5 if dtype == np.float32 else 2e-2
+    np.testing.assert_allclose(g, r, rtol=tol, atol=tol * scale)
+    # error in units of the output scale should be near the rounding level
+    rel = np.abs(g - r).max() / scale
+    assert rel < (1e-5 if dtype == np.float32 else 1.6e-2), rel
+
+
+@pytest.fixture(autouse=True)
+def _no_device_errors(mx):
+    from phew_b200.ops import check_device_errors
+
+    yield
+    mx.synchronize()
+    check_device_errors()
+
+
+@pytest.mark.parametrize("dtype", [BF16, np.float16])
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 512, 4096), (300, 200, 96),
+                                   (1, 256, 128), (129, 257, 200), (64, 1024, 64)])
+def test_gemm_b_row_major(mx, dtype, M, N, K):
+    rng = np.random.default_rng(M * 7 + N)
+    a = _rand(rng, (M, K), dtype)
+    b = _rand(rng, (K, N), dtype, 1 / np.sqrt(K))
+    got = mx.array(a) @ mx.array(b)
+    check(got, mlx_cpu.matmul(mlx_cpu.array(a), mlx_cpu.array(b)), dtype)
+
+
+@pytest.mark.parametrize("dtype", [BF16, np.float16])
+@pytest.mark.parametrize("M,N,K", [(128, 128, 128), (512, 384, 256), (77, 130, 64)])
+def test_gemm_b_transposed_view(mx, dtype, M, N, K):
+    """q @ k.T: B is a transposed view of a [N, K] array (K-major operand)."""
+    rng = np.random.default_rng(N)
+    a = _rand(rng, (M, K), dtype)
+    bt = _rand(rng, (N, K), dtype, 1 / np.sqrt(K))
+    got = mx.array(a) @ mx.array(bt).T
+    check(got, mlx_cpu.matmul(mlx_cpu.array(a), mlx_cpu.array(bt).T), dtype)
+
+
+def test_gemm_batched_attention_shapes(mx):
+    rng = np.random.default_rng(3)
+    B, H, L, D = 2, 3, 256, 128
+    q = _rand(rng, (B, H, L, D), BF16)
+    k = _rand(rng, (B, H, L, D), BF16)
+    v = _rand(rng, (B, H, L, D), BF16)
+    s = mx.array(q) @ mx.array(k).transpose(0, 1, 3, 2)
+    check(s, mlx_cpu.matmul(mlx_cpu.array(q), mlx_cpu.array(k).transpose(0, 1, 3, 2)), BF16)
+    p = _rand(rng, (B, H, L, L), BF16, 0.05)
+    o = mx.array(p) @ mx.array(v)
+    check(o, mlx_cpu.matmul(mlx_cpu.array(p), mlx_cpu.array(v)), BF16)
+
+
+def test_gemm_broadcast_weight(mx):
+    rng = np.random.default_rng(4)
+    x = _rand(rng, (3, 100, 256), BF16)
+    w = _rand(rng, (256, 384), BF16, 1 / 16)
+    got = mx.array(x) @ mx.array(w)
+    check(got, mlx_cpu.matmul(mlx_cpu.array(x), mlx_cpu.array(w)), BF16)
+
+
+def test_gemm_simt_paths(mx):
+    rng = np.random.default_rng(5)
+    a = _rand(rng, (33, 100), np.float32)
+    b = _rand(rng, (100, 17), np.float32)
+    check(mx.array(a) @ mx.array(b), mlx_cpu.matmul(mlx_cpu.array(a), mlx_cpu.array(b)), np.float32)
+    a16 = _rand(rng, (40, 100), BF16)  # 100 * 2 bytes is not a multiple of 16
+    b16 = _rand(rng, (100, 24), BF16, 0.1)
+    check(mx.array(a16) @ mx.array(b16), mlx_cpu.matmul(mlx_cpu.array(a16), mlx_cpu.array(b16)), BF16)
+
+
+def test_gemm_vector_operands(mx):
+    rng = np.random.default_rng(6)
+    a = _rand(rng, (128,), BF16)
+    b = _rand(rng, (128, 64), BF16, 0.1)
+    got = mx.array(a) @ mx.array(b)
+    assert got.shape == (64,)
+    check(got, mlx_cpu.matmul(mlx_cpu.array(a), mlx_cpu.array(b)), BF16)
+
+
+@pytest.mark.parametrize("M,K,N", [(256, 4096, 512), (200, 512, 256)])
+def test_normed_matmul_fused(mx, M, K, N):
+    from phew_b200.ops import normed_matmul
+
+    rng = np.random.default_rng(M)
+    x = _rand(rng, (M, K), BF16)
+    w = _rand(rng, (K, N), BF16, 1 / np.sqrt(K))
+    got = normed_matmul(mx.array(x), mx.array(w), eps=1e-5)
+    xf = x.astype(np.float32)
+    r = 1.0 / np.sqrt(np.mean(xf.astype(np.float64) ** 2, -1, keepdims=True) + 1e-5)
+    ref = (xf @ w.astype(np.float32)) * r
+    check(got, ref.astype(BF16), BF16)

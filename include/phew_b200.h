@@ -159,6 +159,24 @@ int phew_gemm(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
               int64_t stride_b, int64_t stride_c, int b_layout, int in_dtype, int out_dtype,
               int row_scale, float eps, int* error_flag, void* stream);
 
+/* ---- attention --------------------------------------------------------- */
+
+/* 1 when phew_sdpa's tensor-core kernel handles this shape/dtype
+ * (D == 128, L % 128 == 0, bf16/f16). */
+int phew_sdpa_supported(int64_t L, int64_t D, int dtype);
+
+/* o = softmax(q k^T * scale (+ causal mask)) v for batch_heads independent
+ * [L, D] slices stored contiguously ([B*H, L, D], D contiguous).  S = QK^T and
+ * O += PV run on tcgen05 with TMEM accumulators; the softmax (running max with
+ * lazy rescaling, exp2) runs between them on the CUDA cores; scores never
+ * reach HBM.  causal = 1 masks key j > query i.  error_flag as in phew_gemm.
+ * Replaces mx.fast.scaled_dot_product_attention(q, k, v, scale=)
+ * (emit/codegen.py:421-426; FastScaledDotProductAttention ir/ops.py:182-187,
+ * produced by rules/primitive_subst.py:413-499). */
+int phew_sdpa(const void* q, const void* k, const void* v, void* o, int64_t batch_heads,
+              int64_t L, int64_t D, float scale, int causal, int dtype, int* error_flag,
+              void* stream);
+
 /* ---- equivalence comparison -------------------------------------------- */
 
 /* Result of one baseline/candidate comparison, written to DEVICE memory. */

@@ -42,6 +42,8 @@ EXPORTED_SYMBOLS = (
     "phew_copy_strided",
     "phew_l2_flush",
     "phew_gemm",
+    "phew_sdpa_supported",
+    "phew_sdpa",
     "phew_compare_scratch_bytes",
     "phew_compare",
 )
@@ -117,6 +119,11 @@ _SIGNATURES = {
     "phew_l2_flush": ([_vp, ctypes.c_size_t, _vp], _int),
     "phew_gemm": (
         [_vp, _vp, _vp] + [_i64] * 10 + [_int, _int, _int, _int, ctypes.c_float, _vp, _vp],
+        _int,
+    ),
+    "phew_sdpa_supported": ([_i64, _i64, _int], _int),
+    "phew_sdpa": (
+        [_vp, _vp, _vp, _vp, _i64, _i64, _i64, ctypes.c_float, _int, _int, _vp, _vp],
         _int,
     ),
     "phew_compare_scratch_bytes": ([_i64], ctypes.c_size_t),

@@ -25,20 +25,16 @@
 //               the main loop runs, so the norm costs no extra HBM pass
 // Every mbarrier wait is bounded; a wait that runs out sets *error_flag and the
 // kernel winds down instead of spinning.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
-#include <mutex>
-
-#include "common.cuh"
+#include "tc_common.cuh"
 
 namespace phew {
 namespace gemm {
 
+using namespace tc;
+
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 x 16-bit = one 128-byte swizzle row
 constexpr int kNumThreads = 192;
-constexpr uint32_t kSpinLimit = 1u << 26;
 
 template <int BN> struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;
@@ -62,100 +58,6 @@ struct Params {
   float eps;
   int* error_flag;
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Waits for the phase with `parity` to complete; false after kSpinLimit tries.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  return false;
-}
-
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* tm, uint64_t* bar, int c0,
-                                            int c1, int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes "
-      "[%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(tm)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-
-// Shared-memory matrix descriptor for tcgen05 (SWIZZLE_128B, 1024-byte aligned tiles).
-__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((saddr & 0x3FFFF) >> 4);
-  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFF) << 16;
-  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFF) << 32;
-  d |= static_cast<uint64_t>(1) << 46;  // descriptor version for tcgen05
-  d |= static_cast<uint64_t>(2) << 61;  // SWIZZLE_128B
-  return d;
-}
-
-// Instruction descriptor, kind::f16: fp32 accumulator, A/B bf16 or f16,
-// A K-major, B K- or MN-major, M = 128, N = BN.
-__host__ __device__ constexpr uint32_t instr_desc(int bf16, int b_mn_major, int n) {
-  return (1u << 4) | (static_cast<uint32_t>(bf16) << 7) | (static_cast<uint32_t>(bf16) << 10) |
-         (static_cast<uint32_t>(b_mn_major) << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
-         (static_cast<uint32_t>(BM >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                     uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
 
 template <typename T>
 __device__ __forceinline__ void store_row32(T* dst, const float* v, int ncols) {
@@ -202,10 +104,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(tmem_slot)),
-                 "r"(C::TMEM_COLS));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -221,7 +120,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       for (int kb = 0; kb < num_kb && ok; ++kb) {
         const int s = kb % C::STAGES;
         const uint32_t ph = (kb / C::STAGES) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1)) {
+        if (!mbar_wait(&empty[s], ph ^ 1, p.error_flag)) {
           ok = false;
           break;
         }
@@ -241,12 +140,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr uint32_t idesc = instr_desc(BF16 ? 1 : 0, 0, BN);
-      const uint32_t idesc_b = p.b_mn_major ? instr_desc(BF16 ? 1 : 0, 1, BN) : idesc;
+      constexpr uint32_t idesc = instr_desc_f16(BF16 ? 1 : 0, 0, BM, BN);
+      const uint32_t idesc_b = p.b_mn_major ? instr_desc_f16(BF16 ? 1 : 0, 1, BM, BN) : idesc;
       for (int kb = 0; kb < num_kb && ok; ++kb) {
         const int s = kb % C::STAGES;
         const uint32_t ph = (kb / C::STAGES) & 1;
-        if (!mbar_wait(&full[s], ph)) {
+        if (!mbar_wait(&full[s], ph, p.error_flag)) {
           ok = false;
           break;
         }
@@ -258,11 +157,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           const uint64_t ad = smem_desc(sa + kk * 32, 16, 1024);
           const uint64_t bd = p.b_mn_major ? smem_desc(sb + kk * (16 * 128), 64 * BK * 2, 1024)
                                            : smem_desc(sb + kk * 32, 16, 1024);
-          umma(tmem, ad, bd, idesc_b, (kb > 0 || kk > 0) ? 1u : 0u);
+          mma_ss(tmem, ad, bd, idesc_b, (kb > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&empty[s]);
+        commit(&empty[s]);
       }
-      if (ok) umma_commit(accum_full);
+      if (ok) commit(accum_full);
     }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
@@ -273,7 +172,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       for (int kb = 0; kb < num_kb && ok; ++kb) {
         const int s = kb % C::STAGES;
         const uint32_t ph = (kb / C::STAGES) & 1;
-        if (!mbar_wait(&full[s], ph)) {
+        if (!mbar_wait(&full[s], ph, p.error_flag)) {
           ok = false;
           break;
         }
@@ -299,7 +198,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         if (lane == 0) mbar_arrive(&empty[s]);
       }
     }
-    if (ok && !mbar_wait(accum_full, 0)) ok = false;
+    if (ok && !mbar_wait(accum_full, 0, p.error_flag)) ok = false;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (ok) {
       const float scale = p.row_scale ? 1.0f / sqrtf(ss / static_cast<float>(p.K) + p.eps) : 1.0f;
@@ -308,7 +207,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         float v[32];
-        tmem_ld32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + c, v);
+        {
+          uint32_t r[32];
+          tmem_ld32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + c, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        }
         if (row < p.M && n0 + c < p.N) {
           if (p.row_scale) {
 #pragma unroll
@@ -330,8 +235,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(C::TMEM_COLS));
+    tmem_dealloc(tmem, C::TMEM_COLS);
   }
 }
 
@@ -383,49 +287,26 @@ __global__ void gemm_simt_kernel(const T* A, const T* B, Params p, long long lda
 // host side
 // ---------------------------------------------------------------------------
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  });
-  return fn;
-}
-
-int make_map(CUtensorMap* tm, const void* base, CUtensorMapDataType dt, uint64_t d0, uint64_t d1,
-             uint64_t d2, uint64_t s1_bytes, uint64_t s2_bytes, uint32_t b0, uint32_t b1) {
-  auto fn = encode_fn();
-  if (!fn) return set_error(PHEW_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
-  cuuint64_t dims[3] = {d0, d1, d2};
-  cuuint64_t strides[2] = {s1_bytes, s2_bytes};
-  cuuint32_t box[3] = {b0, b1, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(tm, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS)
-    return set_error(PHEW_ERR_INVALID, "cuTensorMapEncodeTiled rejected the operand layout (code " +
-                                           std::to_string(static_cast<int>(r)) + ")");
-  return PHEW_OK;
+int make_map(CUtensorMap* tm, const void* base, bool bf16, uint64_t d0, uint64_t d1, uint64_t d2,
+             uint64_t s1_bytes, uint64_t s2_bytes, uint32_t b0, uint32_t b1) {
+  const uint64_t dims[3] = {d0, d1, d2};
+  const uint64_t strides[2] = {s1_bytes, s2_bytes};
+  const uint32_t box[3] = {b0, b1, 1};
+  return make_map_16bit(tm, base, bf16, 3, dims, strides, box);
 }
 
 template <int BN, bool BF16>
 int launch_tc(const void* A, const void* B, const Params& p, long long lda, long long ldb,
               long long sa, long long sb, cudaStream_t st) {
   using C = Cfg<BN>;
-  const CUtensorMapDataType dt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap ta, tb;
   const uint64_t nba = p.a_batched ? p.batch : 1, nbb = p.b_batched ? p.batch : 1;
-  int s = make_map(&ta, A, dt, p.K, p.M, nba, lda * 2, (p.a_batched ? sa : (long long)p.M * lda) * 2, BK, BM);
+  int s = make_map(&ta, A, BF16, p.K, p.M, nba, lda * 2, (p.a_batched ? sa : (long long)p.M * lda) * 2, BK, BM);
   if (s) return s;
   if (p.b_mn_major)
-    s = make_map(&tb, B, dt, p.N, p.K, nbb, ldb * 2, (p.b_batched ? sb : (long long)p.K * ldb) * 2, 64, BK);
+    s = make_map(&tb, B, BF16, p.N, p.K, nbb, ldb * 2, (p.b_batched ? sb : (long long)p.K * ldb) * 2, 64, BK);
   else
-    s = make_map(&tb, B, dt, p.K, p.N, nbb, ldb * 2, (p.b_batched ? sb : (long long)p.N * ldb) * 2, BK, BN);
+    s = make_map(&tb, B, BF16, p.K, p.N, nbb, ldb * 2, (p.b_batched ? sb : (long long)p.N * ldb) * 2, BK, BN);
   if (s) return s;
   static bool attr_set = false;
   if (!attr_set) {

@@ -12,7 +12,8 @@
 namespace phew {
 namespace {
 
-constexpr int kMaxVPT = 8;  // 16-byte vectors held per thread
+constexpr int kMaxVPT = 8;    // 16-byte vectors held per thread
+constexpr int kMaxTPR = 512;  // threads per row (keeps VPT=8 kernels within the register file)
 
 template <typename T> struct Vec {
   static constexpr int E = 16 / sizeof(T);  // elements per 16-byte vector
@@ -57,7 +58,7 @@ __device__ __forceinline__ float row_allreduce(float v, float* smem) {
 // rms_norm: y = w * T(x * rsqrt(mean(x^2) + eps))
 // ---------------------------------------------------------------------------
 template <typename T, int VPT>
-__global__ void rms_norm_vec_kernel(const T* __restrict__ x, const T* __restrict__ w,
+__global__ void __launch_bounds__(512) rms_norm_vec_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                     T* __restrict__ y, int64_t rows, int64_t cols, float eps) {
   __shared__ float smem[32 * 32];
   constexpr int E = Vec<T>::E;
@@ -127,7 +128,7 @@ __global__ void rms_norm_loop_kernel(const T* __restrict__ x, const T* __restric
 // softmax over the last axis: y = exp(x - max) / sum(exp(x - max))
 // ---------------------------------------------------------------------------
 template <typename T, int VPT>
-__global__ void softmax_vec_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t rows,
+__global__ void __launch_bounds__(512) softmax_vec_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t rows,
                                    int64_t cols) {
   __shared__ float smem[32 * 32];
   constexpr int E = Vec<T>::E;
@@ -269,7 +270,7 @@ struct RowLaunch {
 RowLaunch plan_rows(int64_t nvec) {
   int tpr = static_cast<int>(((nvec + 3) / 4 + 31) / 32 * 32);
   if (tpr < 32) tpr = 32;
-  if (tpr > 1024) tpr = 1024;
+  if (tpr > kMaxTPR) tpr = kMaxTPR;
   int vpt = static_cast<int>((nvec + tpr - 1) / tpr);
   int rpb = tpr >= 128 ? 1 : 128 / tpr;
   return {tpr, rpb, vpt};
@@ -285,7 +286,7 @@ int rms_norm_typed(const void* x, const void* w, void* y, int64_t rows, int64_t 
   const T* xp = static_cast<const T*>(x);
   const T* wp = static_cast<const T*>(w);
   T* yp = static_cast<T*>(y);
-  if (aligned && cols % E == 0 && nvec <= 1024LL * kMaxVPT) {
+  if (aligned && cols % E == 0 && nvec <= static_cast<int64_t>(kMaxTPR) * kMaxVPT) {
     RowLaunch L = plan_rows(nvec);
     dim3 block(L.tpr, L.rpb), grid(static_cast<unsigned>((rows + L.rpb - 1) / L.rpb));
     switch (L.vpt) {
@@ -312,7 +313,7 @@ int softmax_typed(const void* x, void* y, int64_t rows, int64_t cols, cudaStream
   const int64_t nvec = cols / E;
   const T* xp = static_cast<const T*>(x);
   T* yp = static_cast<T*>(y);
-  if (aligned && cols % E == 0 && nvec <= 1024LL * kMaxVPT) {
+  if (aligned && cols % E == 0 && nvec <= static_cast<int64_t>(kMaxTPR) * kMaxVPT) {
     RowLaunch L = plan_rows(nvec);
     dim3 block(L.tpr, L.rpb), grid(static_cast<unsigned>((rows + L.rpb - 1) / L.rpb));
     switch (L.vpt) {

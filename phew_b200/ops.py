@@ -159,5 +159,64 @@ def normed_matmul(x, w, eps: float = 1e-5) -> array:
     return matmul(x, w, row_scale=True, eps=eps)
 
 
+_mask_cache: dict[tuple, array] = {}
+
+
+def causal_mask(L: int, S: int, dtype) -> array:
+    """Additive causal mask (0 on and below the diagonal, -inf above),
+    aligned bottom-right when S > L, cached per shape and dtype."""
+    import numpy as np
+
+    from .mx.core import array as _array
+
+    key = (L, S, dtype.name)
+    m = _mask_cache.get(key)
+    if m is None:
+        host = np.zeros((L, S), np.float32)
+        host[np.triu_indices(L, S - L + 1, S)] = -np.inf
+        m = _array(host, dtype)
+        _mask_cache[key] = m
+    return m
+
+
 def scaled_dot_product_attention(q, k, v, *, scale=1.0, mask=None) -> array:
-    raise NotImplementedError("scaled_dot_product_attention: the tcgen05 kernel is not built yet")
+    """``mx.fast.scaled_dot_product_attention(q, k, v, scale=, mask=)``.
+
+    q, k, v: [B, H, L, D].  ``mask`` None (no mask), ``"causal"`` or an
+    additive array broadcastable to [B, H, L, S].  The fused tcgen05 kernel
+    runs for D = 128, L = S multiple of 128, bf16/fp16, equal head counts and
+    mask None / "causal"; any other case is composed from this backend's GEMM
+    and softmax kernels (scores materialised in HBM).
+    """
+    from .mx.core import astype, softmax, swapaxes
+
+    q = asarray_device(q)
+    k = asarray_device(k)
+    v = asarray_device(v)
+    causal = isinstance(mask, str) and mask == "causal"
+    if isinstance(mask, str) and not causal:
+        raise ValueError(f"unknown mask mode {mask!r}")
+    fast_ok = (
+        q.ndim == 4 and q.shape == k.shape == v.shape and q.dtype is k.dtype is v.dtype
+        and q.dtype.name in ("bfloat16", "float16") and q.shape[-1] == 128
+        and q.shape[-2] % 128 == 0 and (mask is None or causal)
+    )
+    if fast_ok:
+        B, H, L, D = q.shape
+        out = empty(q.shape, q.dtype)
+        _native.call(
+            "phew_sdpa",
+            ctypes.c_void_p(q._t.data_ptr()), ctypes.c_void_p(k._t.data_ptr()),
+            ctypes.c_void_p(v._t.data_ptr()), ctypes.c_void_p(out._t.data_ptr()),
+            B * H, L, D, ctypes.c_float(scale), 1 if causal else 0, q.dtype.code,
+            ctypes.c_void_p(error_flag().data_ptr()), _stream(),
+        )
+        return out
+    s = matmul(q, swapaxes(k, -1, -2)) * float(scale)
+    if causal:
+        s = s + causal_mask(q.shape[-2], k.shape[-2], s.dtype)
+    elif mask is not None:
+        mk = mask if isinstance(mask, array) else array(mask)
+        s = s + (mk if mk.dtype is s.dtype else astype(mk, s.dtype))
+    p = softmax(s, axis=-1)
+    return matmul(p, v)

@@ -111,5 +111,10 @@ def test_normed_matmul_fused(mx, M, K, N):
     got = normed_matmul(mx.array(x), mx.array(w), eps=1e-5)
     xf = x.astype(np.float32)
     r = 1.0 / np.sqrt(np.mean(xf.astype(np.float64) ** 2, -1, keepdims=True) + 1e-5)
-    ref = (xf @ w.astype(np.float32)) * r
+    mm = xf @ w.astype(np.float32)
+    ref = mm * r
+    g = np.asarray(got).astype(np.float64)
+    implied = np.sum(g * mm, -1) / np.sum(mm * mm, -1)
+    bad = np.nonzero(np.abs(implied / r[:, 0] - 1) > 5e-3)[0]
+    assert len(bad) == 0, f"rows with a wrong scale: {bad[:20]} ratios {(implied / r[:, 0])[bad[:8]]}"
     check(got, ref.astype(BF16), BF16)

@@ -1,23 +1,28 @@
 """Benchmark of phew's candidate-evaluation path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl phew|reference]
-                    [--workload gelu_chain]
+                    [--workload gelu_chain|attention|normed_matmul|rms_norm]
 
-Default workload: the fused elementwise chain z = tanh-GELU(x*a + b) *
-sigmoid(c) + x on fp16 (4096, 8192) -- the fuse->=3-ops path, HBM-bound.
-A step is one launch of the fused kernel over one batch of inputs.
+Default workload (gelu_chain): the fused elementwise chain
+z = tanh-GELU(x*a + b) * sigmoid(c) + x on fp16 (4096, 8192) -- the
+fuse->=3-ops path, HBM-bound.  A step is one launch of the fused kernel over
+one batch of inputs.  The other workloads time one launch of the attention
+kernel (bf16 (4, 32, 2048, 128), causal), the normed matmul
+(x bf16 (8192, 4096) @ W (4096, 4096), fused row norm) and rms_norm
+(fp32 (4096, 2048)).
 
 Printed (one JSON line, rank 0):
-  value       fused-kernel HBM GB/s over all ranks (algorithmic bytes / time),
-              inputs resident in HBM, three rotating input sets (each set is
-              201 MB, so no step finds its inputs in the 126 MB L2)
-  e2e         the same metric through the public kernel API with pinned host
-              buffers: H2D of x, a, b, c and D2H of z inside every step
-  roofline    achieved vs the measured HBM copy bandwidth
+  value       the workload's throughput over all ranks (HBM GB/s for the
+              memory-bound kernels, TFLOP/s for the tensor-core ones) with
+              inputs resident in HBM and rotated so no step finds its inputs in
+              the 126 MB L2
+  e2e         the same metric through the public API with pinned host
+              buffers: H2D of the inputs and D2H of the output inside every step
+  roofline    achieved vs the measured HBM copy bandwidth / cuBLAS bf16 peak
   cpu_baseline  the oracle (numpy restatement of the MLX-CPU evaluation)
-              timed on a bounded sample of rows on the host
-  optimized_ms / baseline_ms   fused kernel vs the unfused op-by-op
-              evaluation of the same harness function on this backend
+              timed on a bounded sample on the host
+  optimized_ms / baseline_ms   (gelu_chain) fused kernel vs the unfused
+              op-by-op evaluation of the same harness function on this backend
 
 ``--impl reference`` times the reference's path on the host CPU (the oracle
 port: MLX, the reference's runtime, is not installable here), using all
@@ -34,6 +39,7 @@ import argparse
 import concurrent.futures as cf
 import ctypes
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -45,9 +51,6 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-METRIC = "fused_kernel_hbm_gbs"
-ROWS, COLS = 4096, 8192
-
 
 def parse_args(argv=None):
     ap = argparse.ArgumentParser()
@@ -55,8 +58,8 @@ def parse_args(argv=None):
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["phew", "reference"], default="phew")
-    ap.add_argument("--workload", default="gelu_chain", choices=["gelu_chain"])
-    ap.add_argument("--cpu-rows", type=int, default=512, help="rows per CPU-baseline sample")
+    ap.add_argument("--workload", default="gelu_chain",
+                    choices=["gelu_chain", "attention", "normed_matmul", "rms_norm"])
     return ap.parse_args(argv)
 
 
@@ -64,12 +67,13 @@ def load_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
-def load_traffic() -> float | None:
-    p = ROOT / "profiles" / "gelu_chain_fp16_4096x8192.json"
+def load_traffic(name: str) -> float | None:
+    p = ROOT / "profiles" / f"{name}.json"
     if p.exists():
         return json.loads(p.read_text()).get("dram_bytes_per_launch")
     return None
@@ -81,13 +85,14 @@ def load_traffic() -> float | None:
 
 
 class Dist:
-    def __init__(self, n: int) -> None:
+    def __init__(self) -> None:
         import torch
 
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
         self.torch = torch
+        self.dist = None
         if self.world > 1:
             import datetime
 
@@ -97,10 +102,8 @@ class Dist:
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                     device_id=torch.device("cuda", self.local))
             self.dist = dist
-        else:
-            self.dist = None
-            if torch.cuda.is_available():
-                torch.cuda.set_device(0)
+        elif torch.cuda.is_available():
+            torch.cuda.set_device(0)
 
     def barrier(self):
         if self.dist:
@@ -119,7 +122,7 @@ class Dist:
 
 
 # ---------------------------------------------------------------------------
-# clocks
+# clocks during the timed region
 # ---------------------------------------------------------------------------
 
 
@@ -129,9 +132,7 @@ class ClockSampler:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index: int) -> None:
-        self.index = index
-        self.proc = None
-        self.path = None
+        self.index, self.proc, self.path = index, None, None
 
     def __enter__(self):
         fd, self.path = tempfile.mkstemp(suffix=".csv")
@@ -148,6 +149,7 @@ class ClockSampler:
 
     def __exit__(self, *exc):
         if self.proc is not None:
+            time.sleep(0.25)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -183,172 +185,343 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
-# CPU baselines (oracle port)
+# workloads
 # ---------------------------------------------------------------------------
 
 
-def cpu_chain_sample(rows: int, threads: int) -> dict:
-    """Time the oracle's evaluation of the chain on `rows` rows (bounded)."""
-    import numpy as np
+class GeluChain:
+    """Fused elementwise chain, fp16 (4096, 8192): HBM-bound."""
 
-    from oracle import mlx_cpu
-    from phew_b200.workloads import gelu_chain_bytes, gelu_chain_inputs, gelu_chain_nodes
+    name = "gelu_chain"
+    metric, unit, bound, dtype = "fused_kernel_hbm_gbs", "GB/s", "hbm", "f16"
+    ROWS, COLS = 4096, 8192
+    kernel_regex = "gelu_chain_fused"
 
-    xs = gelu_chain_inputs("typical", 0, rows=rows)
-    blocks = max(1, threads)
-    per = -(-rows // blocks)
-    parts = []
-    for b in range(blocks):
-        lo, hi = b * per, min(rows, (b + 1) * per)
-        if lo >= hi:
-            continue
-        chain, ins, outs = gelu_chain_nodes(hi - lo)
-        parts.append((chain, ins, outs, [xs[0][lo:hi], xs[1], xs[2], xs[3][lo:hi]]))
+    def describe(self):
+        return (f"gelu_chain: z = tanh-GELU(x*a+b)*sigmoid(c)+x, fp16 ({self.ROWS},{self.COLS}), "
+                "one fused NVRTC kernel per step")
 
-    def run(p):
-        return mlx_cpu.eval_chain(*p)[0]
+    def work_per_step(self):
+        from phew_b200.workloads import gelu_chain_bytes
 
-    with cf.ThreadPoolExecutor(max_workers=blocks) as ex:
-        list(ex.map(run, parts))  # warm
+        return gelu_chain_bytes(self.ROWS, self.COLS)
+
+    def host_inputs(self, seed):
+        from phew_b200.workloads import gelu_chain_inputs
+
+        return gelu_chain_inputs("typical", seed)
+
+    def setup(self, mx, host):
+        import torch
+
+        from phew_b200 import _native
+        from phew_b200.emit.cuda_codegen import SubgraphCUDACodegen
+        from phew_b200.workloads import gelu_chain_nodes
+
+        base = [mx.array(h) for h in host]
+        self.sets = [base] + [[mx.array(a._t.clone()) for a in base] for _ in range(2)]
+        chain, ins, outs = gelu_chain_nodes(self.ROWS, self.COLS)
+        src, in_names, out_names = SubgraphCUDACodegen().emit(chain, ins, outs)
+        self.kern = mx.fast.cuda_kernel("gelu_chain_fused", in_names, out_names, src)
+        self.threads = mx.elementwise_threads(self.ROWS * self.COLS)
+        self.outs = [mx.core.empty((self.ROWS, self.COLS), mx.float16) for _ in range(3)]
+        self.api(self.sets[0])
+        self.handle = next(iter(self.kern._handles.values()))
+        self.argvs, self.keep = [], []
+        for s, o in zip(self.sets, self.outs):
+            vals = [ctypes.c_void_p(a._t.data_ptr()) for a in s + [o]]
+            vals += [ctypes.c_uint64(a.size) for a in s + [o]]
+            self.keep.append(vals)
+            self.argvs.append((ctypes.c_void_p * len(vals))(
+                *[ctypes.cast(ctypes.byref(v), ctypes.c_void_p) for v in vals]))
+        self.lib = _native.load()
+        self.blocks = -(-self.threads // 256)
+        self.st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        self._native = _native
+
+    def api(self, inputs):
+        from phew_b200 import mx
+
+        return self.kern(inputs=inputs, output_shapes=[(self.ROWS, self.COLS)],
+                         output_dtypes=[mx.float16], grid=(self.threads, 1, 1),
+                         threadgroup=(256, 1, 1))[0]
+
+    def launch(self, i):
+        rc = self.lib.phew_launch(ctypes.c_uint64(self.handle), self.argvs[i % 3], len(self.keep[0]),
+                                  self.blocks, 1, 1, 256, 1, 1, 0, self.st)
+        if rc:
+            self._native.check(rc, "phew_launch")
+
+    def extras(self, mx):
+        from phew_b200.bench import benchmark
+        from phew_b200.workloads import gelu_chain_fn
+
+        opt = benchmark(lambda *a: self.api(list(a)), *self.sets[0], n_warmup=3, n_bench=10,
+                        max_n_bench=30)
+        basel = benchmark(gelu_chain_fn(mx), *self.sets[0], n_warmup=2, n_bench=5, max_n_bench=15)
+        return {"optimized_ms": opt.mean_ms, "baseline_ms": basel.mean_ms,
+                "optimized_over_baseline": opt.mean_ms / basel.mean_ms}
+
+    def cpu_sample(self, threads: int, rows: int = 512):
+        from oracle import mlx_cpu
+        from phew_b200.workloads import gelu_chain_bytes, gelu_chain_inputs, gelu_chain_nodes
+
+        xs = gelu_chain_inputs("typical", 0, rows=rows)
+        per = -(-rows // threads)
+        parts = []
+        for b in range(threads):
+            lo, hi = b * per, min(rows, (b + 1) * per)
+            if lo < hi:
+                c, i, o = gelu_chain_nodes(hi - lo)
+                parts.append((c, i, o, [xs[0][lo:hi], xs[1], xs[2], xs[3][lo:hi]]))
+        with cf.ThreadPoolExecutor(max_workers=threads) as ex:
+            list(ex.map(lambda p: mlx_cpu.eval_chain(*p), parts))
+            t0 = time.perf_counter()
+            list(ex.map(lambda p: mlx_cpu.eval_chain(*p), parts))
+            dt = time.perf_counter() - t0
+        return gelu_chain_bytes(rows) / dt / 1e9, dt, f"{rows} of {self.ROWS} rows"
+
+
+class Attention:
+    """Fused causal attention, bf16 (4, 32, 2048, 128): tensor-core bound."""
+
+    name = "attention"
+    metric, unit, bound, dtype = "sdpa_tflops", "TFLOP/s", "tensor", "bf16"
+    B, H, L, D = 4, 32, 2048, 128
+    kernel_regex = "sdpa_fwd"
+    scale = 1.0 / math.sqrt(128)
+
+    def describe(self):
+        return (f"causal SDPA softmax(q k^T / sqrt(128)) v, bf16 ({self.B},{self.H},{self.L},{self.D}), "
+                "one tcgen05 kernel per step")
+
+    def work_per_step(self):
+        from phew_b200.workloads import attention_flops
+
+        return attention_flops(self.B, self.H, self.L, self.D, causal=True)
+
+    def host_inputs(self, seed):
+        from phew_b200.workloads import attention_inputs
+
+        return attention_inputs("typical", seed)[:3]
+
+    def setup(self, mx, host):
+        base = [mx.array(h) for h in host]
+        self.sets = [base, [mx.array(a._t.clone()) for a in base]]
+        self.api(self.sets[0])
+
+    def api(self, inputs):
+        from phew_b200 import mx
+
+        return mx.fast.scaled_dot_product_attention(*inputs, scale=self.scale, mask="causal")
+
+    def launch(self, i):
+        self.api(self.sets[i % 2])
+
+    def extras(self, mx):
+        return {}
+
+    def cpu_sample(self, threads: int):
+        import numpy as np
+
+        from oracle import mlx_cpu
+
+        q, k, v = [h[:1, :threads] for h in self.host_inputs(0)]
+        mlx_cpu.sdpa(*[mlx_cpu.array(x[:, :1]) for x in (q, k, v)], self.scale, "causal")
         t0 = time.perf_counter()
-        outs = list(ex.map(run, parts))
+        with cf.ThreadPoolExecutor(max_workers=threads) as ex:
+            list(ex.map(lambda h: mlx_cpu.sdpa(*[mlx_cpu.array(x[:, h:h + 1]) for x in (q, k, v)],
+                                               self.scale, "causal"), range(q.shape[1])))
         dt = time.perf_counter() - t0
-    assert sum(o.shape[0] for o in outs) == rows
-    _ = np
-    return {"seconds": dt, "bytes": gelu_chain_bytes(rows), "gbs": gelu_chain_bytes(rows) / dt / 1e9}
+        flops = 2 * q.shape[1] * self.L * self.L * self.D
+        _ = np
+        return flops / dt / 1e12, dt, f"{q.shape[1]} of {self.B * self.H} heads"
+
+
+class NormedMatmul:
+    """(x @ W) * rsqrt(mean(x^2) + eps), bf16 8192 x 4096 x 4096: tensor-core bound."""
+
+    name = "normed_matmul"
+    metric, unit, bound, dtype = "normed_matmul_tflops", "TFLOP/s", "tensor", "bf16"
+    M, K, N = 8192, 4096, 4096
+    kernel_regex = "gemm_tc"
+
+    def describe(self):
+        return (f"normed matmul (x @ W) * rsqrt(mean(x*x,-1)+1e-5), bf16 x ({self.M},{self.K}), "
+                f"W ({self.K},{self.N}); one tcgen05 GEMM with the row norm fused")
+
+    def work_per_step(self):
+        return 2 * self.M * self.N * self.K
+
+    def host_inputs(self, seed):
+        from phew_b200.workloads import normed_matmul_inputs
+
+        return normed_matmul_inputs("typical", seed)
+
+    def setup(self, mx, host):
+        base = [mx.array(h) for h in host]
+        self.sets = [base] + [[mx.array(a._t.clone()) for a in base] for _ in range(2)]
+        self.api(self.sets[0])
+
+    def api(self, inputs):
+        from phew_b200.ops import normed_matmul
+
+        return normed_matmul(*inputs, eps=1e-5)
+
+    def launch(self, i):
+        self.api(self.sets[i % 3])
+
+    def extras(self, mx):
+        return {}
+
+    def cpu_sample(self, threads: int, rows: int = 1024):
+        import numpy as np
+
+        x, w = self.host_inputs(0)
+        xs = x[:rows].astype(np.float32)
+        wf = w.astype(np.float32)
+        t0 = time.perf_counter()
+        r = 1.0 / np.sqrt(np.mean(xs.astype(np.float64) ** 2, -1, keepdims=True) + 1e-5)
+        _ = (xs @ wf) * r
+        dt = time.perf_counter() - t0
+        return 2 * rows * self.N * self.K / dt / 1e12, dt, f"{rows} of {self.M} rows (BLAS fp32)"
+
+
+class RmsNorm:
+    """rms_norm fp32 (4096, 2048): HBM-bound (inputs rotated past the L2)."""
+
+    name = "rms_norm"
+    metric, unit, bound, dtype = "rms_norm_hbm_gbs", "GB/s", "hbm", "f32"
+    N, C = 4096, 2048
+    kernel_regex = "rms_norm"
+    R = 8
+
+    def describe(self):
+        return f"mx.fast.rms_norm fp32 ({self.N},{self.C}), one kernel per step"
+
+    def work_per_step(self):
+        return 2 * self.N * self.C * 4 + self.C * 4
+
+    def host_inputs(self, seed):
+        from phew_b200.workloads import rms_norm_inputs
+
+        return rms_norm_inputs("large", seed)
+
+    def setup(self, mx, host):
+        base = [mx.array(h) for h in host]
+        self.sets = [base] + [[mx.array(base[0]._t.clone()), base[1]] for _ in range(self.R - 1)]
+        self.api(self.sets[0])
+
+    def api(self, inputs):
+        from phew_b200 import mx
+
+        return mx.fast.rms_norm(inputs[0], inputs[1], eps=1e-5)
+
+    def launch(self, i):
+        self.api(self.sets[i % self.R])
+
+    def extras(self, mx):
+        return {}
+
+    def cpu_sample(self, threads: int):
+        from oracle import mlx_cpu
+
+        x, w = self.host_inputs(0)
+        t0 = time.perf_counter()
+        mlx_cpu.rms_norm(mlx_cpu.array(x), mlx_cpu.array(w), 1e-5)
+        dt = time.perf_counter() - t0
+        return self.work_per_step() / dt / 1e9, dt, f"full ({self.N},{self.C})"
+
+
+WORKLOADS = {c.name: c for c in (GeluChain, Attention, NormedMatmul, RmsNorm)}
+
+
+# ---------------------------------------------------------------------------
+# arms
+# ---------------------------------------------------------------------------
 
 
 def run_reference(args) -> None:
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+    if int(os.environ.get("RANK", "0")) != 0:
         return
+    w = WORKLOADS[args.workload]()
     threads = os.cpu_count() or 1
-    rows = args.cpu_rows
     for _ in range(max(1, args.warmup)):
-        cpu_chain_sample(rows, threads)
-    times, nbytes = [], 0
+        w.cpu_sample(threads)
+    vals, secs = [], []
+    sample = ""
     for _ in range(args.steps):
-        r = cpu_chain_sample(rows, threads)
-        times.append(r["seconds"])
-        nbytes = r["bytes"]
-    total = sum(times)
-    val = nbytes * len(times) / total / 1e9
+        v, dt, sample = w.cpu_sample(threads)
+        vals.append(v)
+        secs.append(dt)
+    val = statistics.mean(vals)
     line = {
-        "impl": "reference",
-        "metric": METRIC,
-        "value": val,
-        "unit": "GB/s",
-        "n_gpus": args.gpus,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": total / len(times) * 1e3,
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "f16",
-        "data": "synthetic (np.random.default_rng(0): x, c ~ N(0,1), a, b ~ U(-1,1))",
-        "config": {"workload": f"gelu_chain fp16 ({ROWS},{COLS}); CPU sample {rows} rows per step"},
-        "cpu_baseline": {"value": val, "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"{rows} of {ROWS} rows per step, numpy restatement "
-                                   "(fp32 compute, fp16 rounding per node), row blocks on "
-                                   f"{threads} threads"},
-        "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "impl": "reference", "metric": w.metric, "value": val, "unit": w.unit,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": statistics.mean(secs) * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": w.dtype,
+        "data": "synthetic (np.random.default_rng(0))",
+        "config": {"workload": w.describe() + f"; CPU sample {sample} per step"},
+        "cpu_baseline": {"value": val, "unit": w.unit, "cores": threads, "kind": "port",
+                         "sample": f"{sample} per step, numpy restatement of the MLX-CPU "
+                                   f"evaluation on {threads} threads"},
+        "e2e": {"value": val, "unit": w.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "MLX (the reference's runtime) is not installable here; the oracle port is timed",
     }
     print(json.dumps(line), flush=True)
-
-
-# ---------------------------------------------------------------------------
-# GPU arm
-# ---------------------------------------------------------------------------
 
 
 def run_phew(args) -> None:
     import numpy as np
     import torch
 
-    from phew_b200 import _native, mx
-    from phew_b200.bench import benchmark
-    from phew_b200.emit.cuda_codegen import SubgraphCUDACodegen
-    from phew_b200.workloads import (
-        gelu_chain_bytes,
-        gelu_chain_fn,
-        gelu_chain_inputs,
-        gelu_chain_nodes,
-    )
+    from phew_b200 import mx
+    from phew_b200.ops import check_device_errors
 
-    d = Dist(args.gpus)
+    d = Dist()
     dev = mx.core.device()
     stream = torch.cuda.current_stream()
-    nbytes = gelu_chain_bytes(ROWS, COLS)
-
-    host = gelu_chain_inputs("typical", d.rank)
-    base = [mx.array(h) for h in host]
-    R = 3
-    sets = [base] + [[mx.array(a._t.clone()) for a in base] for _ in range(R - 1)]
-    chain, ins, outs = gelu_chain_nodes(ROWS, COLS)
-    src, in_names, out_names = SubgraphCUDACodegen().emit(chain, ins, outs)
-    kern = mx.fast.cuda_kernel("gelu_chain_fused", in_names, out_names, src)
-    threads = mx.elementwise_threads(ROWS * COLS)
-    outs_dev = [mx.core.empty((ROWS, COLS), mx.float16) for _ in range(R)]
-
-    # Pre-resolved launches (the kernel API call minus allocation), so the
-    # timed loop measures the device, not Python.
-    kern(inputs=sets[0], output_shapes=[(ROWS, COLS)], output_dtypes=[mx.float16],
-         grid=(threads, 1, 1), threadgroup=(256, 1, 1))
-    handle = next(iter(kern._handles.values()))
-    argvs = []
-    keep = []
-    for s, o in zip(sets, outs_dev):
-        vals = [ctypes.c_void_p(a._t.data_ptr()) for a in s + [o]]
-        vals += [ctypes.c_uint64(a.size) for a in s + [o]]
-        keep.append(vals)
-        argvs.append((ctypes.c_void_p * len(vals))(*[ctypes.cast(ctypes.byref(v), ctypes.c_void_p) for v in vals]))
-    lib = _native.load()
-    blocks = -(-threads // 256)
-    st = ctypes.c_void_p(stream.cuda_stream)
-
-    def launch(i):
-        rc = lib.phew_launch(ctypes.c_uint64(handle), argvs[i % R], len(keep[0]), blocks, 1, 1,
-                             256, 1, 1, 0, st)
-        if rc:
-            _native.check(rc, "phew_launch")
+    w = WORKLOADS[args.workload]()
+    work = w.work_per_step()
+    scale = 1e9 if w.unit == "GB/s" else 1e12
+    host = w.host_inputs(d.rank)
+    w.setup(mx, host)
 
     for i in range(args.warmup):
-        launch(i)
+        w.launch(i)
     torch.cuda.synchronize()
-
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(torch.cuda.current_device()) as clk:
         d.barrier()
         torch.cuda.synchronize()
         ev0.record(stream)
         for i in range(args.steps):
-            launch(i)
+            w.launch(i)
         ev1.record(stream)
         torch.cuda.synchronize()
         d.barrier()
+    check_device_errors()
     local_ms = ev0.elapsed_time(ev1)
     max_ms = d.max(local_ms)
-    per_launch_ms = local_ms / args.steps
-    value = nbytes * args.steps * d.world / (max_ms / 1e3) / 1e9
-    achieved = nbytes / (per_launch_ms / 1e3) / 1e9
+    value = work * args.steps * d.world / (max_ms / 1e3) / scale
+    achieved = work / (local_ms / args.steps / 1e3) / scale
 
-    # e2e through the public kernel API with pinned host buffers.
-    pinned_in = [torch.from_numpy(np.ascontiguousarray(h)).pin_memory() for h in host]
-    pinned_out = torch.empty((ROWS, COLS), dtype=torch.float16).pin_memory()
-    dev_in = [torch.empty_like(p, device=dev) for p in pinned_in]
+    # e2e through the public API with pinned host buffers
+    pinned_in = [torch.from_numpy(np.ascontiguousarray(h.view(np.int16) if h.dtype.itemsize == 2 and h.dtype.kind == "V" else h)).pin_memory()
+                 for h in host]
+    dev_in = [torch.empty(p.shape, dtype=a._t.dtype, device=dev) for p, a in zip(pinned_in, w.sets[0])]
+    out0 = w.api(w.sets[0])
+    pinned_out = torch.empty(out0._t.shape, dtype=out0._t.dtype).pin_memory()
     h2d = sum(p.numel() * p.element_size() for p in pinned_in)
     d2h = pinned_out.numel() * pinned_out.element_size()
 
     def e2e_step():
         for dst, srcp in zip(dev_in, pinned_in):
-            dst.copy_(srcp, non_blocking=True)
-        z = kern(inputs=[mx.array(t) for t in dev_in], output_shapes=[(ROWS, COLS)],
-                 output_dtypes=[mx.float16], grid=(threads, 1, 1), threadgroup=(256, 1, 1))[0]
+            dst.view(srcp.dtype).copy_(srcp, non_blocking=True)
+        z = w.api([mx.array(t) for t in dev_in])
         pinned_out.copy_(z._t, non_blocking=True)
 
-    for _ in range(args.warmup):
+    for _ in range(2):
         e2e_step()
     torch.cuda.synchronize()
     e2e_steps = max(3, min(args.steps, 20))
@@ -362,61 +535,32 @@ def run_phew(args) -> None:
     torch.cuda.synchronize()
     d.barrier()
     e2e_ms = d.max(e0.elapsed_time(e1))
-    e2e_val = nbytes * e2e_steps * d.world / (e2e_ms / 1e3) / 1e9
-
-    # Fused vs unfused (the phew speedup question), on this backend.
-    fn = gelu_chain_fn(mx)
-    opt = benchmark(lambda *a: kern(inputs=list(a), output_shapes=[(ROWS, COLS)],
-                                    output_dtypes=[mx.float16], grid=(threads, 1, 1),
-                                    threadgroup=(256, 1, 1)), *sets[0], n_warmup=3, n_bench=10,
-                    max_n_bench=30)
-    basel = benchmark(fn, *sets[0], n_warmup=2, n_bench=5, max_n_bench=15)
+    e2e_val = work * e2e_steps * d.world / (e2e_ms / 1e3) / scale
 
     peaks = load_peaks()
+    peak = peaks["hbm_gbs"] if w.bound == "hbm" else peaks["bf16_tflops"]
     line = {
-        "metric": METRIC,
-        "value": value,
-        "unit": "GB/s",
-        "n_gpus": d.world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": max_ms / args.steps,
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "f16",
-        "data": "synthetic (np.random.default_rng(rank): x, c ~ N(0,1), a, b ~ U(-1,1))",
-        "config": {
-            "workload": f"gelu_chain: z = tanh-GELU(x*a+b)*sigmoid(c)+x, fp16 ({ROWS},{COLS}), "
-                        "one fused NVRTC kernel per step",
-            "bytes_per_step": nbytes,
-            "l2": "inputs larger than L2, 3 rotating input sets",
-            "parallelism": f"replicas x{d.world}",
-        },
-        "roofline": {
-            "bound": "hbm",
-            "achieved": achieved,
-            "peak": peaks["hbm_gbs"],
-            "unit": "GB/s",
-            "frac": achieved / peaks["hbm_gbs"],
-            "traffic": load_traffic(),
-            "peak_source": peaks["source"],
-        },
-        "e2e": {"value": e2e_val, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+        "metric": w.metric, "value": value, "unit": w.unit, "n_gpus": d.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": max_ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": w.dtype,
+        "data": "synthetic (np.random.default_rng(rank))",
+        "config": {"workload": w.describe(), "work_per_step": work,
+                   "l2": "inputs larger than L2 or rotated across sets larger than L2",
+                   "parallelism": f"replicas x{d.world}"},
+        "roofline": {"bound": w.bound, "achieved": achieved, "peak": peak, "unit": w.unit,
+                     "frac": achieved / peak, "traffic": load_traffic(f"{w.name}_traffic"),
+                     "peak_source": peaks["source"] + (" (burst)" if w.bound == "tensor" else "")},
+        "e2e": {"value": e2e_val, "unit": w.unit, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps},
         "gpu_launches": args.steps,
-        "optimized_ms": opt.mean_ms,
-        "baseline_ms": basel.mean_ms,
-        "optimized_over_baseline": opt.mean_ms / basel.mean_ms,
         "clocks": clk.summary(),
     }
+    line.update(w.extras(mx))
     if d.rank == 0 and d.world == 1:
-        cpu = cpu_chain_sample(args.cpu_rows, 1)
-        line["cpu_baseline"] = {
-            "value": cpu["gbs"], "unit": "GB/s", "cores": 1, "kind": "port",
-            "sample": f"{args.cpu_rows} of {ROWS} rows, numpy restatement of the MLX-CPU "
-                      "evaluation (fp32 compute, fp16 rounding per node), single thread",
-        }
+        v, dt, sample = w.cpu_sample(1)
+        line["cpu_baseline"] = {"value": v, "unit": w.unit, "cores": 1, "kind": "port",
+                                "sample": f"{sample}, numpy restatement of the MLX-CPU "
+                                          f"evaluation, single thread ({dt * 1e3:.0f} ms)"}
     if d.rank == 0:
         print(json.dumps(line), flush=True)
     d.close()

@@ -148,6 +148,8 @@ int phew_l2_flush(void* buf, size_t bytes, void* stream);
  *   row_scale = 1 multiplies row m of the product by
  *   rsqrt(mean_k(A[m, k]^2) + eps), computed inside the kernel from the A tiles
  *   it already loads (the normed matmul (x @ W) * rsqrt(mean(x^2) + eps)).
+ *   row_scale = 2 writes each row's sum of squares of A instead of the
+ *   product (a diagnostic of the fused norm).
  *   error_flag (device int, may be NULL) receives PHEW_ERR_TIMEOUT if a
  *   bounded pipeline wait ran out.
  * in_dtype bf16/f16 use the tensor cores when every row stride and base is

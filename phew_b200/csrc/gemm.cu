@@ -194,6 +194,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             ss = fmaf(x, x, ss);
           }
         }
+        // The next TMA write into this stage must be ordered after these
+        // generic-proxy reads.
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
       }
@@ -215,9 +218,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
         }
         if (row < p.M && n0 + c < p.N) {
-          if (p.row_scale) {
+          if (p.row_scale == 1) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] *= scale;
+          } else if (p.row_scale == 2) {  // diagnostic: the row's sum of squares
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = ss;
           }
           const int ncols = p.N - (n0 + c);
           if (p.out_dtype == PHEW_BF16)

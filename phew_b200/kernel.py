@@ -143,14 +143,13 @@ __device__ __forceinline__ float phew_rcp(float x) {
 __device__ __forceinline__ float phew_exp16(float x) { return phew_ex2(x * 1.4426950408889634f); }
 // sigmoid(x) = 1 / (1 + e^-x)
 __device__ __forceinline__ float phew_sigmoid16(float x) { return phew_rcp(1.0f + phew_exp16(-x)); }
-// tanh(x) = sign(x) (1 - 2 / (e^{2|x|} + 1)); below |x| = 1/16, where that
-// difference cancels, the odd Taylor series x - x^3/3 + 2x^5/15.
+// tanh(x) = sign(x) (1 - 2 / (e^{2|x|} + 1)).  The subtraction loses bits as
+// |x| shrinks (about 2^-14.5 relative at |x| = 2^-8); below 2^-8,
+// tanh(x) = x to within x^3/3 < 2^-16 |x|, so x itself is returned.
 __device__ __forceinline__ float phew_tanh16(float x) {
   const float ax = fabsf(x);
   const float big = 1.0f - 2.0f * phew_rcp(phew_ex2(ax * 2.8853900817779268f) + 1.0f);
-  const float x2 = x * x;
-  const float small = x + x * x2 * (-0.33333333333f + x2 * 0.13333333333f);
-  return ax < 0.0625f ? small : copysignf(big, x);
+  return ax < 0.00390625f ? x : copysignf(big, x);
 }
 
 // numpy semantics for the ops below (NaN-propagating max/min, Python-style

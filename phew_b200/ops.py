@@ -144,7 +144,7 @@ def matmul(a, b, *, row_scale: bool = False, eps: float = 1e-5) -> array:
             ctypes.c_void_p(ta.data_ptr()), ctypes.c_void_p(tb.data_ptr()),
             ctypes.c_void_p(out._t.data_ptr()),
             M, N, K, nbatch, lda, ldb, N, sa, sb, M * N if nbatch > 1 else 0,
-            layout, res.code, res.code, 1 if row_scale else 0, ctypes.c_float(eps),
+            layout, res.code, res.code, int(row_scale), ctypes.c_float(eps),
             ctypes.c_void_p(error_flag().data_ptr()), _stream(),
         )
     if squeeze_a:

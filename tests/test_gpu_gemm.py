@@ -101,6 +101,21 @@ def test_gemm_vector_operands(mx):
     check(got, mlx_cpu.matmul(mlx_cpu.array(a), mlx_cpu.array(b)), BF16)
 
 
+@pytest.mark.parametrize("M,K,N", [(256, 4096, 512), (200, 512, 256), (128, 256, 128)])
+def test_fused_row_sum_of_squares(mx, M, K, N):
+    """The in-kernel sum of squares of each A row (row_scale mode 2)."""
+    from phew_b200.ops import matmul
+
+    rng = np.random.default_rng(M + K)
+    x = _rand(rng, (M, K), BF16)
+    w = _rand(rng, (K, N), BF16, 1 / np.sqrt(K))
+    got = np.asarray(matmul(mx.array(x), mx.array(w), row_scale=2)).astype(np.float64)
+    ss = np.sum(x.astype(np.float64) ** 2, -1)
+    rel = np.abs(got[:, 0] / ss - 1)
+    bad = np.nonzero(rel > 1e-2)[0]
+    assert len(bad) == 0, f"rows {bad[:16]}: got {got[bad[:4], 0]} want {ss[bad[:4]]}"
+
+
 @pytest.mark.parametrize("M,K,N", [(256, 4096, 512), (200, 512, 256)])
 def test_normed_matmul_fused(mx, M, K, N):
     from phew_b200.ops import normed_matmul

@@ -578,7 +578,115 @@ def run_phew(args) -> None:
     d.close()
 
 
+# ---------------------------------------------------------------------------
+# verification sweep (decoder block, 16 candidates)
+# ---------------------------------------------------------------------------
+
+SOURCES = ROOT / "tests" / "golden" / "sources"
+
+
+def decoder_specs(dims, seqs):
+    from phew_b200.sweep import ArgSpec
+    from phew_b200.workloads import decoder_arg_shapes, decoder_fan_in
+
+    def specs(size):
+        shapes = decoder_arg_shapes(seqs[size], dims)
+        kinds = ["normal", "ones", "normal", "normal", "normal", "normal", "normal", "causal_mask"]
+        return [ArgSpec(tuple(s), "bfloat16", k, f)
+                for s, k, f in zip(shapes, kinds, decoder_fan_in(dims))]
+
+    return specs
+
+
+def run_sweep(args) -> None:
+    import torch
+
+    from phew_b200 import mx, sweep
+    from phew_b200.ops import check_device_errors
+    from phew_b200.workloads import DECODER_FULL, DECODER_SEQ, DECODER_TINY, DECODER_TINY_SEQ, decoder_block_fn
+
+    d = Dist()
+    mx.core.device()
+    full = not args.tiny
+    dims, seqs = (DECODER_FULL, DECODER_SEQ) if full else (DECODER_TINY, DECODER_TINY_SEQ)
+    tag = "decoder_full" if full else "decoder_tiny"
+    names = sorted(p.stem for p in SOURCES.glob(f"{tag}__*.py"))
+    cands = sweep.load_candidates({n: (SOURCES / f"{n}.py").read_text() for n in names})
+    baseline = decoder_block_fn(mx, dims)
+    seeds = list(range(args.seeds))
+    sizes = ["small", "typical", "large"]
+    variants = sweep.VARIANT_SETS[args.variants]
+    shards = sweep.make_shards(names, seeds)
+    mine = sweep.partition(shards, d.world, d.rank)
+    jdir = Path(args.journal_dir) if args.journal_dir else Path(tempfile.mkdtemp(prefix="sweep_"))
+    if d.dist:  # every rank journals into rank 0's directory
+        obj = [str(jdir)]
+        d.dist.broadcast_object_list(obj, src=0)
+        jdir = Path(obj[0])
+    jdir.mkdir(parents=True, exist_ok=True)
+    journal = jdir / f"journal.rank{d.rank}.jsonl"
+    ev = sweep.DeviceEvaluator(baseline, cands, sweep.DeviceInputs(decoder_specs(dims, seqs)))
+
+    # warm-up: compile every kernel the candidates use on the smallest size
+    for c in names:
+        ev(c, 99, "small", variants[0])
+    ev.release()
+    torch.cuda.synchronize()
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        d.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        e0.record()
+        recs = sweep.run_shards(mine, ev, sizes, variants, journal=journal, rank=d.rank)
+        e1.record()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        d.barrier()
+    check_device_errors()
+    dev_s = e0.elapsed_time(e1) / 1e3
+    max_s = d.max(dev_s)
+    max_wall = d.max(wall)
+    if d.rank == 0:
+        verdicts, missing = sweep.merge(jdir, shards)
+        units = len(shards) * len(sizes) * len(variants)
+        line = {
+            "metric": "verified_candidates_per_s", "value": len(names) / max_s,
+            "unit": "candidates/s", "n_gpus": d.world, "steps": 1, "warmup": 1,
+            "ms_per_step": max_s * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (device counter-based RNG)",
+            "config": {"workload": f"{tag} verification sweep: {len(names)} candidates x {len(seeds)} "
+                                   f"seeds x sizes {[seqs[s] for s in sizes]} x variants {list(variants)}",
+                       "dims": vars(dims) if hasattr(dims, "__dict__") else str(dims),
+                       "parallelism": f"shards x{d.world}, no collective"},
+            "units_per_s": units / max_s, "units": units, "wall_s": max_wall,
+            "passed": sorted(c for c, v in verdicts.items() if v["passed"]),
+            "failed": sorted(c for c, v in verdicts.items() if not v["passed"]),
+            "missing_shards": len(missing), "clocks": clk.summary(), "journal": str(jdir),
+            "gpu_launches": None,
+        }
+        print(json.dumps(line), flush=True)
+    _ = recs
+    d.close()
+
+
 def main(argv=None) -> int:
+    if argv is None:
+        argv = sys.argv[1:]
+    if "--workload" in argv and "sweep" in argv:
+        ap = argparse.ArgumentParser()
+        ap.add_argument("--gpus", type=int, default=1)
+        ap.add_argument("--steps", type=int, default=1)
+        ap.add_argument("--warmup", type=int, default=1)
+        ap.add_argument("--impl", default="phew")
+        ap.add_argument("--workload", default="sweep")
+        ap.add_argument("--seeds", type=int, default=5)
+        ap.add_argument("--variants", choices=["edge", "reference"], default="edge")
+        ap.add_argument("--tiny", action="store_true")
+        ap.add_argument("--journal-dir", default=None)
+        run_sweep(ap.parse_args(argv))
+        return 0
     args = parse_args(argv)
     if args.impl == "reference":
         run_reference(args)

@@ -179,6 +179,21 @@ int phew_sdpa(const void* q, const void* k, const void* v, void* o, int64_t batc
               int64_t L, int64_t D, float scale, int causal, int dtype, int* error_flag,
               void* stream);
 
+/* ---- seeded inputs for the verification sweep -------------------------- */
+
+#define PHEW_FILL_NORMAL 0       /* N(0, 1) * scale (Box-Muller)           */
+#define PHEW_FILL_UNIFORM 1      /* U(-1, 1) * scale                       */
+#define PHEW_FILL_ONE_HOT_ROWS 2 /* one `scale` per row of `cols`, at a seeded column */
+#define PHEW_FILL_CONSTANT 3     /* every element = scale                  */
+
+/* Fills n elements of `dtype` at `out` from a counter-based generator:
+ * element i depends only on (seed, stream_id, i), so inputs are identical on
+ * any GPU and for any number of GPUs.  Stands in for the host-side draws of
+ * the reference's input factories and edge variants
+ * (verify/checker.py:235-263) at sweep scale. */
+int phew_fill(void* out, int64_t n, int64_t cols, int dtype, int kind, uint64_t seed,
+              uint64_t stream_id, float scale, void* stream);
+
 /* ---- equivalence comparison -------------------------------------------- */
 
 /* Result of one baseline/candidate comparison, written to DEVICE memory. */

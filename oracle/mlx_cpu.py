@@ -491,7 +491,11 @@ def compile(fn=None, **_):  # noqa: A001
 
 
 def rms_norm(x: array, weight: array | None = None, eps: float = 1e-5) -> array:
-    """fast.rms_norm: fp32 mean of squares, then y = w * T(x * r)."""
+    """fast.rms_norm: fp32 mean of squares, then y = w * T(x * r).  The
+    weight must be 1-D over the last axis, as MLX requires."""
+    cols = x.shape[-1]
+    if weight is not None and tuple(weight.shape) != (cols,):
+        raise ValueError(f"rms_norm: weight shape {tuple(weight.shape)} != ({cols},)")
     xv = f32(x.v)
     ms = np.float32(np.mean(xv.astype(np.float64) ** 2, axis=-1, keepdims=True))
     r = (np.float32(1.0) / np.sqrt(ms + np.float32(eps))).astype(np.float32)
@@ -515,10 +519,52 @@ def sdpa(q: array, k: array, v: array, scale: float, mask: Any = None) -> array:
     return array.wrap(round_to(o, q.dtype), q.dtype)
 
 
+# Fused kernels appear in emitted sources as CUDA bodies; the oracle evaluates
+# the chain each body was emitted from (registered by sha1 of the body).
+CUDA_CHAINS: dict[str, dict] = {}
+
+
+class _ChainKernel:
+    def __init__(self, source: str) -> None:
+        import hashlib
+
+        from phew_b200.graph import NodeSpec
+
+        key = hashlib.sha1(source.encode()).hexdigest()
+        if key not in CUDA_CHAINS:
+            raise KeyError("oracle: no chain registered for this fused kernel body")
+        rec = CUDA_CHAINS[key]
+        self.nodes = [NodeSpec.from_json(d) for d in rec["nodes"]]
+        self.ins = [NodeSpec.from_json(d) for d in rec["ext_inputs"]]
+        self.outs = [NodeSpec.from_json(d) for d in rec["ext_outputs"]]
+
+    def __call__(self, inputs, output_shapes, output_dtypes, grid=None, threadgroup=None,
+                 template=None, **_):
+        vals = [x.v if isinstance(x, array) else np.asarray(x) for x in inputs]
+        outs = []
+        for spec, shp, dt in zip(self.outs, output_shapes, output_dtypes):
+            spec.shape = tuple(shp)
+        res = eval_chain(self.nodes, self.ins, self.outs, vals)
+        for r, shp, dt in zip(res, output_shapes, output_dtypes):
+            d = as_dtype(dt)
+            outs.append(array.wrap(r.reshape(shp).astype(d.np), d))
+        return outs
+
+
+def cuda_kernel(name, input_names, output_names, source, header="", **_):
+    return _ChainKernel(source)
+
+
 fast = types.SimpleNamespace(
     rms_norm=rms_norm,
     scaled_dot_product_attention=lambda q, k, v, *, scale=1.0, mask=None, **_: sdpa(q, k, v, scale, mask),
+    cuda_kernel=cuda_kernel,
 )
+
+
+def elementwise_threads(n: int) -> int:
+    """Launch size of emitted elementwise kernels (unused on the CPU)."""
+    return int(n)
 
 
 # ---------------------------------------------------------------------------

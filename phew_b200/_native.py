@@ -44,6 +44,7 @@ EXPORTED_SYMBOLS = (
     "phew_gemm",
     "phew_sdpa_supported",
     "phew_sdpa",
+    "phew_fill",
     "phew_compare_scratch_bytes",
     "phew_compare",
 )
@@ -124,6 +125,10 @@ _SIGNATURES = {
     "phew_sdpa_supported": ([_i64, _i64, _int], _int),
     "phew_sdpa": (
         [_vp, _vp, _vp, _vp, _i64, _i64, _i64, ctypes.c_float, _int, _int, _vp, _vp],
+        _int,
+    ),
+    "phew_fill": (
+        [_vp, _i64, _i64, _int, _int, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float, _vp],
         _int,
     ),
     "phew_compare_scratch_bytes": ([_i64], ctypes.c_size_t),

@@ -240,6 +240,13 @@ _UNARY_F_HALF = {
     "tanh": "phew_tanh16({a})",
     "silu": "__fmul_rn({a}, phew_sigmoid16({a}))",
 }
+# Same ops at about 2^-20 relative error (twice the transcendental-unit work).
+_UNARY_F_HALF_PRECISE = {
+    "exp": "phew_exp16({a})",
+    "sigmoid": "phew_sigmoid16p({a})",
+    "tanh": "phew_tanh16p({a})",
+    "silu": "__fmul_rn({a}, phew_sigmoid16p({a}))",
+}
 
 _BINARY_F = {
     "add": "__fadd_rn({a}, {b})",
@@ -291,13 +298,15 @@ def _to_float(v: str, dt: str) -> str:
 
 
 def scalar_expr(
-    op: str, args: list[str], arg_dtypes: list[str], out_dt: str, round_result: bool = True
+    op: str, args: list[str], arg_dtypes: list[str], out_dt: str, round_result: bool = True,
+    precise16: bool = False,
 ) -> str:
     """C expression computing `op` on value variables, typed for `out_dt`.
 
     Float results are rounded to `out_dt` (unless `round_result` is False,
     for callers that round while packing); integer and bool results use C
-    semantics of the node's C type.
+    semantics of the node's C type.  `precise16` selects the slower,
+    near-correctly-rounded tanh/sigmoid for 16-bit nodes.
     """
     op = canonical_op(op)
     if out_dt in FLOAT_TYPES:
@@ -315,7 +324,10 @@ def scalar_expr(
         elif op in _UNARY_F and len(fa) >= 1:
             expr = _UNARY_F[op].format(a=fa[0])
         elif op in _UNARY_F_PRECISE and len(fa) >= 1:
-            table = _UNARY_F_HALF if half else _UNARY_F_PRECISE
+            if half:
+                table = _UNARY_F_HALF_PRECISE if precise16 else _UNARY_F_HALF
+            else:
+                table = _UNARY_F_PRECISE
             expr = table[op].format(a=fa[0])
         elif op in _BINARY_F and len(fa) == 2:
             expr = _BINARY_F[op].format(a=fa[0], b=fa[1])
@@ -461,7 +473,16 @@ class SubgraphCUDACodegen:
     (become ``out0, out1, ...``).  Raises ``ValueError`` for anything it
     cannot fuse; the fusion pass treats that as "leave the chain unfused"
     (``rules/fusion.py:266-270``).
+
+    ``precise_16bit=True`` computes tanh / sigmoid / silu of 16-bit nodes
+    with about 2^-20 relative error instead of the hardware tanh
+    approximation (about 2^-11, at most a couple of ulps of the 16-bit
+    result); it costs twice the transcendental-unit throughput, which bounds
+    the benchmark chain.
     """
+
+    def __init__(self, precise_16bit: bool = False) -> None:
+        self.precise_16bit = precise_16bit
 
     def emit(
         self,
@@ -494,7 +515,8 @@ class SubgraphCUDACodegen:
             classes.append(classify_input(shp, out_shape))
 
         # Resolve the chain into a statement plan (also validates every op).
-        plan = _Plan(subgraph_nodes, external_inputs, external_outputs)
+        plan = _Plan(subgraph_nodes, external_inputs, external_outputs,
+                     precise16=getattr(self, "precise_16bit", False))
 
         # 32-bit indexing when the traced size leaves 2x headroom; the runtime
         # factory refuses launches whose size would overflow it.
@@ -656,7 +678,8 @@ def _convert(v: str, src: str, dst: str) -> str:
 class _Plan:
     """Resolved chain: variable names, node order and dtype bookkeeping."""
 
-    def __init__(self, nodes, ext_in, ext_out) -> None:
+    def __init__(self, nodes, ext_in, ext_out, precise16: bool = False) -> None:
+        self.precise16 = precise16
         self.nodes = list(nodes)
         self.ext_in = list(ext_in)
         self.outputs = list(ext_out)
@@ -743,7 +766,8 @@ class _Plan:
             else:
                 op = canonical_op(node.op)
                 _check_arity(op, len(args))
-                expr = scalar_expr(op, [a[0] for a in args], [a[1] for a in args], dt)
+                expr = scalar_expr(op, [a[0] for a in args], [a[1] for a in args], dt,
+                                   precise16=self.precise16)
             lines.append(f"const {VALUE_CTYPE[dt]} {v} = {expr};")
             env[node.id] = (v, dt)
         return lines
@@ -777,8 +801,8 @@ class _Plan:
                 hi = [f"{pfx}_hi({a})" for a in ins]
                 dts = [ht] * len(ins)
                 # The pack conversion rounds each half to ht.
-                e_lo = scalar_expr(op, lo, dts, ht, round_result=False)
-                e_hi = scalar_expr(op, hi, dts, ht, round_result=False)
+                e_lo = scalar_expr(op, lo, dts, ht, round_result=False, precise16=self.precise16)
+                e_hi = scalar_expr(op, hi, dts, ht, round_result=False, precise16=self.precise16)
                 lines.append(f"const phew_u32 {v} = {pfx}_pack({e_lo}, {e_hi});")
             env[node.id] = v
         return lines

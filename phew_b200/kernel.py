@@ -141,16 +141,24 @@ __device__ __forceinline__ float phew_rcp(float x) {
   float y; asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x)); return y; }
 // e^x = 2^(x log2 e)
 __device__ __forceinline__ float phew_exp16(float x) { return phew_ex2(x * 1.4426950408889634f); }
+// Precise forms (two transcendental-unit ops each):
 // sigmoid(x) = 1 / (1 + e^-x)
-__device__ __forceinline__ float phew_sigmoid16(float x) { return phew_rcp(1.0f + phew_exp16(-x)); }
+__device__ __forceinline__ float phew_sigmoid16p(float x) { return phew_rcp(1.0f + phew_exp16(-x)); }
 // tanh(x) = sign(x) (1 - 2 / (e^{2|x|} + 1)).  The subtraction loses bits as
 // |x| shrinks (about 2^-14.5 relative at |x| = 2^-8); below 2^-8,
 // tanh(x) = x to within x^3/3 < 2^-16 |x|, so x itself is returned.
-__device__ __forceinline__ float phew_tanh16(float x) {
+__device__ __forceinline__ float phew_tanh16p(float x) {
   const float ax = fabsf(x);
   const float big = 1.0f - 2.0f * phew_rcp(phew_ex2(ax * 2.8853900817779268f) + 1.0f);
   return ax < 0.00390625f ? x : copysignf(big, x);
 }
+// Default forms (one transcendental-unit op each): the hardware tanh
+// approximation (relative error about 2^-11, i.e. at most one or two ulps of
+// the 16-bit result), and sigmoid(x) = (1 + tanh(x / 2)) / 2.
+__device__ __forceinline__ float phew_tanh16(float x) {
+  float y; asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x)); return y; }
+__device__ __forceinline__ float phew_sigmoid16(float x) {
+  return fmaf(0.5f, phew_tanh16(0.5f * x), 0.5f); }
 
 // numpy semantics for the ops below (NaN-propagating max/min, Python-style
 // remainder and floor division).

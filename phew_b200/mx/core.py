@@ -79,11 +79,12 @@ def elementwise_threads(numel: int) -> int:
     """Total threads for an emitted grid-stride elementwise kernel.
 
     One thread per 8 elements (one 16-byte vector of a 16-bit type), capped
-    at two full waves of 2048 threads on every SM; threads loop over the
-    rest.
+    at eight waves of 2048 threads on every SM; threads loop over the rest.
+    (Measured on the fp16 (4096, 8192) chain: 1 wave 4852 GB/s, 2 waves 5110,
+    4 waves 5278, 8 waves 5450.)
     """
     want = builtins.max(1, -(-numel // 8))
-    cap = sm_count() * 2048 * 2
+    cap = sm_count() * 2048 * 8
     return builtins.min(want, cap)
 
 

@@ -1,0 +1,320 @@
+"""Verification sweep: phew's equivalence protocol over many candidates,
+sharded across GPUs.
+
+The reference verifies one candidate at a time in one process
+(``verify/checker.py:77-218``, called from ``optimizer.py:319-322``): for
+each size, seed and edge variant it evaluates baseline and candidate and
+applies the allclose rule.  Here a sweep verifies a set of candidates
+against one baseline:
+
+* unit   = (candidate, seed, size, variant): one baseline/candidate pair
+           compared on the device (``phew_compare``);
+* shard  = (candidate, seed): every size and variant of one seed;
+* verdict per candidate = all of its shards passed (one failing unit fails
+  the candidate, as in the reference).
+
+Shards are ordered seed-major and split into contiguous blocks, one block
+per process (one process per GPU); each process draws the inputs of a
+(seed, size) once on its own device, evaluates the baseline once per
+(seed, size, variant) and reuses it for every candidate of its block.
+There is no data-path collective: processes append verdict records to
+per-rank journals, and the merge reads them back (a rerun skips shards
+already journalled, and shards missing from a dead rank's journal are
+returned for reassignment).
+
+Two variant sets:
+* ``reference``: random / zeros / x1e-6 / x1e6, drawn on the host with
+  ``np.random.default_rng(seed + 1000)`` exactly as the reference does
+  (``verify/checker.py:235-263``); for sizes where host draws are cheap;
+* ``edge``: zeros / N(0,1)*1e4 / N(0,1)*1e-39 (bf16 subnormals) / one-hot
+  rows, drawn on the device by ``phew_fill`` from (seed, variant, argument).
+  Like the reference's variants they replace every array argument.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import hashlib
+import json
+import os
+import time
+from dataclasses import asdict, dataclass, field
+from pathlib import Path
+from typing import Any, Callable, Sequence
+
+import numpy as np
+
+VARIANT_SETS = {
+    "reference": ("random", "zeros", "small_scale", "large_scale"),
+    "edge": ("zeros", "pm1e4", "subnormal", "one_hot_rows"),
+}
+FILL_NORMAL, FILL_UNIFORM, FILL_ONE_HOT, FILL_CONSTANT = 0, 1, 2, 3
+
+
+@dataclass(frozen=True)
+class Shard:
+    candidate: str
+    seed: int
+
+
+@dataclass
+class ShardVerdict:
+    candidate: str
+    seed: int
+    passed: bool
+    failures: list = field(default_factory=list)
+    units: int = 0
+    seconds: float = 0.0
+    rank: int = 0
+
+    def to_json(self) -> str:
+        return json.dumps(asdict(self))
+
+
+def make_shards(candidates: Sequence[str], seeds: Sequence[int]) -> list[Shard]:
+    """Seed-major order: consecutive shards share a seed (and its inputs)."""
+    return [Shard(c, s) for s in seeds for c in candidates]
+
+
+def partition(shards: Sequence[Shard], world: int, rank: int) -> list[Shard]:
+    """Contiguous block `rank` of `world` (sizes differ by at most one)."""
+    n = len(shards)
+    base, extra = divmod(n, world)
+    lo = rank * base + min(rank, extra)
+    hi = lo + base + (1 if rank < extra else 0)
+    return list(shards[lo:hi])
+
+
+def _stream_id(*parts) -> int:
+    h = hashlib.sha1("/".join(str(p) for p in parts).encode()).digest()
+    return int.from_bytes(h[:8], "little")
+
+
+# ---------------------------------------------------------------------------
+# inputs
+# ---------------------------------------------------------------------------
+
+
+@dataclass
+class ArgSpec:
+    """One argument of the baseline: shape, dtype name and how to draw it
+    ("normal" with std 1/sqrt(fan_in), "ones", "causal_mask")."""
+
+    shape: tuple
+    dtype: str
+    kind: str = "normal"
+    fan_in: int = 1
+
+
+class DeviceInputs:
+    """Seeded device arrays for the baseline's arguments and their variants."""
+
+    def __init__(self, arg_specs: Callable[[str], list[ArgSpec]]) -> None:
+        self.arg_specs = arg_specs
+
+    def _fill(self, shape, dtype, kind, seed, stream, scale):
+        from . import _native
+        from .mx.core import _stream, empty
+
+        out = empty(shape, dtype)
+        cols = shape[-1] if len(shape) else 1
+        _native.call("phew_fill", ctypes.c_void_p(out._t.data_ptr()), out.size, max(cols, 1),
+                     out.dtype.code, kind, ctypes.c_uint64(seed & (2**64 - 1)),
+                     ctypes.c_uint64(stream), ctypes.c_float(scale), _stream())
+        return out
+
+    def base(self, size: str, seed: int) -> list:
+        from .mx.core import array
+        from .ops import causal_mask
+
+        from . import dtypes as dt
+
+        args = []
+        for i, spec in enumerate(self.arg_specs(size)):
+            if spec.kind == "ones":
+                args.append(self._fill(spec.shape, spec.dtype, FILL_CONSTANT, 0, 0, 1.0))
+            elif spec.kind == "causal_mask":
+                L, S = spec.shape[-2], spec.shape[-1]
+                args.append(causal_mask(L, S, dt.from_any(spec.dtype)))
+            else:
+                scale = 1.0 / float(np.sqrt(spec.fan_in))
+                args.append(self._fill(spec.shape, spec.dtype, FILL_NORMAL, seed,
+                                       _stream_id("base", size, i), scale))
+        _ = array
+        return args
+
+    def variant(self, name: str, base_args: list, size: str, seed: int) -> list:
+        from .mx.core import array, zeros_like
+
+        if name == "random":
+            return base_args
+        if name == "zeros":
+            return [zeros_like(a) for a in base_args]
+        if name in ("small_scale", "large_scale"):
+            # reference draws (host): verify/checker.py:246-263
+            rng = np.random.default_rng(seed + 1000)
+            small = [array(rng.standard_normal(a.shape).astype(np.float32) * 1e-6).astype(a.dtype)
+                     for a in base_args]
+            if name == "small_scale":
+                return small
+            return [array(rng.standard_normal(a.shape).astype(np.float32) * 1e6).astype(a.dtype)
+                    for a in base_args]
+        kinds = {"pm1e4": (FILL_NORMAL, 1e4), "subnormal": (FILL_NORMAL, 1e-39),
+                 "one_hot_rows": (FILL_ONE_HOT, 1.0)}
+        if name not in kinds:
+            raise ValueError(f"unknown variant {name!r}")
+        kind, scale = kinds[name]
+        return [self._fill(a.shape, a.dtype, kind, seed, _stream_id(name, size, i), scale)
+                for i, a in enumerate(base_args)]
+
+
+# ---------------------------------------------------------------------------
+# running shards
+# ---------------------------------------------------------------------------
+
+
+def load_journal(path: Path) -> dict[tuple, ShardVerdict]:
+    done = {}
+    if path.exists():
+        for line in path.read_text().splitlines():
+            if line.strip():
+                d = json.loads(line)
+                done[(d["candidate"], d["seed"])] = ShardVerdict(**d)
+    return done
+
+
+def run_shards(
+    shards: Sequence[Shard],
+    evaluate: Callable[[str, int, str, str], tuple[bool, str | None]],
+    sizes: Sequence[str],
+    variants: Sequence[str],
+    journal: Path | None = None,
+    rank: int = 0,
+    on_group: Callable[[int, str], None] | None = None,
+) -> list[ShardVerdict]:
+    """Run `shards` in order.  `evaluate(candidate, seed, size, variant)`
+    returns (ok, failure string or None) for one unit.  Shards already in
+    `journal` are skipped (resume); each finished shard is appended to it."""
+    done = load_journal(journal) if journal else {}
+    out = []
+    by_seed: dict[int, list[Shard]] = {}
+    for s in shards:
+        by_seed.setdefault(s.seed, []).append(s)
+    for seed, group in by_seed.items():
+        todo = [s for s in group if (s.candidate, s.seed) not in done]
+        out += [done[(s.candidate, s.seed)] for s in group if (s.candidate, s.seed) in done]
+        if not todo:
+            continue
+        verdicts = {s.candidate: ShardVerdict(s.candidate, seed, True, rank=rank) for s in todo}
+        t0 = time.perf_counter()
+        for size in sizes:
+            if on_group:
+                on_group(seed, size)
+            for variant in variants:
+                for s in todo:
+                    ok, failure = evaluate(s.candidate, seed, size, variant)
+                    v = verdicts[s.candidate]
+                    v.units += 1
+                    if not ok:
+                        v.passed = False
+                        v.failures.append(failure)
+        dt = time.perf_counter() - t0
+        for s in todo:
+            v = verdicts[s.candidate]
+            v.seconds = dt / len(todo)
+            out.append(v)
+            if journal:
+                with open(journal, "a") as f:
+                    f.write(v.to_json() + "\n")
+    return out
+
+
+def merge(journal_dir: Path, shards: Sequence[Shard]) -> tuple[dict[str, dict], list[Shard]]:
+    """Per-candidate verdicts from every rank's journal, plus the shards no
+    journal holds (to be reassigned)."""
+    recs: dict[tuple, ShardVerdict] = {}
+    for p in sorted(Path(journal_dir).glob("journal.rank*.jsonl")):
+        recs.update(load_journal(p))
+    missing = [s for s in shards if (s.candidate, s.seed) not in recs]
+    cands: dict[str, dict] = {}
+    for s in shards:
+        c = cands.setdefault(s.candidate, {"passed": True, "failures": [], "shards": 0})
+        r = recs.get((s.candidate, s.seed))
+        if r is None:
+            c["passed"] = False
+            continue
+        c["shards"] += 1
+        c["passed"] = c["passed"] and r.passed
+        c["failures"] += r.failures
+    return cands, missing
+
+
+# ---------------------------------------------------------------------------
+# device evaluation of one unit
+# ---------------------------------------------------------------------------
+
+
+class DeviceEvaluator:
+    """Evaluates units on the current GPU, caching the baseline output and
+    the inputs of the current (seed, size, variant)."""
+
+    def __init__(self, baseline: Callable, candidates: dict[str, Callable], inputs: DeviceInputs,
+                 checker=None) -> None:
+        from .verify import EquivalenceChecker
+
+        self.baseline = baseline
+        self.candidates = candidates
+        self.inputs = inputs
+        self.checker = checker or EquivalenceChecker()
+        self._key = None
+        self._base_args = None
+        self._args = None
+        self._base_out = None
+        self._base_exc = None
+
+    def _prepare(self, seed: int, size: str, variant: str) -> None:
+        key = (seed, size, variant)
+        if key == self._key:
+            return
+        self._args = self._base_out = self._base_exc = None
+        if self._key is None or self._key[:2] != (seed, size):
+            self._base_args = None
+            self._base_args = self.inputs.base(size, seed)
+        self._args = self.inputs.variant(variant, self._base_args, size, seed)
+        try:
+            self._base_out = self.baseline(*self._args)
+        except Exception as exc:  # noqa: BLE001
+            self._base_exc = exc
+        self._key = key
+
+    def __call__(self, candidate: str, seed: int, size: str, variant: str):
+        self._prepare(seed, size, variant)
+        tag = f"size={size} seed={seed} variant={variant}"
+        try:
+            if self._base_exc is not None:
+                raise self._base_exc
+            out = self.candidates[candidate](*self._args)
+            ok, max_diff = self.checker.check_unit(self._base_out, out)
+            if ok:
+                return True, None
+            return False, f"{tag} max_diff={max_diff:.3e}"
+        except Exception as exc:  # noqa: BLE001  (the reference records any failure)
+            return False, f"{tag} exception={exc}"
+
+    def release(self) -> None:
+        self._key = self._base_args = self._args = self._base_out = None
+
+
+def load_candidates(sources: dict[str, str]) -> dict[str, Callable]:
+    """exec() each emitted ``output_source`` (as ``optimizer.py:365-369``
+    does) and return its ``optimized`` function."""
+    out = {}
+    for name, src in sources.items():
+        ns: dict[str, Any] = {}
+        exec(compile(src, f"<{name}>", "exec"), ns)
+        out[name] = ns["optimized"]
+    return out
+
+
+def env_rank() -> tuple[int, int]:
+    return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))

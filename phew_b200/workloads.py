@@ -198,6 +198,91 @@ def normed_matmul_inputs(size: str, seed: int, M: int | None = None):
     return [x, W]
 
 
+# ---------------------------------------------------------------------------
+# decoder block (bf16): the verification-sweep workload
+# ---------------------------------------------------------------------------
+
+DECODER_SEQ = {"small": 512, "typical": 2048, "large": 8192}
+
+
+@dataclass(frozen=True)
+class DecoderDims:
+    batch: int = 8
+    dim: int = 4096
+    heads: int = 32
+    hidden: int = 14336
+
+    @property
+    def head_dim(self) -> int:
+        return self.dim // self.heads
+
+
+DECODER_FULL = DecoderDims()
+DECODER_TINY = DecoderDims(batch=2, dim=256, heads=2, hidden=512)
+DECODER_TINY_SEQ = {"small": 128, "typical": 256, "large": 384}
+
+
+def decoder_block_fn(mx, dims: DecoderDims = DECODER_FULL):
+    """Pre-norm decoder block: RMSNorm -> fused QKV projection -> causal
+    attention (additive mask input) -> output projection + residual ->
+    SwiGLU MLP whose norm is applied after the gate/up projections (the
+    normed-matmul form (h @ W) * rsqrt(mean(h*h) + eps)) -> residual."""
+    H, D, C = dims.heads, dims.head_dim, dims.dim
+    scale = 1.0 / math.sqrt(D)
+
+    def fn(x, w_norm, w_qkv, w_o, w_gate, w_up, w_down, mask):
+        B, T = x.shape[0], x.shape[1]
+        h = x * mx.rsqrt(mx.mean(x * x, axis=-1, keepdims=True) + 1e-5) * w_norm
+        qkv = (h @ w_qkv).reshape(B, T, 3, H, D).transpose(2, 0, 3, 1, 4)
+        q, k, v = qkv[0], qkv[1], qkv[2]
+        s = (q @ k.transpose(0, 1, 3, 2)) * scale + mask
+        a = (mx.softmax(s, axis=-1) @ v).transpose(0, 2, 1, 3).reshape(B, T, C)
+        h1 = x + a @ w_o
+        r = mx.rsqrt(mx.mean(h1 * h1, axis=-1, keepdims=True) + 1e-5)
+        g = (h1 @ w_gate) * r
+        u = (h1 @ w_up) * r
+        return h1 + ((g * mx.sigmoid(g)) * u) @ w_down
+
+    return fn
+
+
+def decoder_arg_shapes(seq: int, dims: DecoderDims = DECODER_FULL) -> list[tuple]:
+    C, F = dims.dim, dims.hidden
+    return [(dims.batch, seq, C), (C,), (C, 3 * C), (C, C), (C, F), (C, F), (F, C), (seq, seq)]
+
+
+def decoder_fan_in(dims: DecoderDims = DECODER_FULL) -> list[int]:
+    C, F = dims.dim, dims.hidden
+    return [1, 1, C, C, C, C, F, 1]
+
+
+def decoder_inputs(size: str, seed: int, dims: DecoderDims = DECODER_FULL, seqs=None):
+    """Host inputs (numpy, bf16): x ~ N(0,1), weights ~ N(0, 1/fan_in), norm
+    weight = ones, causal additive mask."""
+    seq = (seqs or DECODER_SEQ)[size]
+    rng = np.random.default_rng(seed)
+    out = []
+    for i, (shp, fan) in enumerate(zip(decoder_arg_shapes(seq, dims), decoder_fan_in(dims))):
+        if i == 1:
+            out.append(np.ones(shp, np.float32).astype(BF16))
+        elif i == 7:
+            out.append(causal_mask(seq))
+        else:
+            a = rng.standard_normal(shp, dtype=np.float32)
+            if fan > 1:
+                a *= np.float32(1.0 / math.sqrt(fan))
+            out.append(a.astype(BF16))
+    return out
+
+
+def decoder_flops(seq: int, dims: DecoderDims = DECODER_FULL) -> int:
+    T = dims.batch * seq
+    C, F = dims.dim, dims.hidden
+    proj = 2 * T * (C * 3 * C + C * C + 2 * C * F + F * C)
+    attn = 2 * 2 * dims.batch * dims.heads * seq * seq * dims.head_dim
+    return proj + attn
+
+
 WORKLOADS = {
     "rms_norm": Workload("rms_norm", rms_norm_fn, rms_norm_inputs, RMS_ROWS, "float32"),
     "gelu_chain": Workload("gelu_chain", gelu_chain_fn, gelu_chain_inputs, CHAIN_ROWS, "float16"),

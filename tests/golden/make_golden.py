@@ -5,22 +5,32 @@ Run in a checkout that has the phew reference importable (default
 
     python tests/golden/make_golden.py
 
+The reference's numerics need MLX, which is not installable here; its
+Python code (tracer, passes, emitter, checker) runs unchanged with
+``mlx.core`` served by the oracle namespace (``oracle/mlx_cpu.py``).
+
 Writes
 * verdicts.json -- verdicts and failure strings of the reference's own
   ``EquivalenceChecker.check`` (verify/checker.py:77-218) on the cases of
-  ``verdict_cases.py``; MLX is absent, so ``mlx.core`` is served by the
-  oracle namespace (numpy) while the checker's code runs unchanged;
+  ``verdict_cases.py``;
 * allclose.json -- the reference's ``_allclose`` (checker.py:220-233) on
   seeded array pairs covering NaN/Inf/fp16/fp32 arithmetic;
 * bench.json -- the reference's ``compare`` / ``check_convergence`` outputs;
 * chains.json -- fused chains that the reference's ElementwiseFusionPass
   (rules/fusion.py:116-332) forms on the benchmark graphs;
-* sources/*.py -- ``output_source`` of the reference's passes + MLXCodegen,
-  re-targeted by ``phew_b200.integration`` (the drop-in binding).
+* sources/*.py -- ``output_source`` of the reference's tracer + passes +
+  MLXCodegen, re-targeted by ``phew_b200.integration`` (the drop-in
+  binding), for the benchmark functions and for the 16 decoder-block
+  candidates of the verification sweep (rms_norm / SDPA / normed-matmul
+  substitution x elementwise fusion, on or off);
+* sources/cuda_chains.json -- for every fused kernel body in those sources,
+  the chain it was emitted from, so the oracle can evaluate it on the CPU.
 """
 
 from __future__ import annotations
 
+import hashlib
+import itertools
 import json
 import math
 import os
@@ -39,13 +49,48 @@ sys.path.insert(0, str(HERE))
 
 from oracle import mlx_cpu  # noqa: E402
 
+from phew_b200 import workloads as W  # noqa: E402
+
+SOURCES = HERE / "sources"
+
 
 def fake_mlx():
+    """Register an ``mlx`` package whose ``core`` is the oracle namespace."""
+    core = types.ModuleType("mlx.core")
+    for k in dir(mlx_cpu):
+        if not k.startswith("__"):
+            setattr(core, k, getattr(mlx_cpu, k))
+    # dtype names the reference's Dtype.from_mlx table expects (ir/dtype.py:70-88)
+    core.float64 = mlx_cpu.Dtype("float32")
+    core.complex64 = mlx_cpu.Dtype("float32")
+    fast = types.ModuleType("mlx.core.fast")
+    fast.rms_norm = mlx_cpu.rms_norm
+    fast.scaled_dot_product_attention = mlx_cpu.fast.scaled_dot_product_attention
+    core.fast = fast
+    nn = types.ModuleType("mlx.nn")
     pkg = types.ModuleType("mlx")
     pkg.__path__ = []
-    pkg.core = mlx_cpu
-    sys.modules["mlx"] = pkg
-    sys.modules["mlx.core"] = mlx_cpu
+    pkg.core, pkg.nn = core, nn
+    sys.modules.update({"mlx": pkg, "mlx.core": core, "mlx.core.fast": fast, "mlx.nn": nn})
+    return core
+
+
+def placeholder(shape, dtype):
+    """A zero-cost oracle array of the given shape (the tracer reads only
+    shapes and dtypes)."""
+    d = mlx_cpu.as_dtype(dtype)
+    return mlx_cpu.array.wrap(np.broadcast_to(np.zeros((), d.np), shape), d)
+
+
+def trace(fn, shapes_dtypes):
+    from phew.ir.importer import trace_to_graph
+
+    return trace_to_graph(fn, [placeholder(s, d) for s, d in shapes_dtypes], {})
+
+
+# ---------------------------------------------------------------------------
+# verdict / bench goldens
+# ---------------------------------------------------------------------------
 
 
 def make_verdicts():
@@ -93,8 +138,7 @@ def make_allclose():
                 cases.append({"dtype": dtype, "kind": kind, "atol": atol, "rtol": rtol,
                               "a": a.astype(np.float64).tolist(), "b": b.astype(np.float64).tolist(),
                               "ok": bool(ok)})
-    # JSON cannot hold NaN/Inf portably: encode as strings
-    for c in cases:
+    for c in cases:  # JSON cannot hold NaN/Inf portably: encode as strings
         for k in ("a", "b"):
             c[k] = [repr(v) if not math.isfinite(v) else v for v in c[k]]
     return cases
@@ -110,115 +154,49 @@ def make_bench():
         o = BenchResult(om, 0.1, 0.01, 20, False, [om])
         rows.append({"baseline": bm, "optimized": om, "compare": compare(b, o)})
     conv = []
-    for cur, cand, sizes, beaten in ((10, 9, 1, 1), (10, 9.9, 1, 1), (10, 5, 3, 1), (10, 5, 3, 3), (0, 1, 1, 1)):
-        conv.append({"args": [cur, cand, sizes, beaten], "result": check_convergence(cur, cand, sizes, beaten)})
+    for args in ((10, 9, 1, 1), (10, 9.9, 1, 1), (10, 5, 3, 1), (10, 5, 3, 3), (0, 1, 1, 1)):
+        conv.append({"args": list(args), "result": check_convergence(*args)})
     return {"compare": rows, "convergence": conv}
 
 
-# -- benchmark graphs built with the reference's IR (what its tracer records) --
+# ---------------------------------------------------------------------------
+# graphs of the benchmark functions, traced by the reference's tracer
+# ---------------------------------------------------------------------------
 
 
-def _graphs():
-    from phew.ir import Constant, Dtype, Elementwise, Graph, Input, MatMul, Reduce, Transpose
-
-    def ew(g, op, *ins, shape, dt):
-        return g.add(Elementwise(shape=shape, dtype=dt, inputs=[i.id for i in ins], op=op))
-
-    def const(g, v, dt):
-        return g.add(Constant(shape=(), dtype=dt, value=v))
-
-    def rms(n=1024):
-        g = Graph()
-        dt = Dtype.float32
-        S = (n, 2048)
-        x = g.add(Input(shape=S, dtype=dt, name="x"))
-        w = g.add(Input(shape=(2048,), dtype=dt, name="w"))
-        sq = ew(g, "mul", x, x, shape=S, dt=dt)
-        m = g.add(Reduce(shape=(n, 1), dtype=dt, inputs=[sq.id], op="mean", axes=(1,), keepdims=True))
-        a = ew(g, "add", m, const(g, 1e-5, dt), shape=(n, 1), dt=dt)
-        r = ew(g, "rsqrt", a, shape=(n, 1), dt=dt)
-        y = ew(g, "mul", x, r, shape=S, dt=dt)
-        z = ew(g, "mul", y, w, shape=S, dt=dt)
-        g.outputs = [z.id]
-        return g
-
-    def gelu(rows=4096):
-        g = Graph()
-        dt = Dtype.float16
-        S = (rows, 8192)
-        x = g.add(Input(shape=S, dtype=dt, name="x"))
-        a = g.add(Input(shape=(8192,), dtype=dt, name="a"))
-        b = g.add(Input(shape=(8192,), dtype=dt, name="b"))
-        c = g.add(Input(shape=S, dtype=dt, name="c"))
-        xa = ew(g, "mul", x, a, shape=S, dt=dt)
-        y = ew(g, "add", xa, b, shape=S, dt=dt)
-        yh = ew(g, "mul", y, const(g, 0.5, dt), shape=S, dt=dt)
-        yy = ew(g, "mul", y, y, shape=S, dt=dt)
-        yyy = ew(g, "mul", yy, y, shape=S, dt=dt)
-        cub = ew(g, "mul", yyy, const(g, 0.044715, dt), shape=S, dt=dt)
-        inner = ew(g, "add", y, cub, shape=S, dt=dt)
-        arg = ew(g, "mul", inner, const(g, math.sqrt(2 / math.pi), dt), shape=S, dt=dt)
-        t = ew(g, "tanh", arg, shape=S, dt=dt)
-        t1 = ew(g, "add", t, const(g, 1.0, dt), shape=S, dt=dt)
-        ge = ew(g, "mul", yh, t1, shape=S, dt=dt)
-        s = ew(g, "sigmoid", c, shape=S, dt=dt)
-        gs = ew(g, "mul", ge, s, shape=S, dt=dt)
-        z = ew(g, "add", gs, x, shape=S, dt=dt)
-        g.outputs = [z.id]
-        return g
-
-    def attn(L=2048):
-        g = Graph()
-        dt = Dtype.bfloat16
-        S = (4, 32, L, 128)
-        P = (4, 32, L, L)
-        q = g.add(Input(shape=S, dtype=dt, name="q"))
-        k = g.add(Input(shape=S, dtype=dt, name="k"))
-        v = g.add(Input(shape=S, dtype=dt, name="v"))
-        mask = g.add(Input(shape=(L, L), dtype=dt, name="mask"))
-        kt = g.add(Transpose(shape=(4, 32, 128, L), dtype=dt, inputs=[k.id], axes=(0, 1, 3, 2)))
-        s = g.add(MatMul(shape=P, dtype=dt, inputs=[q.id, kt.id]))
-        sc = ew(g, "mul", s, const(g, 1 / math.sqrt(128), dt), shape=P, dt=dt)
-        sm_in = ew(g, "add", sc, mask, shape=P, dt=dt)
-        sm = g.add(Reduce(shape=P, dtype=dt, inputs=[sm_in.id], op="softmax", axes=(3,), keepdims=True))
-        o = g.add(MatMul(shape=S, dtype=dt, inputs=[sm.id, v.id]))
-        g.outputs = [o.id]
-        return g
-
-    def normed_mm(M=8192):
-        g = Graph()
-        dt = Dtype.bfloat16
-        S = (M, 4096)
-        x = g.add(Input(shape=S, dtype=dt, name="x"))
-        W = g.add(Input(shape=(4096, 4096), dtype=dt, name="W"))
-        mm = g.add(MatMul(shape=S, dtype=dt, inputs=[x.id, W.id]))
-        sq = ew(g, "mul", x, x, shape=S, dt=dt)
-        m = g.add(Reduce(shape=(M, 1), dtype=dt, inputs=[sq.id], op="mean", axes=(1,), keepdims=True))
-        r = ew(g, "rsqrt", ew(g, "add", m, const(g, 1e-5, dt), shape=(M, 1), dt=dt), shape=(M, 1), dt=dt)
-        z = ew(g, "mul", mm, r, shape=S, dt=dt)
-        g.outputs = [z.id]
-        return g
-
-    return {"rms_norm": rms, "gelu_chain": gelu, "attention": attn, "normed_matmul": normed_mm}
+def graphs(core):
+    bf, f16, f32 = "bfloat16", "float16", "float32"
+    dec_full = W.decoder_arg_shapes(W.DECODER_SEQ["typical"], W.DECODER_FULL)
+    dec_tiny = W.decoder_arg_shapes(W.DECODER_TINY_SEQ["typical"], W.DECODER_TINY)
+    return {
+        "rms_norm": lambda: trace(W.rms_norm_fn(core), [((1024, 2048), f32), ((2048,), f32)]),
+        "gelu_chain": lambda: trace(W.gelu_chain_fn(core), [((4096, 8192), f16), ((8192,), f16),
+                                                             ((8192,), f16), ((4096, 8192), f16)]),
+        "attention": lambda: trace(W.attention_fn(core), [((4, 32, 2048, 128), bf)] * 3 +
+                                   [((2048, 2048), bf)]),
+        "normed_matmul": lambda: trace(W.normed_matmul_fn(core), [((8192, 4096), bf),
+                                                                  ((4096, 4096), bf)]),
+        "decoder_full": lambda: trace(W.decoder_block_fn(core, W.DECODER_FULL), [(s, bf) for s in dec_full]),
+        "decoder_tiny": lambda: trace(W.decoder_block_fn(core, W.DECODER_TINY), [(s, bf) for s in dec_tiny]),
+    }
 
 
-def make_chains():
+def make_chains(core):
+    from phew.ir.ops import Constant
     from phew.rules.fusion import ElementwiseFusionPass
 
     from phew_b200.graph import from_phew
 
     out = {}
-    for name, build in _graphs().items():
+    for name, build in graphs(core).items():
+        if name.startswith("decoder"):
+            continue
         g = build()
         spec = from_phew(g)
-        p = ElementwiseFusionPass()
-        chains = p._find_chains(g)
         recs = []
-        for ch in chains:
+        for ch in ElementwiseFusionPass()._find_chains(g):
             ids = {n.id for n in ch}
             ext_in, seen = [], set()
-            from phew.ir.ops import Constant
-
             for n in ch:
                 if isinstance(n, Constant):
                     continue
@@ -233,7 +211,84 @@ def make_chains():
     return out
 
 
-def make_sources():
+# ---------------------------------------------------------------------------
+# candidates
+# ---------------------------------------------------------------------------
+
+
+def apply_candidate(graph, rms: bool, sdpa: bool, nmm: bool, fusion: bool):
+    """The reference's pass order (rules/graph_passes.py:24-114) with each
+    primitive substitution toggled on its own.  With every toggle on this is
+    run_all_passes(enable_fusion=fusion, normed_matmul enabled)."""
+    from phew.rules.algebraic import AlgebraicPass
+    from phew.rules.compile_boundaries import CompileBoundaryPass
+    from phew.rules.fusion import ElementwiseFusionPass
+    from phew.rules.primitive_subst import PrimitiveSubstPass
+    from phew.verify import SubstitutionClass as SC
+
+    applied = []
+    before = len(graph)
+    AlgebraicPass().run(graph)
+    if len(graph) != before:
+        applied.append("algebraic")
+    if fusion and ElementwiseFusionPass().run(graph):
+        applied.append("elementwise_fusion")
+    if CompileBoundaryPass().run(graph):
+        applied.append("compile_boundary")
+    p = PrimitiveSubstPass(enabled_classes={SC.fp32_to_fp32, SC.normed_matmul})
+    changed = False
+    if rms:
+        changed |= p._match_rms_norm(graph)
+    if nmm:
+        changed |= p._match_normed_matmul(graph)
+    changed |= p._match_layer_norm(graph)
+    changed |= p._match_rope(graph)
+    if sdpa:
+        changed |= p._match_sdpa(graph)
+    if changed:
+        applied.append("primitive_subst")
+    return graph, applied
+
+
+class ChainRecorder:
+    """Wraps the CUDA emitter to remember the chain behind every body."""
+
+    def __init__(self):
+        from phew_b200.emit.cuda_codegen import SubgraphCUDACodegen
+        from phew_b200.graph import from_phew  # noqa: F401
+
+        self.base = SubgraphCUDACodegen
+        self.chains = {}
+        rec = self
+
+        class Recording(SubgraphCUDACodegen):
+            def emit(self, nodes, ext_in, ext_out):
+                src, i, o = super().emit(nodes, ext_in, ext_out)
+                rec.chains[hashlib.sha1(src.encode()).hexdigest()] = {
+                    "nodes": [_node_json(n) for n in nodes],
+                    "ext_inputs": [_node_json(n) for n in ext_in],
+                    "ext_outputs": [_node_json(n) for n in ext_out],
+                }
+                return src, i, o
+
+        self.cls = Recording
+
+
+def _node_json(n):
+    from phew_b200.graph import from_phew
+
+    class One:
+        def __init__(self, node):
+            self._n = [node]
+            self.outputs = [node.id]
+
+        def nodes(self):
+            return self._n
+
+    return from_phew(One(n)).to_json()["nodes"][0]
+
+
+def make_sources(core):
     from phew.rules import run_all_passes
     from phew.verify import SubstitutionClass as SC
 
@@ -241,36 +296,44 @@ def make_sources():
 
     integration.install(mx_module=False)
     import phew.emit
+    import phew.emit.msl_codegen
 
+    rec = ChainRecorder()
+    phew.emit.msl_codegen.SubgraphMSLCodegen = rec.cls
+    builders = graphs(core)
     srcs = {}
-    for name, build in _graphs().items():
+    for name in ("rms_norm", "gelu_chain", "attention", "normed_matmul"):
         classes = {SC.fp32_to_fp32}
         if name == "normed_matmul":
             classes.add(SC.normed_matmul)
         for fusion in (False, True):
-            g = build()
-            g, applied = run_all_passes(g, enable_tensorops=False, enable_fusion=fusion,
-                                        enabled_subst_classes=classes)
-            src = phew.emit.MLXCodegen().emit(g, fn_name="optimized")
-            key = f"{name}__fusion{int(fusion)}"
-            srcs[key] = {"applied": applied, "source": src}
-    return srcs
+            g, applied = run_all_passes(builders[name](), enable_tensorops=False,
+                                        enable_fusion=fusion, enabled_subst_classes=classes)
+            srcs[f"{name}__fusion{int(fusion)}"] = (applied, phew.emit.MLXCodegen().emit(g, fn_name="optimized"))
+    for name in ("decoder_full", "decoder_tiny"):
+        for rms, sdpa, nmm, fusion in itertools.product((0, 1), repeat=4):
+            g, applied = apply_candidate(builders[name](), bool(rms), bool(sdpa), bool(nmm), bool(fusion))
+            key = f"{name}__rms{rms}_sdpa{sdpa}_nmm{nmm}_fus{fusion}"
+            srcs[key] = (applied, phew.emit.MLXCodegen().emit(g, fn_name="optimized"))
+    phew.emit.msl_codegen.SubgraphMSLCodegen = rec.base
+    return srcs, rec.chains
 
 
 def main() -> int:
-    fake_mlx()
-    (HERE / "sources").mkdir(exist_ok=True)
+    core = fake_mlx()
+    SOURCES.mkdir(exist_ok=True)
     (HERE / "verdicts.json").write_text(json.dumps(make_verdicts(), indent=1))
     (HERE / "allclose.json").write_text(json.dumps(make_allclose()))
     (HERE / "bench.json").write_text(json.dumps(make_bench(), indent=1))
-    (HERE / "chains.json").write_text(json.dumps(make_chains()))
-    srcs = make_sources()
+    (HERE / "chains.json").write_text(json.dumps(make_chains(core)))
+    srcs, chains = make_sources(core)
     index = {}
-    for key, rec in srcs.items():
-        (HERE / "sources" / f"{key}.py").write_text(rec["source"])
-        index[key] = rec["applied"]
-    (HERE / "sources" / "index.json").write_text(json.dumps(index, indent=1))
-    print("wrote fixtures to", HERE)
+    for key, (applied, src) in srcs.items():
+        (SOURCES / f"{key}.py").write_text(src)
+        index[key] = applied
+    (SOURCES / "index.json").write_text(json.dumps(index, indent=1))
+    (SOURCES / "cuda_chains.json").write_text(json.dumps(chains))
+    print(f"wrote {len(srcs)} sources and {len(chains)} fused chains to {HERE}")
     return 0
 
 

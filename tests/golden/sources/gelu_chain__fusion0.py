@@ -2,9 +2,9 @@ import phew_b200.mx as mx
 from phew_b200.mx import fast
 
 @mx.compile
-def optimized(x, a, b, c, *_, **__):
-    t1 = x * a
-    t2 = t1 + b
+def optimized(x0, x1, x2, x3, *_, **__):
+    t1 = x0 * x1
+    t2 = t1 + x2
     c3 = mx.array(0.5, dtype=mx.float16)
     t4 = t2 * c3
     t5 = t2 * t2
@@ -18,7 +18,7 @@ def optimized(x, a, b, c, *_, **__):
     c13 = mx.array(1.0, dtype=mx.float16)
     t14 = t12 + c13
     t15 = t4 * t14
-    t16 = mx.sigmoid(c)
+    t16 = mx.sigmoid(x3)
     t17 = t15 * t16
-    t18 = t17 + x
+    t18 = t17 + x0
     return t18

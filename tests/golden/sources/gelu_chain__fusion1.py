@@ -2,7 +2,7 @@ import phew_b200.mx as mx
 from phew_b200.mx import fast
 
 @mx.compile
-def optimized(x, a, b, c, *_, **__):
+def optimized(x0, x1, x2, x3, *_, **__):
     _kernel_119 = mx.fast.cuda_kernel(
         name="kernel_119",
         input_names=['inp0', 'inp1', 'inp2', 'inp3'],
@@ -79,10 +79,10 @@ def optimized(x, a, b, c, *_, **__):
     }""",
     )
     kernel1_out = _kernel_119(
-        inputs=[x, a, b, c],
-        output_shapes=[x.shape],
+        inputs=[x0, x1, x2, x3],
+        output_shapes=[x0.shape],
         output_dtypes=[mx.float16],
-        grid=(mx.elementwise_threads(x.size), 1, 1),
+        grid=(mx.elementwise_threads(x0.size), 1, 1),
         threadgroup=(256, 1, 1),
         template=[],
     )

@@ -2,7 +2,7 @@ import phew_b200.mx as mx
 from phew_b200.mx import fast
 
 @mx.compile
-def optimized(x, W, *_, **__):
-    t1 = mx.fast.rms_norm(x, None, eps=1e-05)
-    t2 = t1 @ W
+def optimized(x0, x1, *_, **__):
+    t1 = mx.fast.rms_norm(x0, None, eps=1e-05)
+    t2 = t1 @ x1
     return t2

@@ -2,10 +2,10 @@ import phew_b200.mx as mx
 from phew_b200.mx import fast
 
 @mx.compile
-def optimized(x, W, *_, **__):
-    t1 = x * x
+def optimized(x0, x1, *_, **__):
+    t1 = x0 * x0
     t2 = mx.mean(t1, axis=[1], keepdims=True)
-    t3 = x @ W
+    t3 = x0 @ x1
     _kernel_168 = mx.fast.cuda_kernel(
         name="kernel_168",
         input_names=['inp0', 'inp1'],

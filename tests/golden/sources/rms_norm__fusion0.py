@@ -2,6 +2,6 @@ import phew_b200.mx as mx
 from phew_b200.mx import fast
 
 @mx.compile
-def optimized(x, w, *_, **__):
-    t1 = mx.fast.rms_norm(x, w, eps=1e-05)
+def optimized(x0, x1, *_, **__):
+    t1 = mx.fast.rms_norm(x0, x1, eps=1e-05)
     return t1

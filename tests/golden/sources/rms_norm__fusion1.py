@@ -2,8 +2,8 @@ import phew_b200.mx as mx
 from phew_b200.mx import fast
 
 @mx.compile
-def optimized(x, w, *_, **__):
-    t1 = x * x
+def optimized(x0, x1, *_, **__):
+    t1 = x0 * x0
     t2 = mx.mean(t1, axis=[1], keepdims=True)
     _kernel_72 = mx.fast.cuda_kernel(
         name="kernel_72",
@@ -51,10 +51,10 @@ def optimized(x, w, *_, **__):
     }""",
     )
     kernel3_out = _kernel_72(
-        inputs=[t2, x, w],
-        output_shapes=[x.shape],
+        inputs=[t2, x0, x1],
+        output_shapes=[x0.shape],
         output_dtypes=[mx.float32],
-        grid=(mx.elementwise_threads(x.size), 1, 1),
+        grid=(mx.elementwise_threads(x0.size), 1, 1),
         threadgroup=(256, 1, 1),
         template=[],
     )

@@ -60,7 +60,13 @@ def test_gelu_chain_parity(mx, dtype, rows):
     xs = [x.astype(np.float32).astype(np_dt) for x in xs]
     got = run_chain(mx, chain, ins, outs, xs)[0]
     ref = mlx_cpu.eval_chain(chain, ins, outs, xs)[0]
-    assert_close(got, ref, dtype, max_ulps=8 if dtype != "float32" else 64, frac_exact=0.97)
+    # 16-bit results round away the last-ulp differences between CUDA's and
+    # numpy's fp32 transcendentals, so nearly every element is bit-identical;
+    # fp32 results keep them (a few ulps).
+    if dtype == "float32":
+        assert_close(got, ref, dtype, max_ulps=64)
+    else:
+        assert_close(got, ref, dtype, max_ulps=8, frac_exact=0.97)
 
 
 def test_chain_tail_and_unaligned(mx):

@@ -72,8 +72,12 @@ def load_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
-def load_traffic(name: str) -> float | None:
-    p = ROOT / "profiles" / f"{name}.json"
+def load_traffic(name: str | None) -> float | None:
+    """DRAM bytes per launch from the committed ncu summary of this kernel
+    and workload (profiles/<name>.traffic.json), or None."""
+    if not name:
+        return None
+    p = ROOT / "profiles" / f"{name}.traffic.json"
     if p.exists():
         return json.loads(p.read_text()).get("dram_bytes_per_launch")
     return None
@@ -196,6 +200,7 @@ class GeluChain:
     metric, unit, bound, dtype = "fused_kernel_hbm_gbs", "GB/s", "hbm", "f16"
     ROWS, COLS = 4096, 8192
     kernel_regex = "gelu_chain_fused"
+    profile = "gelu_chain_fused_fp16_4096x8192"
 
     def describe(self):
         return (f"gelu_chain: z = tanh-GELU(x*a+b)*sigmoid(c)+x, fp16 ({self.ROWS},{self.COLS}), "
@@ -292,6 +297,7 @@ class Attention:
     metric, unit, bound, dtype = "sdpa_tflops", "TFLOP/s", "tensor", "bf16"
     B, H, L, D = 4, 32, 2048, 128
     kernel_regex = "sdpa_fwd"
+    profile = "sdpa_fwd_causal_bf16_4x32x2048x128"
     scale = 1.0 / math.sqrt(128)
 
     def describe(self):
@@ -348,6 +354,7 @@ class NormedMatmul:
     metric, unit, bound, dtype = "normed_matmul_tflops", "TFLOP/s", "tensor", "bf16"
     M, K, N = 8192, 4096, 4096
     kernel_regex = "gemm_tc"
+    profile = "gemm_tc_normed_matmul_bf16_8192x4096x4096"
 
     def describe(self):
         return (f"normed matmul (x @ W) * rsqrt(mean(x*x,-1)+1e-5), bf16 x ({self.M},{self.K}), "
@@ -560,7 +567,7 @@ def run_phew(args) -> None:
                    "l2": "inputs larger than L2 or rotated across sets larger than L2",
                    "parallelism": f"replicas x{d.world}"},
         "roofline": {"bound": w.bound, "achieved": achieved, "peak": peak, "unit": w.unit,
-                     "frac": achieved / peak, "traffic": load_traffic(f"{w.name}_traffic"),
+                     "frac": achieved / peak, "traffic": load_traffic(getattr(w, "profile", None)),
                      "peak_source": peaks["source"] + (" (burst)" if w.bound == "tensor" else "")},
         "e2e": {"value": e2e_val, "unit": w.unit, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps},

@@ -54,6 +54,11 @@ uint32 = Dtype("uint32", 4, torch.uint32, "u", None, np.dtype(np.uint32))
 uint64 = Dtype("uint64", 8, torch.uint64, "u", None, np.dtype(np.uint64))
 bool_ = Dtype("bool", 1, torch.bool, "b", None, np.dtype(np.bool_))
 
+# Named for mlx.core compatibility (phew's Dtype.from_mlx table lists them,
+# ir/dtype.py:70-88); arrays of these types are not supported on the GPU.
+float64 = Dtype("float64", 8, torch.float64, "f", None, np.dtype(np.float64))
+complex64 = Dtype("complex64", 8, torch.complex64, "c", None, np.dtype(np.complex64))
+
 ALL = (float32, float16, bfloat16, int8, int16, int32, int64, uint8, uint16, uint32, uint64, bool_)
 _BY_NAME = {d.name: d for d in ALL}
 _BY_NAME["bool_"] = bool_

@@ -35,8 +35,10 @@ from ..dtypes import (  # noqa: F401  (re-exported as mx.float16 ...)
     Dtype,
     bfloat16,
     bool_,
+    complex64,
     float16,
     float32,
+    float64,
     int8,
     int16,
     int32,

@@ -229,6 +229,25 @@ int phew_compare(const void* b, const void* c, int64_t n, int dtype,
                  double atol, double rtol, void* scratch, size_t scratch_bytes,
                  phew_compare_stats* out, void* stream);
 
+/* phew_compare for callers that cannot allocate device memory when they
+ * need a verdict -- code running during CUDA graph capture, inside a host
+ * runtime whose allocator owns the device, or in a context that must not
+ * synchronise the device (cudaMalloc/cudaFree may).  Same inputs, outputs
+ * and result as phew_compare, but the per-block partials live in a
+ * 48 KiB array in this library's own device memory (held by every GPU that
+ * loads the library until the process exits); the call allocates nothing.
+ *   - The first call on each device looks up that array's address on the
+ *     current device (cudaGetSymbolAddress); make that first call before
+ *     any stream capture.
+ *   - Every call shares the one array: calls that overlap on the GPU (for
+ *     instance on two streams at once) race.  Nothing in it needs clearing.
+ *   - Comparisons whose scratch need (phew_compare_scratch_bytes) exceeds
+ *     the array are refused with PHEW_ERR_INVALID.
+ * No counterpart in the reference (its comparison runs in numpy on the
+ * host, verify/checker.py:220-233). */
+int phew_compare_static(const void* b, const void* c, int64_t n, int dtype,
+                        double atol, double rtol, phew_compare_stats* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -47,6 +47,7 @@ EXPORTED_SYMBOLS = (
     "phew_fill",
     "phew_compare_scratch_bytes",
     "phew_compare",
+    "phew_compare_static",
 )
 
 
@@ -134,6 +135,10 @@ _SIGNATURES = {
     "phew_compare_scratch_bytes": ([_i64], ctypes.c_size_t),
     "phew_compare": (
         [_vp, _vp, _i64, _int, ctypes.c_double, ctypes.c_double, _vp, ctypes.c_size_t, _vp, _vp],
+        _int,
+    ),
+    "phew_compare_static": (
+        [_vp, _vp, _i64, _int, ctypes.c_double, ctypes.c_double, _vp, _vp],
         _int,
     ),
 }

@@ -266,3 +266,64 @@ extern "C" int phew_compare(const void* b, const void* c, int64_t n, int dtype, 
     default: return set_error(PHEW_ERR_INVALID, "phew_compare: bad dtype");
   }
 }
+
+// ---------------------------------------------------------------------------
+// phew_compare_static: the same comparison without any allocation.
+//
+// Some callers cannot allocate device memory at the moment they need a
+// verdict: code running while a CUDA graph is being captured (cudaMalloc is
+// not capturable), code inside a host runtime whose allocator owns the whole
+// device (an inference server's pool, where a stray cudaMalloc can fail or
+// fragment it), or a watchdog that checks outputs from a context that must
+// not synchronise the device (cudaMalloc / cudaFree can).  For them the
+// per-block partial results live in one array in this library's own device
+// memory instead of a caller-provided scratch buffer.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace phew {
+namespace {
+// Partials of at most kMaxBlocks blocks: 48 KiB.  Every GPU that loads this
+// library holds the array until the process exits.
+constexpr size_t kStaticScratchBytes =
+    sizeof(StatsPartial) * kMaxBlocks + sizeof(ComparePartial) * kMaxBlocks;
+constexpr int kMaxStaticDevices = 256;
+std::mutex g_static_mu;
+void* g_static_scratch[kMaxStaticDevices] = {};
+}  // namespace
+}  // namespace phew
+
+static __device__ __align__(256) unsigned char g_compare_static_scratch[phew::kStaticScratchBytes];
+
+extern "C" int phew_compare_static(const void* b, const void* c, int64_t n, int dtype,
+                                   double atol, double rtol, phew_compare_stats* out,
+                                   void* stream) {
+  int dev = 0;
+  PHEW_CHECK_CUDA(cudaGetDevice(&dev));
+  PHEW_REQUIRE(dev >= 0 && dev < kMaxStaticDevices, "phew_compare_static: device index out of range");
+  const size_t need = phew_compare_scratch_bytes(n);
+  if (need > kStaticScratchBytes)
+    return set_error(PHEW_ERR_INVALID,
+                     "phew_compare_static: this comparison needs " + std::to_string(need) +
+                         " bytes of scratch but the static array holds " +
+                         std::to_string(kStaticScratchBytes) + "; use phew_compare");
+  void* scratch = nullptr;
+  {
+    // First call on each device: translate the array's symbol into this
+    // device's address (with the device current).  A host-side reference to
+    // g_compare_static_scratch is only a stand-in, never a device address.
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    if (g_static_scratch[dev] == nullptr) {
+      void* p = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&p, g_compare_static_scratch);
+      if (e != cudaSuccess || p == nullptr)
+        return set_error(PHEW_ERR_CUDA, std::string("phew_compare_static: cudaGetSymbolAddress: ") +
+                                            cudaGetErrorString(e));
+      g_static_scratch[dev] = p;
+    }
+    scratch = g_static_scratch[dev];
+  }
+  // Nothing in the array needs clearing: each call writes every partial it
+  // later reads.
+  return phew_compare(b, c, n, dtype, atol, rtol, scratch, kStaticScratchBytes, out, stream);
+}

@@ -12,13 +12,14 @@
 // [N, K] (K contiguous: a K-major operand, `b_layout = 1`, e.g. k.T in q @ k.T).
 // Batches are strided; a zero batch stride broadcasts the operand.
 //
-// One CTA computes one BM x BN tile (BM = 128, BN = 128 or 256):
+// One CTA computes one (MT x 128) x BN tile (BN = 128 or 256, MT = 1 or 2):
 //   warp 0      TMA producer: 128B-swizzled tiles of A and B into a STAGES-deep
 //               shared-memory ring (no cluster multicast: these kernels also run
 //               in multi-GPU jobs)
 //   warp 1      allocates TMEM, one elected lane issues tcgen05.mma (M=128,
-//               N=BN, K=16) into a TMEM fp32 accumulator and commits each stage
-//               back to the producer
+//               N=BN, K=16) into MT TMEM fp32 accumulators (one per 128 rows,
+//               all sharing the stage's B tile) and commits each stage back to
+//               the producer
 //   warps 2-5   epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
 //               32*(w%4)..), scale, convert, store; with the fused row scale they
 //               also accumulate each row's sum of squares from the A tiles while
@@ -36,13 +37,16 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // 64 x 16-bit = one 128-byte swizzle row
 constexpr int kNumThreads = 192;
 
-template <int BN> struct Cfg {
-  static constexpr int A_BYTES = BM * BK * 2;
+// A CTA computes MT x 128 rows by BN columns: MT accumulators of 128 x BN in
+// TMEM that share every B tile (MT = 2 halves the B bytes per MMA).
+template <int BN, int MT> struct Cfg {
+  static constexpr int ROWS = BM * MT;
+  static constexpr int A_BYTES = ROWS * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (200 * 1024) / STAGE_BYTES;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
-  static constexpr int TMEM_COLS = BN;
+  static constexpr int TMEM_COLS = BN * MT;
 };
 
 struct Params {
@@ -76,11 +80,11 @@ __device__ __forceinline__ void store_row32(T* dst, const float* v, int ncols) {
   }
 }
 
-template <int BN, bool BF16>
+template <int BN, int MT, bool BF16>
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const Params p) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, MT>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
@@ -91,7 +95,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BN;
-  const int m0 = blockIdx.y * BM;
+  const int m0 = blockIdx.y * C::ROWS;
   const int bz = blockIdx.z;
   const int num_kb = (p.K + BK - 1) / BK;
 
@@ -154,10 +158,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const uint32_t sb = sa + C::A_BYTES;
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
-          const uint64_t ad = smem_desc(sa + kk * 32, 16, 1024);
           const uint64_t bd = p.b_mn_major ? smem_desc(sb + kk * (16 * 128), 64 * BK * 2, 1024)
                                            : smem_desc(sb + kk * 32, 16, 1024);
-          mma_ss(tmem, ad, bd, idesc_b, (kb > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+          for (int h = 0; h < MT; ++h) {
+            // rows h*128.. of the A tile start h*128*128 bytes in (1024-aligned)
+            const uint64_t ad = smem_desc(sa + h * (BM * 128) + kk * 32, 16, 1024);
+            mma_ss(tmem + h * BN, ad, bd, idesc_b, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
         }
         commit(&empty[s]);
       }
@@ -166,8 +174,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     const int quarter = warp & 3;
-    const int row_in_tile = quarter * 32 + lane;
-    float ss = 0.f;
+    float ss[MT];
+#pragma unroll
+    for (int h = 0; h < MT; ++h) ss[h] = 0.f;
     if (p.row_scale) {
       for (int kb = 0; kb < num_kb && ok; ++kb) {
         const int s = kb % C::STAGES;
@@ -178,20 +187,24 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         // A row r occupies bytes [r*128, r*128+128) of the tile; the 128B
         // swizzle only permutes 16-byte chunks within the row.
-        const uint4* row = reinterpret_cast<const uint4*>(smem + s * C::STAGE_BYTES + row_in_tile * 128);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint4 raw = row[c];
-          const uint16_t* h = reinterpret_cast<const uint16_t*>(&raw);
+        for (int h = 0; h < MT; ++h) {
+          const int r = h * BM + quarter * 32 + lane;
+          const uint4* row = reinterpret_cast<const uint4*>(smem + s * C::STAGE_BYTES + r * 128);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            float x;
-            if (BF16) {
-              x = __uint_as_float(static_cast<uint32_t>(h[i]) << 16);
-            } else {
-              asm("cvt.f32.f16 %0, %1;" : "=f"(x) : "h"(h[i]));
+          for (int c = 0; c < 8; ++c) {
+            const uint4 raw = row[c];
+            const uint16_t* hv = reinterpret_cast<const uint16_t*>(&raw);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              float x;
+              if (BF16) {
+                x = __uint_as_float(static_cast<uint32_t>(hv[i]) << 16);
+              } else {
+                asm("cvt.f32.f16 %0, %1;" : "=f"(x) : "h"(hv[i]));
+              }
+              ss[h] = fmaf(x, x, ss[h]);
             }
-            ss = fmaf(x, x, ss);
           }
         }
         // The next TMA write into this stage must be ordered after these
@@ -203,16 +216,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     }
     if (ok && !mbar_wait(accum_full, 0, p.error_flag)) ok = false;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (ok) {
-      const float scale = p.row_scale ? 1.0f / sqrtf(ss / static_cast<float>(p.K) + p.eps) : 1.0f;
-      const int row = m0 + row_in_tile;
+    for (int h = 0; h < MT && ok; ++h) {
+      const float scale = p.row_scale ? 1.0f / sqrtf(ss[h] / static_cast<float>(p.K) + p.eps) : 1.0f;
+      const int row = m0 + h * BM + quarter * 32 + lane;
       const long long cbase = static_cast<long long>(bz) * p.c_batch_stride + static_cast<long long>(row) * p.ldc;
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         float v[32];
         {
           uint32_t r[32];
-          tmem_ld32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + c, r);
+          tmem_ld32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + h * BN + c, r);
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
@@ -223,7 +236,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             for (int i = 0; i < 32; ++i) v[i] *= scale;
           } else if (p.row_scale == 2) {  // diagnostic: the row's sum of squares
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = ss;
+            for (int i = 0; i < 32; ++i) v[i] = ss[h];
           }
           const int ncols = p.N - (n0 + c);
           if (p.out_dtype == PHEW_BF16)
@@ -301,13 +314,13 @@ int make_map(CUtensorMap* tm, const void* base, bool bf16, uint64_t d0, uint64_t
   return make_map_16bit(tm, base, bf16, 3, dims, strides, box);
 }
 
-template <int BN, bool BF16>
+template <int BN, int MT, bool BF16>
 int launch_tc(const void* A, const void* B, const Params& p, long long lda, long long ldb,
               long long sa, long long sb, cudaStream_t st) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, MT>;
   CUtensorMap ta, tb;
   const uint64_t nba = p.a_batched ? p.batch : 1, nbb = p.b_batched ? p.batch : 1;
-  int s = make_map(&ta, A, BF16, p.K, p.M, nba, lda * 2, (p.a_batched ? sa : (long long)p.M * lda) * 2, BK, BM);
+  int s = make_map(&ta, A, BF16, p.K, p.M, nba, lda * 2, (p.a_batched ? sa : (long long)p.M * lda) * 2, BK, C::ROWS);
   if (s) return s;
   if (p.b_mn_major)
     s = make_map(&tb, B, BF16, p.N, p.K, nbb, ldb * 2, (p.b_batched ? sb : (long long)p.K * ldb) * 2, 64, BK);
@@ -316,12 +329,12 @@ int launch_tc(const void* A, const void* B, const Params& p, long long lda, long
   if (s) return s;
   static bool attr_set = false;
   if (!attr_set) {
-    PHEW_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, BF16>,
+    PHEW_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, MT, BF16>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr_set = true;
   }
-  dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, p.batch);
-  gemm_tc_kernel<BN, BF16><<<grid, kNumThreads, C::SMEM, st>>>(ta, tb, p);
+  dim3 grid((p.N + BN - 1) / BN, (p.M + C::ROWS - 1) / C::ROWS, p.batch);
+  gemm_tc_kernel<BN, MT, BF16><<<grid, kNumThreads, C::SMEM, st>>>(ta, tb, p);
   return launch_status("gemm_tc_kernel");
 }
 
@@ -367,10 +380,15 @@ extern "C" int phew_gemm(const void* A, const void* B, void* Cout, int64_t M, in
       (stride_b * 2) % 16 == 0 && K > 0;
   if (aligned16 && in_dtype != PHEW_F32) {
     const bool bf = in_dtype == PHEW_BF16;
-    if (N <= 128) return bf ? launch_tc<128, true>(A, B, p, lda, ldb, stride_a, stride_b, st)
-                            : launch_tc<128, false>(A, B, p, lda, ldb, stride_a, stride_b, st);
-    return bf ? launch_tc<256, true>(A, B, p, lda, ldb, stride_a, stride_b, st)
-              : launch_tc<256, false>(A, B, p, lda, ldb, stride_a, stride_b, st);
+    // Tile choice: 128 x 128 for narrow outputs; 256 x 256 (two 128-row
+    // accumulators sharing each B tile: 64 operand bytes per MMA cycle
+    // instead of 96) when both M and N exceed 128, else 128 x 256.
+    if (N <= 128) return bf ? launch_tc<128, 1, true>(A, B, p, lda, ldb, stride_a, stride_b, st)
+                            : launch_tc<128, 1, false>(A, B, p, lda, ldb, stride_a, stride_b, st);
+    if (M > 128) return bf ? launch_tc<256, 2, true>(A, B, p, lda, ldb, stride_a, stride_b, st)
+                           : launch_tc<256, 2, false>(A, B, p, lda, ldb, stride_a, stride_b, st);
+    return bf ? launch_tc<256, 1, true>(A, B, p, lda, ldb, stride_a, stride_b, st)
+              : launch_tc<256, 1, false>(A, B, p, lda, ldb, stride_a, stride_b, st);
   }
   dim3 grid(static_cast<unsigned>((N + 15) / 16), static_cast<unsigned>((M + 15) / 16),
             static_cast<unsigned>(batch));

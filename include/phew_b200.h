@@ -171,7 +171,8 @@ int phew_sdpa_supported(int64_t L, int64_t D, int dtype);
  * [L, D] slices stored contiguously ([B*H, L, D], D contiguous).  S = QK^T and
  * O += PV run on tcgen05 with TMEM accumulators; the softmax (running max with
  * lazy rescaling, exp2) runs between them on the CUDA cores; scores never
- * reach HBM.  causal = 1 masks key j > query i.  error_flag as in phew_gemm.
+ * reach HBM.  causal = 1 masks key j > query i.  scale must be positive
+ * (PHEW_ERR_INVALID otherwise).  error_flag as in phew_gemm.
  * Replaces mx.fast.scaled_dot_product_attention(q, k, v, scale=)
  * (emit/codegen.py:421-426; FastScaledDotProductAttention ir/ops.py:182-187,
  * produced by rules/primitive_subst.py:413-499). */

@@ -184,8 +184,8 @@ def scaled_dot_product_attention(q, k, v, *, scale=1.0, mask=None) -> array:
 
     q, k, v: [B, H, L, D].  ``mask`` None (no mask), ``"causal"`` or an
     additive array broadcastable to [B, H, L, S].  The fused tcgen05 kernel
-    runs for D = 128, L = S multiple of 128, bf16/fp16, equal head counts and
-    mask None / "causal"; any other case is composed from this backend's GEMM
+    runs for D = 128, L = S multiple of 128, bf16/fp16, equal head counts,
+    scale > 0 and mask None / "causal"; any other case is composed from this backend's GEMM
     and softmax kernels (scores materialised in HBM).
     """
     from .mx.core import astype, softmax, swapaxes
@@ -199,7 +199,7 @@ def scaled_dot_product_attention(q, k, v, *, scale=1.0, mask=None) -> array:
     fast_ok = (
         q.ndim == 4 and q.shape == k.shape == v.shape and q.dtype is k.dtype is v.dtype
         and q.dtype.name in ("bfloat16", "float16") and q.shape[-1] == 128
-        and q.shape[-2] % 128 == 0 and (mask is None or causal)
+        and q.shape[-2] % 128 == 0 and (mask is None or causal) and float(scale) > 0.0
     )
     if fast_ok:
         B, H, L, D = q.shape

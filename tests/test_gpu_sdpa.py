@@ -45,7 +45,8 @@ def check(got, ref, v=None):
 
 @pytest.mark.parametrize("dtype", [BF16, np.float16])
 @pytest.mark.parametrize("causal", [True, False])
-@pytest.mark.parametrize("shape", [(1, 1, 128, 128), (2, 3, 512, 128), (1, 2, 1024, 128)])
+@pytest.mark.parametrize("shape", [(1, 1, 128, 128), (1, 2, 384, 128), (2, 3, 512, 128),
+                                   (1, 1, 640, 128), (1, 2, 1024, 128)])
 def test_sdpa_fused(mx, dtype, causal, shape):
     rng = np.random.default_rng(shape[2] + causal)
     q, k, v = _qkv(rng, shape, dtype)
@@ -67,6 +68,43 @@ def test_sdpa_large_logits(mx):
                                                mask="causal")
     ref = mlx_cpu.sdpa(mlx_cpu.array(q), mlx_cpu.array(k), mlx_cpu.array(v), 0.3, "causal")
     check(got, ref, v)
+
+
+def test_sdpa_nan_rows_and_keys(mx):
+    """A NaN query element gives a NaN output row; a NaN key element poisons
+    every row that sees that key (all rows without a mask, the rows at or
+    after it with the causal mask)."""
+    rng = np.random.default_rng(8)
+    shape = (1, 2, 512, 128)
+    for causal in (True, False):
+        q, k, v = _qkv(rng, shape, BF16)
+        q[0, 0, 37, 5] = np.nan
+        k[0, 1, 300, 17] = np.nan
+        mask = "causal" if causal else None
+        got = np.asarray(mx.fast.scaled_dot_product_attention(
+            mx.array(q), mx.array(k), mx.array(v), scale=1 / math.sqrt(128), mask=mask)).astype(np.float32)
+        ref = np.asarray(mlx_cpu.sdpa(mlx_cpu.array(q), mlx_cpu.array(k), mlx_cpu.array(v),
+                                      1 / math.sqrt(128), mask)).astype(np.float32)
+        assert np.array_equal(np.isnan(got), np.isnan(ref))
+        assert np.isnan(got[0, 0, 37]).all() and np.isfinite(got[0, 0, 36]).all()
+        assert np.isnan(got[0, 1, 300]).all()
+        assert np.isfinite(got[0, 1, 299]).all() == causal
+        fin = np.isfinite(ref)
+        check(np.where(fin, got, 0), np.where(fin, ref, 0), v)
+
+
+def test_sdpa_nonpositive_scale_uses_composed_path(mx):
+    rng = np.random.default_rng(9)
+    shape = (1, 1, 256, 128)
+    q, k, v = _qkv(rng, shape, BF16)
+    # The composed path rounds the scores to bf16 before the softmax (as the
+    # unsubstituted graph does); small |scale| keeps that rounding inside the
+    # tolerance of the float32 oracle.
+    for scale in (0.0, -0.05):
+        got = mx.fast.scaled_dot_product_attention(mx.array(q), mx.array(k), mx.array(v), scale=scale,
+                                                   mask="causal")
+        ref = mlx_cpu.sdpa(mlx_cpu.array(q), mlx_cpu.array(k), mlx_cpu.array(v), scale, "causal")
+        check(got, ref, v)
 
 
 def test_sdpa_composed_fallback(mx):

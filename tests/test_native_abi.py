@@ -64,3 +64,15 @@ def test_compare_scratch_is_bounded(lib):
     small = lib.phew_compare_scratch_bytes(ctypes.c_int64(10))
     big = lib.phew_compare_scratch_bytes(ctypes.c_int64(1 << 40))
     assert 0 < small == big <= 1 << 20
+
+
+def test_sdpa_rejects_nonpositive_scale(lib):
+    from phew_b200 import _native
+
+    fake = ctypes.c_void_p(256)  # never dereferenced: the check runs first
+    for scale in (0.0, -0.5):
+        st = lib.phew_sdpa(fake, fake, fake, fake, ctypes.c_int64(1), ctypes.c_int64(128),
+                           ctypes.c_int64(128), ctypes.c_float(scale), 1, _native.PHEW_BF16,
+                           None, None)
+        assert st == _native.PHEW_ERR_INVALID
+        assert "scale must be positive" in _native.last_error()

@@ -16,20 +16,21 @@
 // after both P V products, so the next loads start early.
 //
 //   warp 0      TMA: Q_a, Q_b once, then K_j and V_j (128B-swizzled, no multicast)
-//   warp 1      TMEM owner + MMA issuer, per key tile j:
-//                 O_a += P_a V_j, O_b += P_b V_j        (P from TMEM)
-//                 S_a  = Q_a K_{j+1}^T, S_b = Q_b K_{j+1}^T
-//               so the softmax of one query tile overlaps the products of
-//               the other, and each wait for a finished product is covered
-//               by the other tile's product still running.
+//   warp 1      TMEM owner + MMA issuer.  Per key tile j and query tile t:
+//                 O_t += P_t V_j, then (once that product has read P_t out of
+//                 S_t) S_t = Q_t K_{j+1}^T, so the softmax of tile a runs
+//                 while the tensor pipe works for tile b and the other way
+//                 round.
 //   warps 2-5   softmax of tile a, warps 6-9 softmax of tile b, one query row
 //               per thread: masked row max, running max with lazy rescaling
 //               (O and the row sum are rescaled only when the max grows by
 //               more than 2^8), P = exp2(S*scale*log2e - max) written back over
 //               S as packed 16-bit pairs, and the final O / rowsum epilogue.
-//               A quarter of the exponentials run on the FMA pipe (a cubic
-//               for 2^f after rounding off the integer part) so that the
-//               transcendental unit is not the limit.
+//               Past the first key tile P is computed against the running
+//               max while the tile max is still being reduced, and redone in
+//               the rare case that the max grew past the threshold.  The
+//               scale/shift and the row sum run on pairs of scores (packed
+//               f32x2 FMA), so each warp issues fewer instructions per score.
 //
 // TMEM (512 columns): S_a 0..127, S_b 128..255, O_a 256..383, O_b 384..511.
 // All waits are bounded; a wait that runs out sets *error_flag and the CTA
@@ -63,29 +64,39 @@ struct Params {
   int* error_flag;
 };
 
+// ---- scalar and packed (f32x2) arithmetic helpers ----
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-
-// 2^x on the FMA pipe for x <= 8: x = j + f with j = round(x) and f in
-// [-0.5, 0.5]; 2^f by a cubic whose coefficients minimise the relative error
-// on that interval (fitted by iteratively reweighted least squares; max
-// relative error 7.5e-5, below half an ulp of the 16-bit P it feeds), times
-// 2^j built in the exponent field.  Adding 1.5 * 2^23 rounds x to an integer
-// held in the low mantissa bits (1.5 * 2^23 has zero low bits, so the
-// exponent field of 2^j is (bits(t) + 127) << 23).  x is clamped at -127,
-// where 2^j becomes +0: masked (-inf) scores give exactly 0, as the
-// flush-to-zero ex2.approx does; NaN passes through the clamp and the product.
-__device__ __forceinline__ float ex2_fma(float x) {
-  x = x < -127.0f ? -127.0f : x;
-  const float t = __fadd_rn(x, 12582912.0f);
-  const float f = __fsub_rn(x, __fsub_rn(t, 12582912.0f));
-  float p = fmaf(0.0551716648f, f, 0.242611125f);
-  p = fmaf(p, f, 0.693260968f);
-  p = fmaf(p, f, 0.999928057f);
-  return p * __int_as_float((__float_as_int(t) + 127) << 23);
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float lo_of(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ float hi_of(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// max(a, b, c), NaN if any operand is NaN (a NaN score must poison its row).
+__device__ __forceinline__ float max3n(float a, float b, float c) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float max2n(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
 }
 
 template <bool BF16>
@@ -96,6 +107,46 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   else
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
   return d;
+}
+
+// P = exp2(raw * c - m) over one row of 128 scores, packed into 64 16-bit
+// pairs and stored to TMEM at s_addr (columns 0..63 of the S buffer).
+// Returns the row sum of this tile's (unrounded) P.
+template <bool BF16>
+__device__ __forceinline__ float compute_p(const uint32_t* raw, float c, float m, uint32_t s_addr) {
+  const uint64_t c2 = f2(c, c), nm2 = f2(-m, -m);
+  uint64_t l2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    uint32_t pk[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int pi = 16 * h + i;
+      const uint64_t x = fma2(f2(__uint_as_float(raw[2 * pi]), __uint_as_float(raw[2 * pi + 1])), c2, nm2);
+      const uint64_t e = f2(ex2(lo_of(x)), ex2(hi_of(x)));
+      l2[i & 1] = add2(l2[i & 1], e);
+      pk[i] = pack2<BF16>(lo_of(e), hi_of(e));
+    }
+    tmem_st16(s_addr + 16 * h, pk);
+  }
+  const uint64_t l = add2(l2[0], l2[1]);
+  return lo_of(l) + hi_of(l);
+}
+
+// max over 128 scores: eight independent chains of three-input max.
+__device__ __forceinline__ float row_max(const uint32_t* raw) {
+  float m8[8];
+#pragma unroll
+  for (int a = 0; a < 8; ++a)
+    m8[a] = max3n(__uint_as_float(raw[3 * a]), __uint_as_float(raw[3 * a + 1]), __uint_as_float(raw[3 * a + 2]));
+#pragma unroll
+  for (int i = 24; i + 16 <= 128; i += 16)
+#pragma unroll
+    for (int a = 0; a < 8; ++a)
+      m8[a] = max3n(m8[a], __uint_as_float(raw[i + 2 * a]), __uint_as_float(raw[i + 2 * a + 1]));
+#pragma unroll
+  for (int a = 0; a < 8; ++a) m8[a] = max2n(m8[a], __uint_as_float(raw[120 + a]));
+  return max3n(max3n(m8[0], m8[1], m8[2]), max3n(m8[3], m8[4], m8[5]), max2n(m8[6], m8[7]));
 }
 
 template <bool BF16>
@@ -184,39 +235,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t id_qk = instr_desc_f16(BF16 ? 1 : 0, 0, BQ, BKV);
       constexpr uint32_t id_pv = instr_desc_f16(BF16 ? 1 : 0, 1, BQ, D);
-      // S_t = Q_t K_j^T for every tile that still needs key tile j.
-      auto issue_s = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(&k_full[s], (j >> 1) & 1, p.error_flag)) return false;
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t k_addr = smem_u32(sK + s * TILE_BYTES);
+      auto issue_s = [&](int t, uint32_t k_addr) {
+        const uint32_t q_addr = smem_u32(sQ + t * TILE_BYTES);
 #pragma unroll
-        for (int t = 0; t < QT; ++t) {
-          if (j >= (t == 0 ? n_kv_a : n_kv_b)) continue;
-          // S_t still holds P_t of tile j-1 until O_t += P_t V_{j-1} is done.
-          if (j > 0 && !mbar_wait(&o_done[t], (j - 1) & 1, p.error_flag)) return false;
-          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t q_addr = smem_u32(sQ + t * TILE_BYTES);
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
-            mma_ss(tmem + S_COL + t * 128, smem_desc(q_addr + off, 16, 1024),
-                   smem_desc(k_addr + off, 16, 1024), id_qk, kk > 0 ? 1u : 0u);
-          }
-          commit(&s_full[t]);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
+          mma_ss(tmem + S_COL + t * 128, smem_desc(q_addr + off, 16, 1024),
+                 smem_desc(k_addr + off, 16, 1024), id_qk, kk > 0 ? 1u : 0u);
         }
-        commit(&k_empty[s]);
-        return true;
+        commit(&s_full[t]);
       };
-      if (!mbar_wait(q_full, 0, p.error_flag)) ok = false;
-      if (ok) ok = issue_s(0);
+      if (!mbar_wait(q_full, 0, p.error_flag) || !mbar_wait(&k_full[0], 0, p.error_flag)) ok = false;
+      if (ok) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        for (int t = 0; t < n_tiles; ++t) issue_s(t, smem_u32(sK));
+        commit(&k_empty[0]);
+      }
       for (int j = 0; j < n_kv_max && ok; ++j) {
-        const int s = j & 1;
+        const int s = j & 1, s1 = (j + 1) & 1;
+        const bool more = j + 1 < n_kv_max;
         if (!mbar_wait(&v_full[s], (j >> 1) & 1, p.error_flag)) { ok = false; break; }
+        if (more && !mbar_wait(&k_full[s1], ((j + 1) >> 1) & 1, p.error_flag)) { ok = false; break; }
         const uint32_t v_addr = smem_u32(sV + s * TILE_BYTES);
+        const uint32_t k_addr = smem_u32(sK + s1 * TILE_BYTES);
 #pragma unroll
         for (int t = 0; t < QT; ++t) {
-          if (!ok || j >= (t == 0 ? n_kv_a : n_kv_b)) continue;
+          const int nk = t == 0 ? n_kv_a : n_kv_b;
+          if (!ok || j >= nk) continue;
           if (!mbar_wait(&p_full[t], j & 1, p.error_flag)) { ok = false; continue; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
@@ -227,10 +272,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                    (j > 0 || kk > 0) ? 1u : 0u);
           }
           commit(&o_done[t]);
+          if (j + 1 < nk) {
+            // S_t holds P_t until this product has read it.
+            if (!mbar_wait(&o_done[t], j & 1, p.error_flag)) { ok = false; continue; }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            issue_s(t, k_addr);
+          }
         }
         if (!ok) break;
         commit(&v_empty[s]);
-        if (j + 1 < n_kv_max) ok = issue_s(j + 1);
+        if (more) commit(&k_empty[s1]);
       }
     }
   } else {
@@ -258,49 +309,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 128; ++i)
           if (i > row) raw[i] = __float_as_uint(-INFINITY);
       }
-      // The row max over unscaled scores (scale > 0), then scaled.
-      float mx = __uint_as_float(raw[0]);
-#pragma unroll
-      for (int i = 1; i < 128; ++i) mx = fmaxf(mx, __uint_as_float(raw[i]));
-      const float m_tile = mx * c;
-      // Lazy rescaling: keep the reference max unless the row max grew by
-      // more than 2^kRescaleThreshold (or this is the first tile).
-      float alpha = 1.f;
+      float tile_sum;
       bool rescale = false;
+      float alpha = 1.f;
       if (j == 0) {
-        m_ref = m_tile;
-      } else if (m_tile > m_ref + kRescaleThreshold) {
-        alpha = ex2(m_ref - m_tile);
-        m_ref = m_tile;
-        rescale = true;
-      }
-      l *= alpha;
-      const float neg_m = -m_ref;
-      // P in two halves of 64 keys (32 packed columns each), so that only
-      // 32 packed registers are live beside the scores.
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float x0 = fmaf(__uint_as_float(raw[64 * h + 2 * i]), c, neg_m);
-          const float x1 = fmaf(__uint_as_float(raw[64 * h + 2 * i + 1]), c, neg_m);
-          float e0, e1;
-          if ((i & 3) == 3) {
-            e0 = ex2_fma(x0);
-            e1 = ex2_fma(x1);
-          } else {
-            e0 = ex2(x0);
-            e1 = ex2(x1);
-          }
-          l += e0 + e1;
-          pk[i] = pack2<BF16>(e0, e1);
+        m_ref = row_max(raw) * c;  // raw scores are unscaled; scale > 0
+        tile_sum = compute_p<BF16>(raw, c, m_ref, s_addr);
+      } else {
+        // P against the running max while the tile max is reduced; the max
+        // only decides whether this tile must be redone.
+        tile_sum = compute_p<BF16>(raw, c, m_ref, s_addr);
+        const float m_tile = row_max(raw) * c;
+        // Lazy rescaling: keep the running max unless the tile max exceeds
+        // it by more than 2^kRescaleThreshold; a NaN max (a NaN score)
+        // takes this path too and turns the whole row NaN.
+        if (!(m_tile <= m_ref + kRescaleThreshold)) {
+          alpha = ex2(m_ref - m_tile);
+          m_ref = m_tile;
+          rescale = true;
         }
-        tmem_st32(s_addr + 32 * h, pk);
       }
       if (__any_sync(0xffffffffu, rescale)) {
-        // O_t holds the products of tiles 0..j-1: wait for the last one.
-        // (Done after P is written, when the scores are no longer live.)
+        // Redo P with the new max (rows that kept theirs recompute the same
+        // values), then scale O_t, which holds the products of tiles
+        // 0..j-1: wait for the last one first.
+        tmem_st_wait();
+        tile_sum = compute_p<BF16>(raw, c, m_ref, s_addr);
         if (!mbar_wait(&o_done[t], (j - 1) & 1, p.error_flag)) ok = false;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         if (ok) {
@@ -315,6 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      l = fmaf(l, alpha, tile_sum);
       tmem_st_wait();
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();

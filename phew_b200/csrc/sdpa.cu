@@ -87,15 +87,11 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
-// max(a, b, c), NaN if any operand is NaN (a NaN score must poison its row).
-__device__ __forceinline__ float max3n(float a, float b, float c) {
+// max(a, b, c); like fmaxf a NaN operand is ignored.  (A NaN score still
+// poisons its row: exp2 of it is NaN and so is the row sum.)
+__device__ __forceinline__ float max3(float a, float b, float c) {
   float d;
-  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-__device__ __forceinline__ float max2n(float a, float b) {
-  float d;
-  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
 }
 
@@ -138,15 +134,15 @@ __device__ __forceinline__ float row_max(const uint32_t* raw) {
   float m8[8];
 #pragma unroll
   for (int a = 0; a < 8; ++a)
-    m8[a] = max3n(__uint_as_float(raw[3 * a]), __uint_as_float(raw[3 * a + 1]), __uint_as_float(raw[3 * a + 2]));
+    m8[a] = max3(__uint_as_float(raw[3 * a]), __uint_as_float(raw[3 * a + 1]), __uint_as_float(raw[3 * a + 2]));
 #pragma unroll
   for (int i = 24; i + 16 <= 128; i += 16)
 #pragma unroll
     for (int a = 0; a < 8; ++a)
-      m8[a] = max3n(m8[a], __uint_as_float(raw[i + 2 * a]), __uint_as_float(raw[i + 2 * a + 1]));
+      m8[a] = max3(m8[a], __uint_as_float(raw[i + 2 * a]), __uint_as_float(raw[i + 2 * a + 1]));
 #pragma unroll
-  for (int a = 0; a < 8; ++a) m8[a] = max2n(m8[a], __uint_as_float(raw[120 + a]));
-  return max3n(max3n(m8[0], m8[1], m8[2]), max3n(m8[3], m8[4], m8[5]), max2n(m8[6], m8[7]));
+  for (int a = 0; a < 8; ++a) m8[a] = fmaxf(m8[a], __uint_as_float(raw[120 + a]));
+  return max3(max3(m8[0], m8[1], m8[2]), max3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
 }
 
 template <bool BF16>
@@ -321,9 +317,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tile_sum = compute_p<BF16>(raw, c, m_ref, s_addr);
         const float m_tile = row_max(raw) * c;
         // Lazy rescaling: keep the running max unless the tile max exceeds
-        // it by more than 2^kRescaleThreshold; a NaN max (a NaN score)
-        // takes this path too and turns the whole row NaN.
-        if (!(m_tile <= m_ref + kRescaleThreshold)) {
+        // it by more than 2^kRescaleThreshold.
+        if (m_tile > m_ref + kRescaleThreshold) {
           alpha = ex2(m_ref - m_tile);
           m_ref = m_tile;
           rescale = true;

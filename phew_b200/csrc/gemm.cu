@@ -178,6 +178,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll
     for (int h = 0; h < MT; ++h) ss[h] = 0.f;
     if (p.row_scale) {
+      // Sum of squares of this warp's 32 rows (per 128-row half), read
+      // cooperatively: in read i, lanes 8g..8g+7 cover the 128-byte row
+      // 4i+g, 16 bytes each, so every read instruction touches 4 whole rows
+      // and no two lanes of a phase share a bank.  The order within a row
+      // does not matter, so the 128B swizzle needs no undoing.
+      float part[MT][8];
+#pragma unroll
+      for (int h = 0; h < MT; ++h)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) part[h][i] = 0.f;
       for (int kb = 0; kb < num_kb && ok; ++kb) {
         const int s = kb % C::STAGES;
         const uint32_t ph = (kb / C::STAGES) & 1;
@@ -185,25 +195,22 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           ok = false;
           break;
         }
-        // A row r occupies bytes [r*128, r*128+128) of the tile; the 128B
-        // swizzle only permutes 16-byte chunks within the row.
 #pragma unroll
         for (int h = 0; h < MT; ++h) {
-          const int r = h * BM + quarter * 32 + lane;
-          const uint4* row = reinterpret_cast<const uint4*>(smem + s * C::STAGE_BYTES + r * 128);
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const uint4 raw = row[c];
+          for (int i = 0; i < 8; ++i) {
+            const int r = h * BM + quarter * 32 + 4 * i + (lane >> 3);
+            const uint4 raw = *reinterpret_cast<const uint4*>(smem + s * C::STAGE_BYTES + r * 128 + (lane & 7) * 16);
             const uint16_t* hv = reinterpret_cast<const uint16_t*>(&raw);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
+            for (int e = 0; e < 8; ++e) {
               float x;
               if (BF16) {
-                x = __uint_as_float(static_cast<uint32_t>(hv[i]) << 16);
+                x = __uint_as_float(static_cast<uint32_t>(hv[e]) << 16);
               } else {
-                asm("cvt.f32.f16 %0, %1;" : "=f"(x) : "h"(hv[i]));
+                asm("cvt.f32.f16 %0, %1;" : "=f"(x) : "h"(hv[e]));
               }
-              ss[h] = fmaf(x, x, ss[h]);
+              part[h][i] = fmaf(x, x, part[h][i]);
             }
           }
         }
@@ -212,6 +219,22 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
+      }
+      // Reduce over the 8 lanes that share a row, then give lane R the sum
+      // of row R (held by lanes 8 * (R % 4).., read i = R / 4).
+#pragma unroll
+      for (int h = 0; h < MT; ++h) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          part[h][i] += __shfl_xor_sync(0xffffffffu, part[h][i], 1);
+          part[h][i] += __shfl_xor_sync(0xffffffffu, part[h][i], 2);
+          part[h][i] += __shfl_xor_sync(0xffffffffu, part[h][i], 4);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float v = __shfl_sync(0xffffffffu, part[h][i], 8 * (lane & 3));
+          if ((lane >> 2) == i) ss[h] = v;
+        }
       }
     }
     if (ok && !mbar_wait(accum_full, 0, p.error_flag)) ok = false;

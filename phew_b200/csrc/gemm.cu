@@ -14,8 +14,8 @@
 //
 // One CTA computes one (MT x 128) x BN tile (BN = 128 or 256, MT = 1 or 2):
 //   warp 0      TMA producer: 128B-swizzled tiles of A and B into a STAGES-deep
-//               shared-memory ring (no cluster multicast: these kernels also run
-//               in multi-GPU jobs)
+//               shared-memory ring; each CTA loads its own tiles (these
+//               kernels also run in multi-GPU jobs)
 //   warp 1      allocates TMEM, one elected lane issues tcgen05.mma (M=128,
 //               N=BN, K=16) into MT TMEM fp32 accumulators (one per 128 rows,
 //               all sharing the stage's B tile) and commits each stage back to

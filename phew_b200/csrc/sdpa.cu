@@ -15,7 +15,8 @@
 // released as soon as both S products that read it are done, a value tile
 // after both P V products, so the next loads start early.
 //
-//   warp 0      TMA: Q_a, Q_b once, then K_j and V_j (128B-swizzled, no multicast)
+//   warp 0      TMA: Q_a, Q_b once, then K_j and V_j (128B-swizzled, each CTA
+//               loading its own tiles)
 //   warp 1      TMEM owner + MMA issuer.  Per key tile j and query tile t:
 //                 O_t += P_t V_j, then (once that product has read P_t out of
 //                 S_t) S_t = Q_t K_{j+1}^T, so the softmax of tile a runs

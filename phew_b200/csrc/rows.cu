@@ -127,6 +127,19 @@ __global__ void rms_norm_loop_kernel(const T* __restrict__ x, const T* __restric
 // ---------------------------------------------------------------------------
 // softmax over the last axis: y = exp(x - max) / sum(exp(x - max))
 // ---------------------------------------------------------------------------
+// For 16-bit rows the exponential is the hardware 2^x of (x - max) * log2(e)
+// and the division a multiply by the row's reciprocal sum: both err by a few
+// fp32 ulps, far below half an ulp of the 16-bit result, and they keep the
+// kernel at the HBM rate instead of the cost of the IEEE exp and division
+// (which fp32 rows keep).
+template <typename T>
+__device__ __forceinline__ float softmax_exp(float d) {
+  if (sizeof(T) == 4) return expf(d);
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(d * 1.44269504088896341f));
+  return y;
+}
+
 template <typename T, int VPT>
 __global__ void __launch_bounds__(512) softmax_vec_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t rows,
                                    int64_t cols) {
@@ -155,7 +168,7 @@ __global__ void __launch_bounds__(512) softmax_vec_kernel(const T* __restrict__ 
     if (active && vi < nvec) {
 #pragma unroll
       for (int i = 0; i < E; ++i) {
-        v[j][i] = expf(v[j][i] - m);
+        v[j][i] = softmax_exp<T>(v[j][i] - m);
         s += v[j][i];
       }
     }
@@ -163,13 +176,14 @@ __global__ void __launch_bounds__(512) softmax_vec_kernel(const T* __restrict__ 
   s = row_allreduce<false>(s, smem);
   if (!active) return;
   T* yr = y + row * cols;
+  const float inv = 1.0f / s;
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int64_t vi = threadIdx.x + static_cast<int64_t>(j) * blockDim.x;
     if (vi < nvec) {
       float o[E];
 #pragma unroll
-      for (int i = 0; i < E; ++i) o[i] = __fdiv_rn(v[j][i], s);
+      for (int i = 0; i < E; ++i) o[i] = sizeof(T) == 4 ? __fdiv_rn(v[j][i], s) : v[j][i] * inv;
       store_vec<T>(yr + vi * E, o);
     }
   }
@@ -188,12 +202,15 @@ __global__ void softmax_loop_kernel(const T* __restrict__ x, T* __restrict__ y, 
   m = row_allreduce<true>(m, smem);
   float s = 0.f;
   if (active)
-    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) s += expf(to_f32(xr[c]) - m);
+    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) s += softmax_exp<T>(to_f32(xr[c]) - m);
   s = row_allreduce<false>(s, smem);
   if (!active) return;
   T* yr = y + row * cols;
-  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x)
-    yr[c] = from_f32<T>(__fdiv_rn(expf(to_f32(xr[c]) - m), s));
+  const float inv = 1.0f / s;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+    const float e = softmax_exp<T>(to_f32(xr[c]) - m);
+    yr[c] = from_f32<T>(sizeof(T) == 4 ? __fdiv_rn(e, s) : e * inv);
+  }
 }
 
 // ---------------------------------------------------------------------------

@@ -135,13 +135,15 @@ def test_rms_norm(mx, dtype, rows, cols, weighted):
     assert_close(np.asarray(got), np.asarray(ref), dtype)
 
 
-@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
-@pytest.mark.parametrize("rows,cols", [(64, 2048), (7, 33), (3, 70000)])
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16", "float16"])
+@pytest.mark.parametrize("rows,cols", [(64, 2048), (7, 33), (3, 70000), (16, 8192)])
 def test_softmax(mx, dtype, rows, cols):
     rng = np.random.default_rng(cols)
     npd = mlx_cpu._NP[dtype]
     x = (rng.standard_normal((rows, cols)).astype(np.float32) * 4).astype(npd)
     x[0, cols // 2:] = -np.inf
+    if rows > 4 and dtype != "float16":
+        x[4] = (x[4].astype(np.float32) * 2500).astype(npd)  # scores of magnitude ~1e4
     got = mx.softmax(mx.array(x), axis=-1)
     ref = mlx_cpu.softmax(mlx_cpu.array(x), axis=-1)
     assert_close(np.asarray(got), np.asarray(ref), dtype)

@@ -12,18 +12,23 @@
 // [N, K] (K contiguous: a K-major operand, `b_layout = 1`, e.g. k.T in q @ k.T).
 // Batches are strided; a zero batch stride broadcasts the operand.
 //
-// One CTA computes one (MT x 128) x BN tile (BN = 128 or 256, MT = 1 or 2):
+// Tiles are (MT x 128) x BN (BN = 128 or 256, MT = 1 or 2).  The kernel is
+// persistent: at most one CTA per SM, each walking the tiles t = blockIdx.x,
+// blockIdx.x + gridDim.x, ... with ACC (1 or 2) accumulators in TMEM, so the
+// epilogue of one tile overlaps the main loop of the next when ACC = 2, and
+// the TMA producer runs ahead across tile boundaries either way:
 //   warp 0      TMA producer: 128B-swizzled tiles of A and B into a STAGES-deep
 //               shared-memory ring; each CTA loads its own tiles (these
 //               kernels also run in multi-GPU jobs)
 //   warp 1      allocates TMEM, one elected lane issues tcgen05.mma (M=128,
-//               N=BN, K=16) into MT TMEM fp32 accumulators (one per 128 rows,
-//               all sharing the stage's B tile) and commits each stage back to
-//               the producer
+//               N=BN, K=16) into MT fp32 accumulators per tile (one per 128
+//               rows, all sharing the stage's B tile) and commits each stage
+//               back to the producer and each finished tile to the epilogue
 //   warps 2-5   epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
-//               32*(w%4)..), scale, convert, store; with the fused row scale they
-//               also accumulate each row's sum of squares from the A tiles while
-//               the main loop runs, so the norm costs no extra HBM pass
+//               32*(w%4)..), hand it back to the MMA warp after the last
+//               read, scale, convert, store; with the fused row scale they
+//               also accumulate each row's sum of squares from the A tiles
+//               while the main loop runs, so the norm costs no extra HBM pass
 // Every mbarrier wait is bounded; a wait that runs out sets *error_flag and the
 // kernel winds down instead of spinning.
 #include "tc_common.cuh"
@@ -39,14 +44,17 @@ constexpr int kNumThreads = 192;
 
 // A CTA computes MT x 128 rows by BN columns: MT accumulators of 128 x BN in
 // TMEM that share every B tile (MT = 2 halves the B bytes per MMA).
-template <int BN, int MT> struct Cfg {
+template <int BN, int MT, int ACC> struct Cfg {
   static constexpr int ROWS = BM * MT;
   static constexpr int A_BYTES = ROWS * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (200 * 1024) / STAGE_BYTES;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
-  static constexpr int TMEM_COLS = BN * MT;
+  // epilogue staging for TMA stores: 4 warps x 2 buffers x (32 rows x 128 B)
+  static constexpr int OUT_BYTES = 4 * 2 * 32 * 128;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + OUT_BYTES + 1024 + 256;
+  static constexpr int TMEM_COLS = BN * MT * ACC;
+  static_assert(TMEM_COLS <= 512, "accumulators exceed TMEM");
 };
 
 struct Params {
@@ -59,6 +67,7 @@ struct Params {
   long long c_batch_stride;
   int out_dtype;  // PHEW_F32 / PHEW_F16 / PHEW_BF16
   int row_scale;  // 1: fused rsqrt(mean(A^2) + eps) per row
+  int tma_store;  // 1: 16-bit C written by TMA stores through shared memory
   float eps;
   int* error_flag;
 };
@@ -80,31 +89,54 @@ __device__ __forceinline__ void store_row32(T* dst, const float* v, int ncols) {
   }
 }
 
-template <int BN, int MT, bool BF16>
+// Two fp32 values rounded (to nearest even) into a packed bf16x2 / f16x2 word.
+__device__ __forceinline__ uint32_t pack_out(float lo, float hi, bool bf16) {
+  uint32_t d;
+  if (bf16)
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  else
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+template <int BN, int MT, int ACC, bool BF16>
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const Params p) {
-  using C = Cfg<BN, MT>;
+                   const __grid_constant__ CUtensorMap tmC, const Params p) {
+  using C = Cfg<BN, MT, ACC>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint8_t* out_stage = smem + C::STAGES * C::STAGE_BYTES;  // [4 warps][2][32 x 128 B]
+  uint64_t* full = reinterpret_cast<uint64_t*>(out_stage + C::OUT_BYTES);
   uint64_t* empty = full + C::STAGES;
-  uint64_t* accum_full = empty + C::STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_full + 1);
+  uint64_t* acc_full = empty + C::STAGES;  // [ACC]: accumulator a holds a finished tile
+  uint64_t* acc_empty = acc_full + ACC;    // [ACC]: the epilogue has read accumulator a
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + ACC);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN;
-  const int m0 = blockIdx.y * C::ROWS;
-  const int bz = blockIdx.z;
   const int num_kb = (p.K + BK - 1) / BK;
+  const int n_nb = (p.N + BN - 1) / BN;
+  const int n_mb = (p.M + C::ROWS - 1) / C::ROWS;
+  const int num_tiles = n_nb * n_mb * p.batch;
+  // Tile t -> (batch, row block, column block), column blocks fastest so
+  // that CTAs running together share their A rows in L2.
+  auto coords = [&](int t, int& bz, int& m0, int& n0) {
+    n0 = (t % n_nb) * BN;
+    const int r = t / n_nb;
+    m0 = (r % n_mb) * C::ROWS;
+    bz = r / n_mb;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], p.row_scale ? 5 : 1);  // MMA commit (+ 4 epilogue warps)
     }
-    mbar_init(accum_full, 1);
+    for (int a = 0; a < ACC; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -117,27 +149,32 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   bool ok = true;
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- TMA producer: runs ahead across tiles ----------------
     if (lane == 0) {
-      const int ba = p.a_batched ? bz : 0;
-      const int bb = p.b_batched ? bz : 0;
-      for (int kb = 0; kb < num_kb && ok; ++kb) {
-        const int s = kb % C::STAGES;
-        const uint32_t ph = (kb / C::STAGES) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1, p.error_flag)) {
-          ok = false;
-          break;
-        }
-        uint8_t* sa = smem + s * C::STAGE_BYTES;
-        uint8_t* sb = sa + C::A_BYTES;
-        mbar_expect_tx(&full[s], C::STAGE_BYTES);
-        tma_load_3d(sa, &tmA, &full[s], kb * BK, m0, ba);
-        if (p.b_mn_major) {
+      uint32_t kg = 0;  // k-blocks issued so far (ring position)
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int bz, m0, n0;
+        coords(t, bz, m0, n0);
+        const int ba = p.a_batched ? bz : 0;
+        const int bb = p.b_batched ? bz : 0;
+        for (int kb = 0; kb < num_kb; ++kb, ++kg) {
+          const int s = kg % C::STAGES;
+          const uint32_t ph = (kg / C::STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, p.error_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + s * C::STAGE_BYTES;
+          uint8_t* sb = sa + C::A_BYTES;
+          mbar_expect_tx(&full[s], C::STAGE_BYTES);
+          tma_load_3d(sa, &tmA, &full[s], kb * BK, m0, ba);
+          if (p.b_mn_major) {
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j)
-            tma_load_3d(sb + j * (64 * BK * 2), &tmB, &full[s], n0 + j * 64, kb * BK, bb);
-        } else {
-          tma_load_3d(sb, &tmB, &full[s], kb * BK, n0, bb);
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_3d(sb + j * (64 * BK * 2), &tmB, &full[s], n0 + j * 64, kb * BK, bb);
+          } else {
+            tma_load_3d(sb, &tmB, &full[s], kb * BK, n0, bb);
+          }
         }
       }
     }
@@ -146,131 +183,207 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = instr_desc_f16(BF16 ? 1 : 0, 0, BM, BN);
       const uint32_t idesc_b = p.b_mn_major ? instr_desc_f16(BF16 ? 1 : 0, 1, BM, BN) : idesc;
-      for (int kb = 0; kb < num_kb && ok; ++kb) {
-        const int s = kb % C::STAGES;
-        const uint32_t ph = (kb / C::STAGES) & 1;
-        if (!mbar_wait(&full[s], ph, p.error_flag)) {
+      uint32_t kg = 0, it = 0;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+        const int a = it % ACC;
+        // accumulator a is free once the epilogue has read the tile before
+        if (!mbar_wait(&acc_empty[a], ((it / ACC) & 1) ^ 1, p.error_flag)) {
           ok = false;
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
-        const uint32_t sb = sa + C::A_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk) {
-          const uint64_t bd = p.b_mn_major ? smem_desc(sb + kk * (16 * 128), 64 * BK * 2, 1024)
-                                           : smem_desc(sb + kk * 32, 16, 1024);
-#pragma unroll
-          for (int h = 0; h < MT; ++h) {
-            // rows h*128.. of the A tile start h*128*128 bytes in (1024-aligned)
-            const uint64_t ad = smem_desc(sa + h * (BM * 128) + kk * 32, 16, 1024);
-            mma_ss(tmem + h * BN, ad, bd, idesc_b, (kb > 0 || kk > 0) ? 1u : 0u);
+        const uint32_t acc = tmem + a * (MT * BN);
+        for (int kb = 0; kb < num_kb; ++kb, ++kg) {
+          const int s = kg % C::STAGES;
+          const uint32_t ph = (kg / C::STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, p.error_flag)) {
+            ok = false;
+            break;
           }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
+          const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t bd = p.b_mn_major ? smem_desc(sb + kk * (16 * 128), 64 * BK * 2, 1024)
+                                             : smem_desc(sb + kk * 32, 16, 1024);
+#pragma unroll
+            for (int h = 0; h < MT; ++h) {
+              // rows h*128.. of the A tile start h*128*128 bytes in (1024-aligned)
+              const uint64_t ad = smem_desc(sa + h * (BM * 128) + kk * 32, 16, 1024);
+              mma_ss(acc + h * BN, ad, bd, idesc_b, (kb > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          commit(&empty[s]);
         }
-        commit(&empty[s]);
+        if (ok) commit(&acc_full[a]);
       }
-      if (ok) commit(accum_full);
     }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     const int quarter = warp & 3;
-    float ss[MT];
+    uint32_t kg = 0, it = 0, out_idx = 0;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+      int bz, m0, n0;
+      coords(t, bz, m0, n0);
+      const int a = it % ACC;
+      float ss[MT];
 #pragma unroll
-    for (int h = 0; h < MT; ++h) ss[h] = 0.f;
-    if (p.row_scale) {
-      // Sum of squares of this warp's 32 rows (per 128-row half), read
-      // cooperatively: in read i, lanes 8g..8g+7 cover the 128-byte row
-      // 4i+g, 16 bytes each, so every read instruction touches 4 whole rows
-      // and no two lanes of a phase share a bank.  The order within a row
-      // does not matter, so the 128B swizzle needs no undoing.
-      float part[MT][8];
+      for (int h = 0; h < MT; ++h) ss[h] = 0.f;
+      if (p.row_scale) {
+        // Sum of squares of this warp's 32 rows (per 128-row half), read
+        // cooperatively: in read i, lanes 8g..8g+7 cover the 128-byte row
+        // 4i+g, 16 bytes each, so every read instruction touches 4 whole
+        // rows and no two lanes of a phase share a bank.  The order within
+        // a row does not matter, so the 128B swizzle needs no undoing.
+        float part[MT][8];
 #pragma unroll
-      for (int h = 0; h < MT; ++h)
+        for (int h = 0; h < MT; ++h)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) part[h][i] = 0.f;
-      for (int kb = 0; kb < num_kb && ok; ++kb) {
-        const int s = kb % C::STAGES;
-        const uint32_t ph = (kb / C::STAGES) & 1;
-        if (!mbar_wait(&full[s], ph, p.error_flag)) {
-          ok = false;
-          break;
+          for (int i = 0; i < 8; ++i) part[h][i] = 0.f;
+        for (int kb = 0; kb < num_kb; ++kb, ++kg) {
+          const int s = kg % C::STAGES;
+          const uint32_t ph = (kg / C::STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, p.error_flag)) {
+            ok = false;
+            break;
+          }
+#pragma unroll
+          for (int h = 0; h < MT; ++h) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int r = h * BM + quarter * 32 + 4 * i + (lane >> 3);
+              const uint4 raw = *reinterpret_cast<const uint4*>(smem + s * C::STAGE_BYTES + r * 128 + (lane & 7) * 16);
+              const uint16_t* hv = reinterpret_cast<const uint16_t*>(&raw);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                float x;
+                if (BF16) {
+                  x = __uint_as_float(static_cast<uint32_t>(hv[e]) << 16);
+                } else {
+                  asm("cvt.f32.f16 %0, %1;" : "=f"(x) : "h"(hv[e]));
+                }
+                part[h][i] = fmaf(x, x, part[h][i]);
+              }
+            }
+          }
+          // The next TMA write into this stage must be ordered after these
+          // generic-proxy reads.
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[s]);
         }
+        // Reduce over the 8 lanes that share a row, then give lane R the sum
+        // of row R (held by lanes 8 * (R % 4).., read i = R / 4).
 #pragma unroll
         for (int h = 0; h < MT; ++h) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            const int r = h * BM + quarter * 32 + 4 * i + (lane >> 3);
-            const uint4 raw = *reinterpret_cast<const uint4*>(smem + s * C::STAGE_BYTES + r * 128 + (lane & 7) * 16);
-            const uint16_t* hv = reinterpret_cast<const uint16_t*>(&raw);
+            part[h][i] += __shfl_xor_sync(0xffffffffu, part[h][i], 1);
+            part[h][i] += __shfl_xor_sync(0xffffffffu, part[h][i], 2);
+            part[h][i] += __shfl_xor_sync(0xffffffffu, part[h][i], 4);
+          }
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              float x;
-              if (BF16) {
-                x = __uint_as_float(static_cast<uint32_t>(hv[e]) << 16);
-              } else {
-                asm("cvt.f32.f16 %0, %1;" : "=f"(x) : "h"(hv[e]));
+          for (int i = 0; i < 8; ++i) {
+            const float v = __shfl_sync(0xffffffffu, part[h][i], 8 * (lane & 3));
+            if ((lane >> 2) == i) ss[h] = v;
+          }
+        }
+      }
+      if (ok && !mbar_wait(&acc_full[a], (it / ACC) & 1, p.error_flag)) ok = false;
+      if (!ok) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t acc = tmem + a * (MT * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
+      if (p.tma_store) {
+        // 64 columns at a time: TMEM -> registers -> this warp's 32 x 64
+        // staging box (128B-swizzled, so the 8 lanes of a store phase hit
+        // distinct banks) -> one TMA store of the box, double-buffered.
+        uint8_t* my_out = out_stage + (warp - 2) * (2 * 32 * 128);
+        for (int h = 0; h < MT; ++h) {
+          const float scale = p.row_scale ? 1.0f / sqrtf(ss[h] / static_cast<float>(p.K) + p.eps) : 1.0f;
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 64, ++out_idx) {
+            uint32_t r[64];
+            tmem_ld32(acc + h * BN + c, r);
+            tmem_ld32(acc + h * BN + c + 32, r + 32);
+            tmem_ld_wait();
+            if (h == MT - 1 && c + 64 == BN) {
+              // last read of this accumulator: hand it back to the MMA warp
+              asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&acc_empty[a]);
+            }
+            uint8_t* box = my_out + (out_idx & 1) * (32 * 128);
+            if (lane == 0) bulk_wait_read1();  // the store issued two boxes ago has read this one
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              uint32_t w[4];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                float lo = __uint_as_float(r[8 * j + 2 * q]), hi = __uint_as_float(r[8 * j + 2 * q + 1]);
+                if (p.row_scale == 1) {
+                  lo *= scale;
+                  hi *= scale;
+                } else if (p.row_scale == 2) {  // diagnostic: the row's sum of squares
+                  lo = hi = ss[h];
+                }
+                w[q] = pack_out(lo, hi, p.out_dtype == PHEW_BF16);
               }
-              part[h][i] = fmaf(x, x, part[h][i]);
+              *reinterpret_cast<uint4*>(box + lane * 128 + ((j ^ (lane & 7)) * 16)) =
+                  make_uint4(w[0], w[1], w[2], w[3]);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_3d(&tmC, box, n0 + c, m0 + h * BM + quarter * 32, bz);
+              bulk_commit();
             }
           }
         }
-        // The next TMA write into this stage must be ordered after these
-        // generic-proxy reads.
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
+        continue;
       }
-      // Reduce over the 8 lanes that share a row, then give lane R the sum
-      // of row R (held by lanes 8 * (R % 4).., read i = R / 4).
-#pragma unroll
       for (int h = 0; h < MT; ++h) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          part[h][i] += __shfl_xor_sync(0xffffffffu, part[h][i], 1);
-          part[h][i] += __shfl_xor_sync(0xffffffffu, part[h][i], 2);
-          part[h][i] += __shfl_xor_sync(0xffffffffu, part[h][i], 4);
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float v = __shfl_sync(0xffffffffu, part[h][i], 8 * (lane & 3));
-          if ((lane >> 2) == i) ss[h] = v;
-        }
-      }
-    }
-    if (ok && !mbar_wait(accum_full, 0, p.error_flag)) ok = false;
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    for (int h = 0; h < MT && ok; ++h) {
-      const float scale = p.row_scale ? 1.0f / sqrtf(ss[h] / static_cast<float>(p.K) + p.eps) : 1.0f;
-      const int row = m0 + h * BM + quarter * 32 + lane;
-      const long long cbase = static_cast<long long>(bz) * p.c_batch_stride + static_cast<long long>(row) * p.ldc;
+        const float scale = p.row_scale ? 1.0f / sqrtf(ss[h] / static_cast<float>(p.K) + p.eps) : 1.0f;
+        const int row = m0 + h * BM + quarter * 32 + lane;
+        const long long cbase = static_cast<long long>(bz) * p.c_batch_stride + static_cast<long long>(row) * p.ldc;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        float v[32];
-        {
-          uint32_t r[32];
-          tmem_ld32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + h * BN + c, r);
-          tmem_ld_wait();
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          {
+            uint32_t r[32];
+            tmem_ld32(acc + h * BN + c, r);
+            tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-        }
-        if (row < p.M && n0 + c < p.N) {
-          if (p.row_scale == 1) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] *= scale;
-          } else if (p.row_scale == 2) {  // diagnostic: the row's sum of squares
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = ss[h];
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
           }
-          const int ncols = p.N - (n0 + c);
-          if (p.out_dtype == PHEW_BF16)
-            store_row32(static_cast<bf16*>(p.C) + cbase + n0 + c, v, ncols);
-          else if (p.out_dtype == PHEW_F16)
-            store_row32(static_cast<f16*>(p.C) + cbase + n0 + c, v, ncols);
-          else
-            store_row32(static_cast<float*>(p.C) + cbase + n0 + c, v, ncols);
+          if (h == MT - 1 && c + 32 == BN) {
+            // last read of this accumulator: hand it back to the MMA warp
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[a]);
+          }
+          if (row < p.M && n0 + c < p.N) {
+            if (p.row_scale == 1) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] *= scale;
+            } else if (p.row_scale == 2) {  // diagnostic: the row's sum of squares
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = ss[h];
+            }
+            const int ncols = p.N - (n0 + c);
+            if (p.out_dtype == PHEW_BF16)
+              store_row32(static_cast<bf16*>(p.C) + cbase + n0 + c, v, ncols);
+            else if (p.out_dtype == PHEW_F16)
+              store_row32(static_cast<f16*>(p.C) + cbase + n0 + c, v, ncols);
+            else
+              store_row32(static_cast<float*>(p.C) + cbase + n0 + c, v, ncols);
+          }
         }
       }
     }
+    // TMA stores must finish reading shared memory before the CTA exits.
+    if (lane == 0) bulk_wait_all();
   }
   if (!ok && p.error_flag) atomicExch(p.error_flag, PHEW_ERR_TIMEOUT);
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -337,10 +450,23 @@ int make_map(CUtensorMap* tm, const void* base, bool bf16, uint64_t d0, uint64_t
   return make_map_16bit(tm, base, bf16, 3, dims, strides, box);
 }
 
-template <int BN, int MT, bool BF16>
+// Persistent grid: one CTA per SM at most, each looping over tiles.
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+template <int BN, int MT, int ACC, bool BF16>
 int launch_tc(const void* A, const void* B, const Params& p, long long lda, long long ldb,
               long long sa, long long sb, cudaStream_t st) {
-  using C = Cfg<BN, MT>;
+  using C = Cfg<BN, MT, ACC>;
   CUtensorMap ta, tb;
   const uint64_t nba = p.a_batched ? p.batch : 1, nbb = p.b_batched ? p.batch : 1;
   int s = make_map(&ta, A, BF16, p.K, p.M, nba, lda * 2, (p.a_batched ? sa : (long long)p.M * lda) * 2, BK, C::ROWS);
@@ -350,14 +476,27 @@ int launch_tc(const void* A, const void* B, const Params& p, long long lda, long
   else
     s = make_map(&tb, B, BF16, p.K, p.N, nbb, ldb * 2, (p.b_batched ? sb : (long long)p.N * ldb) * 2, BK, BN);
   if (s) return s;
+  // C through TMA stores when it is 16-bit and its layout is describable
+  // (16-byte aligned base and row/batch strides); otherwise direct stores.
+  CUtensorMap tc;
+  Params q = p;
+  const long long cbs = p.batch > 1 ? p.c_batch_stride : static_cast<long long>(p.M) * p.ldc;
+  q.tma_store = p.out_dtype != PHEW_F32 && (reinterpret_cast<uintptr_t>(p.C) & 15) == 0 &&
+                (p.ldc * 2) % 16 == 0 && (cbs * 2) % 16 == 0 && cbs > 0 && p.ldc >= p.N;
+  if (q.tma_store &&
+      make_map(&tc, p.C, p.out_dtype == PHEW_BF16, p.N, p.M, p.batch, p.ldc * 2, cbs * 2, 64, 32) != PHEW_OK)
+    q.tma_store = 0;
+  if (!q.tma_store) tc = ta;  // unused
   static bool attr_set = false;
   if (!attr_set) {
-    PHEW_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, MT, BF16>,
+    PHEW_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, MT, ACC, BF16>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr_set = true;
   }
-  dim3 grid((p.N + BN - 1) / BN, (p.M + C::ROWS - 1) / C::ROWS, p.batch);
-  gemm_tc_kernel<BN, MT, BF16><<<grid, kNumThreads, C::SMEM, st>>>(ta, tb, p);
+  const long long tiles = static_cast<long long>((p.N + BN - 1) / BN) * ((p.M + C::ROWS - 1) / C::ROWS) * p.batch;
+  PHEW_REQUIRE(tiles < (1LL << 31), "phew_gemm: too many tiles");
+  const unsigned grid = static_cast<unsigned>(tiles < sm_count() ? tiles : sm_count());
+  gemm_tc_kernel<BN, MT, ACC, BF16><<<grid, kNumThreads, C::SMEM, st>>>(ta, tb, tc, q);
   return launch_status("gemm_tc_kernel");
 }
 
@@ -395,6 +534,7 @@ extern "C" int phew_gemm(const void* A, const void* B, void* Cout, int64_t M, in
   p.c_batch_stride = stride_c;
   p.out_dtype = out_dtype;
   p.row_scale = row_scale;
+  p.tma_store = 0;
   p.eps = eps;
   p.error_flag = error_flag;
   const bool aligned16 =
@@ -403,15 +543,22 @@ extern "C" int phew_gemm(const void* A, const void* B, void* Cout, int64_t M, in
       (stride_b * 2) % 16 == 0 && K > 0;
   if (aligned16 && in_dtype != PHEW_F32) {
     const bool bf = in_dtype == PHEW_BF16;
-    // Tile choice: 128 x 128 for narrow outputs; 256 x 256 (two 128-row
-    // accumulators sharing each B tile: 64 operand bytes per MMA cycle
-    // instead of 96) when both M and N exceed 128, else 128 x 256.
-    if (N <= 128) return bf ? launch_tc<128, 1, true>(A, B, p, lda, ldb, stride_a, stride_b, st)
-                            : launch_tc<128, 1, false>(A, B, p, lda, ldb, stride_a, stride_b, st);
-    if (M > 128) return bf ? launch_tc<256, 2, true>(A, B, p, lda, ldb, stride_a, stride_b, st)
-                           : launch_tc<256, 2, false>(A, B, p, lda, ldb, stride_a, stride_b, st);
-    return bf ? launch_tc<256, 1, true>(A, B, p, lda, ldb, stride_a, stride_b, st)
-              : launch_tc<256, 1, false>(A, B, p, lda, ldb, stride_a, stride_b, st);
+    // Tile choice (every kernel is persistent: one CTA per SM looping over
+    // tiles, TMA running ahead across tile boundaries):
+    //   N <= 128         128 x 128 tiles, two accumulators (the epilogue of
+    //                    one tile overlaps the main loop of the next)
+    //   K <= 512         128 x 256, two accumulators: short main loops, so
+    //                    the output write is the cost and must overlap
+    //   M > 128          256 x 256 (two 128-row accumulators sharing each B
+    //                    tile: 64 operand bytes per MMA cycle instead of 96)
+    //   otherwise        128 x 256, two accumulators
+    const bool d = bf;
+    if (N <= 128) return d ? launch_tc<128, 1, 2, true>(A, B, p, lda, ldb, stride_a, stride_b, st)
+                           : launch_tc<128, 1, 2, false>(A, B, p, lda, ldb, stride_a, stride_b, st);
+    if (K > 512 && M > 128) return d ? launch_tc<256, 2, 1, true>(A, B, p, lda, ldb, stride_a, stride_b, st)
+                                     : launch_tc<256, 2, 1, false>(A, B, p, lda, ldb, stride_a, stride_b, st);
+    return d ? launch_tc<256, 1, 2, true>(A, B, p, lda, ldb, stride_a, stride_b, st)
+             : launch_tc<256, 1, 2, false>(A, B, p, lda, ldb, stride_a, stride_b, st);
   }
   dim3 grid(static_cast<unsigned>((N + 15) / 16), static_cast<unsigned>((M + 15) / 16),
             static_cast<unsigned>(batch));

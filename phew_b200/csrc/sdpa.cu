@@ -169,10 +169,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int n_qb = (p.L + BQ * QT - 1) / (BQ * QT);
-  // Longest query blocks first across the whole grid: with a causal mask
-  // later blocks do more work, and finishing them first evens out the tail.
-  const int qb = p.causal ? (n_qb - 1 - static_cast<int>(blockIdx.x / p.bh)) : static_cast<int>(blockIdx.x / p.bh);
-  const int bh = static_cast<int>(blockIdx.x % p.bh);
+  // CTA order: heads in groups of 16, so the CTAs running at one time share
+  // the K / V of few heads in L2.  With a causal mask later query blocks do
+  // more work, so within a group the longest go first (evens out the tail);
+  // without one a head's query blocks run side by side.
+  int qb, bh;
+  if (p.causal) {
+    const int G = p.bh < 16 ? p.bh : 16;
+    const int grp = static_cast<int>(blockIdx.x) / (G * n_qb);
+    const int rem = static_cast<int>(blockIdx.x) % (G * n_qb);
+    const int gsize = (grp + 1) * G <= p.bh ? G : p.bh - grp * G;
+    qb = n_qb - 1 - rem / gsize;
+    bh = grp * G + rem % gsize;
+  } else {
+    qb = static_cast<int>(blockIdx.x % n_qb);
+    bh = static_cast<int>(blockIdx.x / n_qb);
+  }
   const int q0 = qb * BQ * QT;
   const int row_base = bh * p.L;  // first row of this (b, h) in the [B*H*L, D] view
   const int n_tiles = (q0 + BQ < p.L) ? 2 : 1;

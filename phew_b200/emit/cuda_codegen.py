@@ -575,6 +575,126 @@ class SubgraphCUDACodegen:
         source = "\n".join(f"    {line}" if line else "" for line in L)
         return source, inp_names, out_names
 
+    # -- elementwise prologue fused into a row softmax --------------------------
+
+    def emit_softmax(self, subgraph_nodes, external_inputs, root, tpr: int, rpb: int,
+                     vpt: int) -> tuple[str, list[str], list[str]]:
+        """Body of ``softmax(root, axis=-1)`` where `root` is the value of the
+        elementwise DAG `subgraph_nodes` over `external_inputs`: each row's
+        elements are computed in registers (rounded per node, as the chain
+        kernels round them) and never written to HBM.
+
+        The thread/element mapping and both reductions are those of
+        ``csrc/rows.cu``'s ``softmax_vec_kernel`` for the same row plan (`tpr`
+        threads per row, `rpb` rows per block, `vpt` 16-byte vectors per
+        thread), so the result has the bits of materialising `root` and then
+        calling ``phew_softmax``.  Launch: block (tpr, rpb), one block per
+        `rpb` rows.  Raises ``ValueError`` when the DAG cannot run 16 bytes
+        at a time in that mapping (the caller then materialises `root`).
+        """
+        out_shape = tuple(int(x) for x in root.shape)
+        if not out_shape:
+            raise ValueError("cuda_codegen: softmax of a 0-d array")
+        cols = out_shape[-1]
+        out_dt = dtype_name(root.dtype)
+        if out_dt not in ("float32", "float16", "bfloat16"):
+            raise ValueError(f"cuda_codegen: softmax over {out_dt}")
+        E = 16 // ITEMSIZE[out_dt]
+        if cols % E:
+            raise ValueError("cuda_codegen: softmax row is not a whole number of vectors")
+        in_dts = [dtype_name(x.dtype) for x in external_inputs]
+        for d in in_dts:
+            if d not in CTYPE:
+                raise ValueError(f"cuda_codegen: unsupported dtype {d!r}")
+        classes = []
+        for x in external_inputs:
+            shp = tuple(int(v) for v in x.shape)
+            if len(shp) > 0 and not broadcast_compatible(shp, out_shape):
+                raise ValueError("cuda_codegen: input not broadcast-compatible with output")
+            classes.append(classify_input(shp, out_shape))
+        itemsizes = [ITEMSIZE[d] for d, (c, _) in zip(in_dts, classes) if c in ("full", "suffix")]
+        V = max(1, min(8, 16 // min(itemsizes + [ITEMSIZE[out_dt]])))
+        if V != E:
+            raise ValueError("cuda_codegen: input vectors narrower than the softmax rows'")
+        if not all(c in ("full", "scalar", "general") or ext % V == 0 for c, ext in classes):
+            raise ValueError("cuda_codegen: broadcast extent not a multiple of the vector")
+        plan = _Plan(subgraph_nodes, external_inputs, [root],
+                     precise16=getattr(self, "precise_16bit", False))
+        inp_names = [f"inp{i}" for i in range(len(external_inputs))]
+        out_names = ["out0"]
+        n = _numel(out_shape)
+        it = "unsigned int" if n < 2**30 else "unsigned long long"
+        u = "u" if it == "unsigned int" else "ull"
+        half_t = plan.pure_half_type(in_dts, [out_dt])
+        packed = half_t is not None and V == 8
+        body = self._vector_body(plan, external_inputs, inp_names, out_names, in_dts, [out_dt],
+                                 classes, out_shape, V, it, u, half_t)
+        body = [b for b in body if not b.startswith("phew_stv<")]
+        ct = CTYPE[out_dt]
+        st = f"phew_st_{_suffix(out_dt)}"
+        div = "__fdiv_rn(phew_sv[j][l], phew_s)" if out_dt == "float32" else "phew_sv[j][l] * phew_inv"
+        L: list[str] = []
+        L.append(
+            f"// elementwise prologue ({len(plan.compute_nodes)} ops, {len(external_inputs)} inputs) "
+            f"+ softmax over rows of {cols}"
+        )
+        L.append(io_contract_line(classes, out_shape, [tuple(x.shape) for x in external_inputs], it))
+        for line in plan.constant_lines(packed_type=half_t if packed else None):
+            L.append(line)
+        L += [
+            "__shared__ float phew_smem[32 * 32];",
+            f"const {it} phew_cols = {cols}{u};",
+            f"const {it} phew_rows = ({it})out0_size / phew_cols;",
+            f"const {it} phew_nvec = phew_cols / {V}{u};",
+            f"const {it} phew_row = ({it})blockIdx.x * blockDim.y + threadIdx.y;",
+            "const bool phew_active = phew_row < phew_rows;",
+            f"float phew_sv[{vpt}][{V}];",
+            "float phew_m = __int_as_float(0xff800000u);",
+            "#pragma unroll",
+            f"for (int j = 0; j < {vpt}; ++j) {{",
+            f"  const {it} phew_vi = threadIdx.x + ({it})j * blockDim.x;",
+            "  if (phew_active && phew_vi < phew_nvec) {",
+            f"    const {it} elem = phew_row * phew_cols + phew_vi * {V}{u};",
+        ]
+        L += ["    " + b for b in body]
+        L += [
+            "    #pragma unroll",
+            f"    for (int l = 0; l < {V}; ++l) phew_sv[j][l] = phew_ld(st0.v[l]);",
+            "    #pragma unroll",
+            f"    for (int l = 0; l < {V}; ++l) phew_m = fmaxf(phew_m, phew_sv[j][l]);",
+            "  }",
+            "}",
+            "phew_m = phew_row_allreduce<true>(phew_m, phew_smem);",
+            "float phew_s = 0.f;",
+            "#pragma unroll",
+            f"for (int j = 0; j < {vpt}; ++j) {{",
+            f"  const {it} phew_vi = threadIdx.x + ({it})j * blockDim.x;",
+            "  if (phew_active && phew_vi < phew_nvec) {",
+            "    #pragma unroll",
+            f"    for (int l = 0; l < {V}; ++l) {{",
+            f"      phew_sv[j][l] = phew_softmax_exp<{ITEMSIZE[out_dt]}>(phew_sv[j][l] - phew_m);",
+            "      phew_s += phew_sv[j][l];",
+            "    }",
+            "  }",
+            "}",
+            "phew_s = phew_row_allreduce<false>(phew_s, phew_smem);",
+            "if (!phew_active) return;",
+            "const float phew_inv = 1.0f / phew_s;",
+            "#pragma unroll",
+            f"for (int j = 0; j < {vpt}; ++j) {{",
+            f"  const {it} phew_vi = threadIdx.x + ({it})j * blockDim.x;",
+            "  if (phew_vi < phew_nvec) {",
+            f"    phew_vec<{ct}, {V}> phew_o;",
+            "    #pragma unroll",
+            f"    for (int l = 0; l < {V}; ++l) phew_o.v[l] = {st}({div});",
+            f"    phew_stv<{ct}, {V}>(out0 + phew_row * phew_cols + phew_vi * {V}{u}, phew_o);",
+            "  }",
+            "}",
+        ]
+        _ = packed
+        source = "\n".join(f"    {line}" if line else "" for line in L)
+        return source, inp_names, out_names
+
     # -- per-element form -----------------------------------------------------
 
     def _index(self, cls, ext, name, node, out_shape, it, u, elem="elem") -> str:

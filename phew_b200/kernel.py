@@ -42,6 +42,39 @@ __device__ __forceinline__ float phew_bf2f(unsigned short b) {
   return __uint_as_float(((unsigned)b) << 16); }
 __device__ __forceinline__ unsigned short phew_f2bf(float f) {
   unsigned short b; asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(b) : "f"(f)); return b; }
+// Row reductions and the softmax exponential of csrc/rows.cu (same order of
+// operations, so fused softmax kernels give its bits).
+__device__ __forceinline__ float phew_warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float phew_warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+template <bool IS_MAX>
+__device__ __forceinline__ float phew_row_allreduce(float v, float* smem) {
+  v = IS_MAX ? phew_warp_max(v) : phew_warp_sum(v);
+  const int warps_per_row = blockDim.x / 32;
+  if (warps_per_row == 1) return v;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float* row_smem = smem + threadIdx.y * 32;
+  __syncthreads();
+  if (lane == 0) row_smem[warp] = v;
+  __syncthreads();
+  float r = lane < warps_per_row ? row_smem[lane] : (IS_MAX ? __int_as_float(0xff800000u) : 0.f);
+  r = IS_MAX ? phew_warp_max(r) : phew_warp_sum(r);
+  return r;
+}
+template <int ITEMSIZE>
+__device__ __forceinline__ float phew_softmax_exp(float d) {
+  if (ITEMSIZE == 4) return expf(d);
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(d * 1.44269504088896341f));
+  return y;
+}
 __device__ __forceinline__ float phew_rnd_f16(float f) { return phew_h2f(phew_f2h(f)); }
 __device__ __forceinline__ float phew_rnd_bf16(float f) { return phew_bf2f(phew_f2bf(f)); }
 

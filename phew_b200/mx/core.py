@@ -23,6 +23,7 @@ import ctypes
 import functools
 import math
 import numbers
+import threading
 import weakref
 from typing import Any, Sequence
 
@@ -406,6 +407,8 @@ def _elementwise(op: str, operands: list, out_dtype: Dtype | None = None,
     compute_dt = res
     node_dt = bool_ if out_bool else (out_dtype or res)
     shape = _broadcast_shapes(*[a.shape for a in arrays])
+    if _tracing() and _numel(shape) > 0:
+        return _Lazy._new(op, operands, compute_dt, node_dt, shape)
     key_parts = []
     for x in operands:
         if isinstance(x, array):
@@ -427,6 +430,207 @@ def _elementwise(op: str, operands: list, out_dtype: Dtype | None = None,
         threadgroup=(256, 1, 1),
     )
     return out[0]
+
+
+# ---------------------------------------------------------------------------
+# deferred elementwise results inside mx.compile
+# ---------------------------------------------------------------------------
+#
+# Inside a function wrapped by ``mx.compile`` elementwise ops do not launch:
+# they return `_Lazy` arrays, nodes of a pending DAG.  The first read of a
+# node's storage (any non-elementwise op, a view, a host copy, the function's
+# return) emits the node and every pending elementwise node it depends on as
+# ONE fused kernel (the same per-element code as the fusion pass's chains:
+# every node rounded to its own dtype, so the values are those of op-by-op
+# evaluation) and keeps the result.  A pending node read by two different
+# materialisations is computed in both (elementwise recompute is cheaper
+# than a round trip through HBM).
+
+_trace = threading.local()
+
+
+def _tracing() -> bool:
+    return getattr(_trace, "depth", 0) > 0
+
+
+class _Lazy(array):
+    """A pending elementwise result (see the section comment)."""
+
+    __slots__ = ("_op", "_shape", "_dtype", "_mt")
+
+    @classmethod
+    def _new(cls, op, operands, compute_dt, node_dt, shape) -> "_Lazy":
+        a = object.__new__(cls)
+        object.__setattr__(a, "_op", (op, tuple(operands), compute_dt, node_dt))
+        object.__setattr__(a, "_shape", tuple(int(x) for x in shape))
+        object.__setattr__(a, "_dtype", node_dt)
+        object.__setattr__(a, "_mt", None)
+        return a
+
+    @property
+    def _t(self) -> torch.Tensor:  # type: ignore[override]
+        if self._mt is None:
+            _materialize(self)
+        return self._mt
+
+    @property
+    def pending(self) -> bool:
+        return self._mt is None
+
+    @property
+    def shape(self) -> tuple:
+        return self._shape
+
+    @property
+    def dtype(self) -> Dtype:
+        return self._dtype
+
+    @property
+    def size(self) -> int:
+        return _numel(self._shape)
+
+    @property
+    def ndim(self) -> int:
+        return len(self._shape)
+
+    @property
+    def itemsize(self) -> int:
+        return self._dtype.size
+
+
+def _fused_dag(root: "_Lazy"):
+    """NodeSpecs of the pending DAG under `root` (topological order), its
+    external inputs (specs and arrays, in first-visit order) and a key that
+    identifies the DAG's structure for the kernel cache."""
+    chain: list = []
+    ext_specs: list = []
+    ext_arrays: list = []
+    key: list = []
+    memo: dict[int, tuple] = {}
+
+    def visit(x):
+        hit = memo.get(id(x))
+        if hit is not None:
+            return hit
+        if isinstance(x, _Lazy) and x._mt is None:
+            op, operands, cdt, ndt = x._op
+            args, arg_keys = [], []
+            for o in operands:
+                if isinstance(o, array):
+                    spec, k = visit(o)
+                    if o.dtype is not cdt and op != "where":
+                        spec = NodeSpec("Cast", o.shape, cdt.name, inputs=[spec.id], target_dtype=cdt.name)
+                        chain.append(spec)
+                        key.append(("cast", k, cdt.name))
+                        k = len(key) - 1
+                else:
+                    spec = NodeSpec("Constant", (), cdt.name, value=o)
+                    chain.append(spec)
+                    key.append(("const", cdt.name, type(o).__name__, repr(o)))
+                    k = len(key) - 1
+                args.append(spec)
+                arg_keys.append(k)
+            node = NodeSpec("Elementwise", x._shape, ndt.name, inputs=[a.id for a in args], op=op)
+            chain.append(node)
+            key.append(("ew", op, x._shape, ndt.name, tuple(arg_keys)))
+        else:
+            node = NodeSpec("Input", x.shape, x.dtype.name)
+            ext_specs.append(node)
+            ext_arrays.append(x)
+            key.append(("in", x.shape, x.dtype.name))
+        memo[id(x)] = (node, len(key) - 1)
+        return memo[id(x)]
+
+    root_spec, _ = visit(root)
+    return chain, ext_specs, ext_arrays, root_spec, tuple(key)
+
+
+def _materialize(root: "_Lazy") -> None:
+    chain, ext_specs, ext_arrays, root_spec, key = _fused_dag(root)
+    ckey = ("fused", key)
+    kern = _kernel_cache.get(ckey)
+    if kern is None:
+        src, in_names, out_names = SubgraphCUDACodegen().emit(chain, ext_specs, [root_spec])
+        kern = CudaKernel(f"phew_fused_{len(chain)}", in_names, out_names, src)
+        _kernel_cache[ckey] = kern
+    out = kern(
+        inputs=[asarray_device(a) for a in ext_arrays],
+        output_shapes=[root._shape],
+        output_dtypes=[root._dtype],
+        grid=(elementwise_threads(_numel(root._shape)), 1, 1),
+        threadgroup=(256, 1, 1),
+    )
+    object.__setattr__(root, "_mt", out[0]._t)
+    object.__setattr__(root, "_op", None)
+
+
+def _softmax_row_plan(cols: int, itemsize: int):
+    """(threads per row, rows per block, vectors per thread) of the vector
+    softmax kernel in csrc/rows.cu for rows of `cols` elements, or None when
+    that kernel would take its loop form."""
+    E = 16 // itemsize
+    if cols % E:
+        return None
+    nvec = cols // E
+    if nvec > 512 * 8:
+        return None
+    tpr = (((nvec + 3) // 4 + 31) // 32) * 32
+    tpr = builtins_min(builtins_max(tpr, 32), 512)
+    vpt = -(-nvec // tpr)
+    rpb = 1 if tpr >= 128 else 128 // tpr
+    return tpr, rpb, vpt
+
+
+def _fused_softmax(a: "_Lazy"):
+    """softmax over the last axis of a pending elementwise DAG, in one kernel
+    that computes the DAG per row in registers; None when it cannot (the
+    caller then materialises `a` and runs the plain softmax)."""
+    plan = _softmax_row_plan(a.shape[-1], a.dtype.size)
+    if plan is None or a.dtype.code is None:
+        return None
+    tpr, rpb, vpt = plan
+    chain, ext_specs, ext_arrays, root_spec, key = _fused_dag(a)
+    ins = [asarray_device(x) for x in ext_arrays]
+    if builtins.any(x._t.data_ptr() % 16 for x in ins):
+        return None
+    ckey = ("fused_softmax", key, plan)
+    kern = _kernel_cache.get(ckey)
+    if kern is None:
+        try:
+            src, in_names, out_names = SubgraphCUDACodegen().emit_softmax(
+                chain, ext_specs, root_spec, tpr, rpb, vpt)
+        except ValueError:
+            _kernel_cache[ckey] = False
+            return None
+        kern = CudaKernel(f"phew_fused_softmax_{len(chain)}", in_names, out_names, src)
+        _kernel_cache[ckey] = kern
+    if kern is False:
+        return None
+    rows = a.size // a.shape[-1]
+    blocks = -(-rows // rpb)
+    return kern(inputs=ins, output_shapes=[a.shape], output_dtypes=[a.dtype],
+                grid=(blocks * tpr, rpb, 1), threadgroup=(tpr, rpb, 1))[0]
+
+
+def trace_enter() -> None:
+    _trace.depth = getattr(_trace, "depth", 0) + 1
+
+
+def trace_exit() -> None:
+    _trace.depth = getattr(_trace, "depth", 1) - 1
+
+
+def settle(x):
+    """Materialise every pending array in `x` (an array or nested list /
+    tuple / dict of them) and return the same structure of plain arrays."""
+    if isinstance(x, _Lazy):
+        return array._wrap(x._t)
+    if isinstance(x, (list, tuple)):
+        vals = [settle(v) for v in x]
+        return type(x)(vals) if isinstance(x, list) else tuple(vals)
+    if isinstance(x, dict):
+        return {k: settle(v) for k, v in x.items()}
+    return x
 
 
 def _numel(shape) -> int:
@@ -684,6 +888,10 @@ def softmax(a, axis=-1, precise=False, **_) -> array:
     if ax != a.ndim - 1:
         moved = swapaxes(a, ax, a.ndim - 1)
         return swapaxes(softmax(moved, axis=-1), ax, a.ndim - 1)
+    if isinstance(a, _Lazy) and a.pending:
+        fused = _fused_softmax(a)
+        if fused is not None:
+            return fused
     src = asarray_device(a)
     out = empty(a.shape, a.dtype)
     cols = a.shape[-1] if a.ndim else 1
@@ -728,12 +936,22 @@ def ones_like(a) -> array:
 
 
 def eval(*args) -> None:  # noqa: A001  (MLX name)
-    """Arrays are computed eagerly; nothing to force."""
-    return None
+    """Computes pending (deferred, inside ``mx.compile``) arrays among `args`
+    (arrays or nested lists / tuples / dicts of them); others already are."""
+    def force(x):
+        if isinstance(x, _Lazy):
+            x._t  # noqa: B018  (materialises)
+        elif isinstance(x, (list, tuple)):
+            for v in x:
+                force(v)
+        elif isinstance(x, dict):
+            for v in x.values():
+                force(v)
+    force(args)
 
 
 def async_eval(*args) -> None:
-    return None
+    eval(*args)
 
 
 def synchronize(stream=None) -> None:

@@ -1,0 +1,135 @@
+"""mx.compile (deferred, fused elementwise groups) gives the same bits as
+op-by-op evaluation, on the graphs the reference's candidates contain."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _same(mx, f, *args):
+    eager = f(*args)
+    fused = mx.compile(f)(*args)
+    e = [np.asarray(x).view(np.uint8) for x in (eager if isinstance(eager, (list, tuple)) else [eager])]
+    c = [np.asarray(x).view(np.uint8) for x in (fused if isinstance(fused, (list, tuple)) else [fused])]
+    assert len(e) == len(c)
+    for a, b in zip(e, c):
+        assert a.shape == b.shape and np.array_equal(a, b)
+
+
+def _rand(mx, rng, shape, dtype, scale=1.0):
+    from oracle import mlx_cpu
+
+    x = (rng.standard_normal(shape).astype(np.float32) * scale).astype(mlx_cpu._NP[dtype])
+    return mx.array(x)
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16", "float32"])
+def test_rms_norm_tail(mx, dtype):
+    rng = np.random.default_rng(1)
+    x = _rand(mx, rng, (2, 33, 256), dtype)
+    w = _rand(mx, rng, (256,), dtype)
+
+    def f(x, w):
+        t = mx.mean(x * x, axis=[2], keepdims=True)
+        return x * mx.rsqrt(t + mx.array(1e-5, dtype=getattr(mx, dtype))) * w
+
+    _same(mx, f, x, w)
+
+
+def test_attention_scores_scale_mask_softmax(mx):
+    rng = np.random.default_rng(2)
+    q = _rand(mx, rng, (2, 4, 256, 128), "bfloat16")
+    k = _rand(mx, rng, (2, 4, 256, 128), "bfloat16")
+    mask = mx.array(np.triu(np.full((256, 256), -1e9, np.float32), 1)).astype(mx.bfloat16)
+
+    def f(q, k, mask):
+        s = (q @ mx.transpose(k, [0, 1, 3, 2])) * mx.array(0.08838834764831843, dtype=mx.bfloat16)
+        return mx.softmax(s + mask, axis=3)
+
+    _same(mx, f, q, k, mask)
+
+
+def test_swiglu_and_residual(mx):
+    rng = np.random.default_rng(3)
+    a = _rand(mx, rng, (64, 512), "bfloat16", 3)
+    b = _rand(mx, rng, (64, 512), "bfloat16")
+    r = _rand(mx, rng, (64, 1), "bfloat16")
+
+    def f(a, b, r):
+        g = a * r
+        return g * mx.sigmoid(g) * (b * r), a + b
+
+    _same(mx, f, a, b, r)
+
+
+def test_gelu_chain_fp16(mx):
+    rng = np.random.default_rng(4)
+    x = _rand(mx, rng, (128, 1024), "float16")
+    a = _rand(mx, rng, (1024,), "float16")
+    c = _rand(mx, rng, (128, 1024), "float16")
+
+    def f(x, a, c):
+        y = x * a + 0.5
+        g = 0.5 * y * (1.0 + mx.tanh(0.7978845608 * (y + 0.044715 * y * y * y)))
+        return g * mx.sigmoid(c) + x
+
+    _same(mx, f, x, a, c)
+
+
+def test_mixed_dtypes_and_shared_terms(mx):
+    rng = np.random.default_rng(5)
+    h = _rand(mx, rng, (300,), "float16")
+    s = _rand(mx, rng, (300,), "float32")
+
+    def f(h, s):
+        t = h + s
+        return t * t - mx.exp(h * 0.1)
+
+    _same(mx, f, h, s)
+
+
+def test_pending_values_read_inside_the_function(mx):
+    """Views, host reads and non-elementwise consumers force a pending value."""
+    rng = np.random.default_rng(6)
+    x = _rand(mx, rng, (8, 64), "bfloat16")
+
+    def f(x):
+        y = x * 2.0
+        z = mx.reshape(y, [4, 128]) + 1.0
+        total = float(np.asarray(mx.sum(y.astype(mx.float32))))
+        return z * total
+
+    _same(mx, f, x)
+
+
+@pytest.mark.parametrize("dtype,cols", [("bfloat16", 256), ("bfloat16", 8192), ("bfloat16", 1000),
+                                        ("bfloat16", 100), ("float16", 512), ("float32", 2048),
+                                        ("float32", 36)])
+def test_fused_softmax_matches_materialised(mx, dtype, cols):
+    """softmax of a pending elementwise value runs as one kernel (prologue in
+    registers) with the bits of materialise-then-softmax."""
+    rng = np.random.default_rng(cols)
+    s = _rand(mx, rng, (3, 7, cols), dtype, 3.0)
+    m = np.zeros((7, cols), np.float32)
+    m[2, cols // 3:] = -np.inf          # partly masked row
+    m[4, :] = -np.inf                   # fully masked row: NaN, in both paths
+    mask = mx.array(m).astype(getattr(mx, dtype))
+
+    def f(s, mask):
+        return mx.softmax(s * 0.125 + mask, axis=-1)
+
+    _same(mx, f, s, mask)
+
+
+def test_fused_softmax_of_mixed_width_inputs_falls_back(mx):
+    rng = np.random.default_rng(7)
+    s = _rand(mx, rng, (4, 64), "float32")
+    b = _rand(mx, rng, (64,), "bfloat16")
+
+    def f(s, b):
+        return mx.softmax((s + 1.0).astype(mx.bfloat16) * b, axis=-1)
+
+    _same(mx, f, s, b)

@@ -606,6 +606,17 @@ def decoder_specs(dims, seqs):
     return specs
 
 
+def _exception_kinds(verdicts) -> dict:
+    kinds: dict[str, int] = {}
+    for v in verdicts.values():
+        for f in v["failures"]:
+            if "exception=" in f:
+                msg = f.split("exception=", 1)[1]
+                k = "out of memory" if "out of memory" in msg else msg.split("(")[0].strip()[:60]
+                kinds[k] = kinds.get(k, 0) + 1
+    return kinds
+
+
 def run_sweep(args) -> None:
     import torch
 
@@ -671,7 +682,11 @@ def run_sweep(args) -> None:
             "units_per_s": units / max_s, "units": units, "wall_s": max_wall,
             "passed": sorted(c for c, v in verdicts.items() if v["passed"]),
             "failed": sorted(c for c, v in verdicts.items() if not v["passed"]),
-            "missing_shards": len(missing), "clocks": clk.summary(), "journal": str(jdir),
+            "missing_shards": len(missing),
+            # units that failed by raising, by kind (a device out-of-memory here
+            # would be a backend fault, not a verdict)
+            "exception_units": _exception_kinds(verdicts),
+            "clocks": clk.summary(), "journal": str(jdir),
             "gpu_launches": None,
         }
         print(json.dumps(line), flush=True)

@@ -541,7 +541,13 @@ def _fused_dag(root: "_Lazy"):
         memo[id(x)] = (node, len(key) - 1)
         return memo[id(x)]
 
-    root_spec, _ = visit(root)
+    try:
+        root_spec, _ = visit(root)
+    finally:
+        # `visit` refers to itself through its closure cell; break that cycle
+        # so the arrays it reaches are freed by reference counting, not left
+        # for the cyclic collector (they can be tens of GB).
+        visit = None  # noqa: F841
     return chain, ext_specs, ext_arrays, root_spec, tuple(key)
 
 
@@ -938,16 +944,15 @@ def ones_like(a) -> array:
 def eval(*args) -> None:  # noqa: A001  (MLX name)
     """Computes pending (deferred, inside ``mx.compile``) arrays among `args`
     (arrays or nested lists / tuples / dicts of them); others already are."""
-    def force(x):
+    stack = list(args)
+    while stack:
+        x = stack.pop()
         if isinstance(x, _Lazy):
             x._t  # noqa: B018  (materialises)
         elif isinstance(x, (list, tuple)):
-            for v in x:
-                force(v)
+            stack.extend(x)
         elif isinstance(x, dict):
-            for v in x.values():
-                force(v)
-    force(args)
+            stack.extend(x.values())
 
 
 def async_eval(*args) -> None:

@@ -118,3 +118,25 @@ def test_compile_wrapper_returns_plain_arrays_and_restores_state(core):
     with pytest.raises(RuntimeError):
         compile_function(bad)(x)
     assert not core._tracing()
+
+
+def test_dag_walk_leaves_no_reference_cycle(core):
+    """Arrays reached while fusing must be freed by reference counting alone
+    (the cyclic collector does not run on device-memory pressure)."""
+    import gc
+    import weakref
+
+    x = _arr(core, (16,))
+    ref = weakref.ref(x._t)
+    core.trace_enter()
+    try:
+        y = x * 2.0 + 1.0
+        core._fused_dag(y)
+    finally:
+        core.trace_exit()
+    gc.disable()
+    try:
+        del x, y
+        assert ref() is None
+    finally:
+        gc.enable()

@@ -110,6 +110,25 @@ int phew_compile_cache_size(void);
 int phew_rms_norm(const void* x, const void* w, void* y, int64_t rows,
                   int64_t cols, float eps, int dtype, void* stream);
 
+/* y[r, :] = T(w * T((x[r, :] - mean) * rsqrt(var + eps)) + b) with the mean
+ * and the biased variance of the row in fp32; w and b may each be NULL.
+ * x, w, b, y share `dtype`.
+ * Replaces `mx.fast.layer_norm(x, w, b, eps=)` (emit/codegen.py:406-411, node
+ * FastLayerNorm ir/ops.py:165-168 from rules/primitive_subst.py:246-333). */
+int phew_layer_norm(const void* x, const void* w, const void* b, void* y, int64_t rows,
+                    int64_t cols, float eps, int dtype, void* stream);
+
+/* Rotary embedding of x viewed as [rows, D], rows = leading dims x L, row r
+ * at position offset + r % L.  The first `dims` (even) features rotate in
+ * pairs (i, i + dims/2), or (2i, 2i + 1) when traditional, by the angle
+ * position * scale * base^(-2i/dims); the rest are copied.
+ * Replaces `mx.fast.rope(x, dims, traditional=, base=, scale=, offset=)`
+ * (emit/codegen.py:413-419, node FastRoPE ir/ops.py:172-179 from
+ * rules/primitive_subst.py:339-407). */
+int phew_rope(const void* x, void* y, int64_t rows, int64_t D, int64_t L, int dims,
+              int traditional, float base, float scale, int64_t offset, int dtype,
+              void* stream);
+
 /* Row softmax over the last axis, fp32 internally, result in `dtype`.
  * Replaces `mx.softmax(x, axis=-1)` (emit/codegen.py:147-150; Reduce op
  * "softmax" recorded at ir/importer.py:494-506). */
@@ -122,12 +141,27 @@ int phew_softmax(const void* x, void* y, int64_t rows, int64_t cols,
 int phew_reduce(int op, const void* x, void* y, int64_t outer, int64_t red,
                 int64_t inner, int dtype, void* stream);
 
+/* Variance over the middle axis of x viewed as [outer, red, inner]:
+ * fp32 mean, fp32 sum of squared deviations / (red - ddof), rounded once to
+ * `dtype`.  Replaces mx.var (emit/codegen.py:94-146, Reduce op "var"). */
+int phew_reduce_var(const void* x, void* y, int64_t outer, int64_t red, int64_t inner,
+                    int ddof, int dtype, void* stream);
+
 /* dst (contiguous) = src viewed with `shape` and element `src_strides`
  * (ndim <= 8).  Materialises Transpose / non-contiguous views
  * (emit/codegen.py:312-317 `mx.transpose`). */
 int phew_copy_strided(const void* src, void* dst, int ndim,
                       const int64_t* shape, const int64_t* src_strides,
                       int elem_bytes, void* stream);
+
+/* Strided-to-strided copy: element (i0..in) of `shape` moves from
+ * src + sum(ik * src_strides[k]) to dst + sum(ik * dst_strides[k]) (element
+ * units; dst_strides NULL = contiguous).  Writes into views of a larger
+ * array: concatenate / stack / pad / slice_update / roll (codegen.py:94-476
+ * array-manipulation ops). */
+int phew_copy_strided_to(const void* src, void* dst, int ndim, const int64_t* shape,
+                         const int64_t* src_strides, const int64_t* dst_strides,
+                         int elem_bytes, void* stream);
 
 /* Writes `bytes` bytes of `buf` so that the L2 holds none of the caller's
  * data afterwards (buf must be larger than the L2).  Used between timed
@@ -179,6 +213,18 @@ int phew_sdpa_supported(int64_t L, int64_t D, int dtype);
 int phew_sdpa(const void* q, const void* k, const void* v, void* o, int64_t batch_heads,
               int64_t L, int64_t D, float scale, int causal, int dtype, int* error_flag,
               void* stream);
+
+/* ---- group-wise quantised weights --------------------------------------- */
+
+/* out[r, c] = T(scales[r, c / g] * q[r, c] + biases[r, c / g]) for codes q
+ * packed 32 / bits per uint32 along c (code j of a word in bits
+ * [j*bits, (j+1)*bits)), scales / biases [rows, cols / g] in `dtype`.
+ * The weight side of mx.quantized_matmul and of
+ * mx.fast.quantized_scaled_dot_product_attention (emit/codegen.py:428-449;
+ * QuantizedMatMul ir/ops.py:209-218 from rules/quantization.py:37-71). */
+int phew_dequantize(const void* wq, const void* scales, const void* biases, void* out,
+                    int64_t rows, int64_t cols, int group_size, int bits, int dtype,
+                    void* stream);
 
 /* ---- seeded inputs for the verification sweep -------------------------- */
 

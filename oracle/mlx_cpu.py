@@ -28,7 +28,10 @@ Semantics restated here (MLX-CPU):
   ``ir/importer.py:171-186``, records them as Constants of that dtype);
 * reductions, softmax, rms_norm and SDPA accumulate in float64 and round
   once to the output dtype; matmul accumulates in fp32 (BLAS sgemm);
-* ``fast.rms_norm``: y = w * T(x * rsqrt(mean(x^2) + eps)).
+* ``fast.rms_norm``: y = w * T(x * rsqrt(mean(x^2) + eps));
+* ``fast.layer_norm``: y = T(w * T((x - mean) * rsqrt(var + eps)) + b);
+* ``fast.rope``: fp32 angle position * scale * base^(-2i/dims), rotated
+  pairs (i, i + dims/2) or, traditional, (2i, 2i+1).
 """
 
 from __future__ import annotations
@@ -433,6 +436,217 @@ def min(a, axis=None, keepdims=False, **_):  # noqa: A001
     return _reduce(np.min, a, axis, keepdims)
 
 
+def var(a, axis=None, keepdims=False, ddof=0, **_):
+    ax = _axes(a, axis)
+    x = a.v.astype(np.float64)
+    n = int(np.prod([a.shape[i] for i in ax])) if ax else 1
+    with np.errstate(all="ignore"):
+        d = x - x.mean(axis=ax, keepdims=True)
+        r = (d * d).sum(axis=ax, keepdims=keepdims) / (n - ddof)
+    return array.wrap(round_to(r, a.dtype), a.dtype)
+
+
+def std(a, axis=None, keepdims=False, ddof=0, **_):
+    return _ew("sqrt", var(a, axis, keepdims, ddof))
+
+
+def logsumexp(a, axis=None, keepdims=False, **_):
+    x = a.v.astype(np.float64)
+    ax = _axes(a, axis)
+    with np.errstate(all="ignore"):
+        m = np.max(x, axis=ax, keepdims=True)
+        m = np.where(np.isinf(m), 0.0, m)
+        r = np.log(np.sum(np.exp(x - m), axis=ax, keepdims=True)) + m
+    if not keepdims:
+        r = np.squeeze(r, axis=ax)
+    return array.wrap(round_to(r, a.dtype), a.dtype)
+
+
+def _pred(fn):
+    return lambda a, *_, **__: array.wrap(fn(f32(a.v)), as_dtype("bool"))
+
+
+isnan = _pred(np.isnan)
+isinf = _pred(np.isinf)
+isfinite = _pred(np.isfinite)
+isposinf = _pred(np.isposinf)
+isneginf = _pred(np.isneginf)
+
+
+def clip(a, a_min=None, a_max=None, **_):
+    out = a
+    if a_min is not None:
+        out = _ew("maximum", out, a_min)
+    if a_max is not None:
+        out = _ew("minimum", out, a_max)
+    return out
+
+
+def all(a, axis=None, keepdims=False, **_):  # noqa: A001
+    return array.wrap(np.all(a.v != 0, axis=_axes(a, axis), keepdims=keepdims), as_dtype("bool"))
+
+
+def any(a, axis=None, keepdims=False, **_):  # noqa: A001
+    return array.wrap(np.any(a.v != 0, axis=_axes(a, axis), keepdims=keepdims), as_dtype("bool"))
+
+
+def concatenate(arrays, axis=0, **_):
+    res = arrays[0].dtype
+    for x in arrays[1:]:
+        res = _promote(res, x.dtype)
+    if axis is None:
+        return array.wrap(np.concatenate([astype(x, res).v.reshape(-1) for x in arrays]), res)
+    return array.wrap(np.concatenate([astype(x, res).v for x in arrays], axis=axis), res)
+
+
+concat = concatenate
+
+
+def stack(arrays, axis=0, **_):
+    return array.wrap(np.stack([x.v for x in arrays], axis=axis), arrays[0].dtype)
+
+
+def split(a, indices_or_sections, axis=0, **_):
+    return [array.wrap(p, a.dtype) for p in np.split(a.v, indices_or_sections, axis=axis)]
+
+
+def pad(a, pad_width, mode="constant", constant_values=0, **_):
+    if isinstance(pad_width, int):
+        pw = pad_width
+    elif len(pad_width) and isinstance(pad_width[0], int):
+        pw = [tuple(pad_width)] * a.ndim if len(pad_width) == 2 else [(p, p) for p in pad_width]
+    else:
+        pw = [tuple(p) for p in pad_width]
+        if len(pw) == 1:
+            pw = pw * a.ndim
+    return array.wrap(np.pad(a.v, pw, constant_values=constant_values), a.dtype)
+
+
+def tile(a, reps, **_):
+    return array.wrap(np.tile(a.v, reps), a.dtype)
+
+
+def repeat(a, repeats, axis=None, **_):
+    return array.wrap(np.repeat(a.v, repeats, axis=axis), a.dtype)
+
+
+def roll(a, shift, axis=None, **_):
+    return array.wrap(np.roll(a.v, shift, axis=axis), a.dtype)
+
+
+def tril(x, k=0, **_):
+    return array.wrap(np.tril(x.v, k), x.dtype)
+
+
+def triu(x, k=0, **_):
+    return array.wrap(np.triu(x.v, k), x.dtype)
+
+
+def cumsum(a, axis=None, reverse=False, inclusive=True, **_):
+    x = a.v.reshape(-1) if axis is None else a.v
+    ax = 0 if axis is None else axis
+    if reverse:
+        x = np.flip(x, ax)
+    r = np.cumsum(x.astype(np.float64) if a.dtype.kind == "f" else x, axis=ax)
+    if not inclusive:
+        r = np.roll(r, 1, ax)
+        idx = [np.s_[:]] * r.ndim
+        idx[ax] = 0
+        r[tuple(idx)] = 0
+    if reverse:
+        r = np.flip(r, ax)
+    return array.wrap(round_to(r, a.dtype) if a.dtype.kind == "f" else r.astype(a.dtype.np), a.dtype)
+
+
+def sort(a, axis=-1, **_):
+    return array.wrap(np.sort(a.v.reshape(-1) if axis is None else a.v, axis=-1 if axis is None else axis,
+                              kind="stable"), a.dtype)
+
+
+def argsort(a, axis=-1, **_):
+    return array.wrap(np.argsort(a.v.reshape(-1) if axis is None else a.v, axis=-1 if axis is None else axis,
+                                 kind="stable").astype(np.int32), as_dtype("int32"))
+
+
+def topk(a, k, axis=-1, **_):
+    s = np.sort(a.v, axis=axis)
+    return array.wrap(np.take(s, np.arange(s.shape[axis] - k, s.shape[axis]), axis=axis), a.dtype)
+
+
+def argmax(a, axis=None, keepdims=False, **_):
+    r = np.argmax(a.v, axis=axis, keepdims=keepdims) if axis is not None else np.argmax(a.v)
+    return array.wrap(np.asarray(r).astype(np.uint32), as_dtype("uint32"))
+
+
+def argmin(a, axis=None, keepdims=False, **_):
+    r = np.argmin(a.v, axis=axis, keepdims=keepdims) if axis is not None else np.argmin(a.v)
+    return array.wrap(np.asarray(r).astype(np.uint32), as_dtype("uint32"))
+
+
+def take_along_axis(a, indices, axis=None, **_):
+    if axis is None:
+        return array.wrap(np.take_along_axis(a.v.reshape(-1), indices.v.reshape(-1).astype(np.int64), 0), a.dtype)
+    return array.wrap(np.take_along_axis(a.v, indices.v.astype(np.int64), axis), a.dtype)
+
+
+def take(a, indices, axis=None, **_):
+    idx = indices.v if isinstance(indices, array) else np.asarray(indices)
+    return array.wrap(np.take(a.v, idx.astype(np.int64), axis=axis), a.dtype)
+
+
+def moveaxis(a, source, destination, **_):
+    return array.wrap(np.moveaxis(a.v, source, destination), a.dtype)
+
+
+def flatten(a, start_axis=0, end_axis=-1, **_):
+    if a.ndim == 0:
+        return reshape(a, (1,))
+    s = start_axis % a.ndim
+    e = end_axis % a.ndim
+    shape = list(a.shape[:s]) + [int(np.prod(a.shape[s:e + 1]))] + list(a.shape[e + 1:])
+    return reshape(a, shape)
+
+
+def bitwise_and(a, b, **_):
+    return array.wrap(np.bitwise_and(a.v, b.v if isinstance(b, array) else b), a.dtype)
+
+
+def bitwise_or(a, b, **_):
+    return array.wrap(np.bitwise_or(a.v, b.v if isinstance(b, array) else b), a.dtype)
+
+
+def bitwise_xor(a, b, **_):
+    return array.wrap(np.bitwise_xor(a.v, b.v if isinstance(b, array) else b), a.dtype)
+
+
+def left_shift(a, b, **_):
+    return array.wrap(np.left_shift(a.v, b.v if isinstance(b, array) else b), a.dtype)
+
+
+def right_shift(a, b, **_):
+    return array.wrap(np.right_shift(a.v, b.v if isinstance(b, array) else b), a.dtype)
+
+
+def dequantize(w, scales, biases, group_size=64, bits=4, **_):
+    """Affine group-wise codes, 32/bits per uint32 along the last axis (code j
+    of a word in bits [j*bits, (j+1)*bits)) -> T(fma(scale, q, bias))."""
+    per = 32 // bits
+    words = np.asarray(w.v).astype(np.uint64)
+    shifts = (np.arange(per, dtype=np.uint64) * np.uint64(bits))
+    q = ((words[..., None] >> shifts) & np.uint64((1 << bits) - 1)).reshape(*words.shape[:-1], -1)
+    s = np.repeat(f32(scales.v).astype(np.float64), group_size, axis=-1)
+    b = np.repeat(f32(biases.v).astype(np.float64), group_size, axis=-1)
+    r = (s * q.astype(np.float64) + b).astype(np.float32)
+    return array.wrap(round_to(r, scales.dtype), scales.dtype)
+
+
+def quantized_matmul(x, w, scales=None, biases=None, transpose=True, group_size=64, bits=4, **_):
+    if scales is None or biases is None:
+        raise TypeError("quantized_matmul: scales and biases are required for affine quantization")
+    wd = dequantize(w, scales, biases, group_size, bits)
+    return matmul(astype(x, wd.dtype), swapaxes(wd, -1, -2) if transpose else wd)
+
+
 def _softmax64(x: np.ndarray, axis: int) -> np.ndarray:
     with np.errstate(all="ignore"):
         m = np.max(x, axis=axis, keepdims=True)
@@ -505,6 +719,56 @@ def rms_norm(x: array, weight: array | None = None, eps: float = 1e-5) -> array:
     return array.wrap(round_to(f32(weight.v) * f32(n), x.dtype), x.dtype)
 
 
+def layer_norm(x: array, weight: array | None = None, bias: array | None = None,
+               eps: float = 1e-5) -> array:
+    """fast.layer_norm (``ir/ops.py:165-168``): float64 mean and biased
+    variance of the row, n = T((x - mean) * rsqrt(var + eps)), then
+    y = T(fp32(w * n) + b) with weight / bias omitted when None."""
+    cols = x.shape[-1]
+    for p, nm in ((weight, "weight"), (bias, "bias")):
+        if p is not None and tuple(p.shape) != (cols,):
+            raise ValueError(f"layer_norm: {nm} shape {tuple(p.shape)} != ({cols},)")
+    xv = f32(x.v).astype(np.float64)
+    mean = xv.mean(axis=-1, keepdims=True)
+    var = ((xv - mean) ** 2).mean(axis=-1, keepdims=True)
+    n = f32(round_to((xv - mean) / np.sqrt(var + eps), x.dtype))
+    if weight is not None:
+        n = (n * f32(weight.v)).astype(np.float32)
+    if bias is not None:
+        n = (n + f32(bias.v)).astype(np.float32)
+    return array.wrap(round_to(n, x.dtype), x.dtype)
+
+
+def rope(x: array, dims: int, *, traditional: bool = False, base: float = 10000.0,
+         scale: float = 1.0, offset: int = 0) -> array:
+    """fast.rope (``ir/ops.py:172-179``): positions offset + l along the
+    second-to-last axis; pair i of the first `dims` features, (i, i + dims/2)
+    or (2i, 2i+1) when traditional, rotates by the fp32 angle
+    fp32(fp32(pos * scale) * fp32(base^(-2i/dims))); each product and sum
+    in fp32; the rest of the features are copied."""
+    xv = f32(x.v)
+    shp = xv.shape
+    D = shp[-1]
+    L = shp[-2] if len(shp) >= 2 else 1
+    half = dims // 2
+    out = xv.copy()
+    if half:
+        inv = np.power(np.float64(base), -2.0 * np.arange(half) / dims).astype(np.float32)
+        pos = (np.float32(offset) + np.arange(L, dtype=np.float32)).astype(np.float32)
+        a = ((pos * np.float32(scale)).astype(np.float32)[:, None] * inv[None, :]).astype(np.float32)
+        c = np.cos(a.astype(np.float64)).astype(np.float32)
+        sn = np.sin(a.astype(np.float64)).astype(np.float32)
+        if traditional:
+            iu, iv = np.arange(half) * 2, np.arange(half) * 2 + 1
+        else:
+            iu, iv = np.arange(half), np.arange(half) + half
+        u, v = xv[..., iu], xv[..., iv]
+        out[..., iu] = ((u * c).astype(np.float32) - (v * sn).astype(np.float32)).astype(np.float32)
+        out[..., iv] = ((u * sn).astype(np.float32) + (v * c).astype(np.float32)).astype(np.float32)
+    _ = D
+    return array.wrap(round_to(out, x.dtype), x.dtype)
+
+
 def sdpa(q: array, k: array, v: array, scale: float, mask: Any = None) -> array:
     """softmax(q k^T * scale [+ mask]) v, fp32 matmuls, float64 softmax."""
     s = np.matmul(f32(q.v), np.swapaxes(f32(k.v), -1, -2)) * np.float32(scale)
@@ -557,6 +821,8 @@ def cuda_kernel(name, input_names, output_names, source, header="", **_):
 
 fast = types.SimpleNamespace(
     rms_norm=rms_norm,
+    layer_norm=lambda x, weight=None, bias=None, eps=1e-5, **_: layer_norm(x, weight, bias, eps),
+    rope=lambda x, dims, **kw: rope(x, dims, **kw),
     scaled_dot_product_attention=lambda q, k, v, *, scale=1.0, mask=None, **_: sdpa(q, k, v, scale, mask),
     cuda_kernel=cuda_kernel,
 )

@@ -37,7 +37,12 @@ EXPORTED_SYMBOLS = (
     "phew_launch",
     "phew_compile_cache_size",
     "phew_rms_norm",
+    "phew_layer_norm",
+    "phew_rope",
     "phew_softmax",
+    "phew_reduce_var",
+    "phew_dequantize",
+    "phew_copy_strided_to",
     "phew_reduce",
     "phew_copy_strided",
     "phew_l2_flush",
@@ -112,7 +117,18 @@ _SIGNATURES = {
     ),
     "phew_compile_cache_size": ([], _int),
     "phew_rms_norm": ([_vp, _vp, _vp, _i64, _i64, ctypes.c_float, _int, _vp], _int),
+    "phew_layer_norm": ([_vp, _vp, _vp, _vp, _i64, _i64, ctypes.c_float, _int, _vp], _int),
+    "phew_rope": (
+        [_vp, _vp, _i64, _i64, _i64, _int, _int, ctypes.c_float, ctypes.c_float, _i64, _int, _vp],
+        _int,
+    ),
     "phew_softmax": ([_vp, _vp, _i64, _i64, _int, _vp], _int),
+    "phew_reduce_var": ([_vp, _vp, _i64, _i64, _i64, _int, _int, _vp], _int),
+    "phew_dequantize": ([_vp, _vp, _vp, _vp, _i64, _i64, _int, _int, _int, _vp], _int),
+    "phew_copy_strided_to": (
+        [_vp, _vp, _int, ctypes.POINTER(_i64), ctypes.POINTER(_i64), ctypes.POINTER(_i64), _int, _vp],
+        _int,
+    ),
     "phew_reduce": ([_int, _vp, _vp, _i64, _i64, _i64, _int, _vp], _int),
     "phew_copy_strided": (
         [_vp, _vp, _int, ctypes.POINTER(_i64), ctypes.POINTER(_i64), _int, _vp],

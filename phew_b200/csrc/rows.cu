@@ -1,4 +1,4 @@
-// Row-wise primitives: rms_norm, softmax and axis reductions.
+// Row-wise primitives: rms_norm, layer_norm, softmax and axis reductions.
 //
 // Layout: the reduced axis is the innermost, contiguous one ([rows, cols],
 // row-major) except for phew_reduce's strided form ([outer, red, inner]).
@@ -122,6 +122,94 @@ __global__ void rms_norm_loop_kernel(const T* __restrict__ x, const T* __restric
     const float n = __fmul_rn(to_f32(xr[c]), r);
     yr[c] = from_f32<T>(w != nullptr ? __fmul_rn(to_f32(w[c]), round_to<T>(n)) : n);
   }
+}
+
+// ---------------------------------------------------------------------------
+// layer_norm: n = T((x - mean) * rsqrt(var + eps)), y = T(w * n + b)
+// (mean and the biased variance in fp32 over the row; w, b optional)
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ float ln_out(float n, const T* w, const T* b, int64_t c) {
+  float y = round_to<T>(n);
+  if (w != nullptr) y = __fmul_rn(to_f32(w[c]), y);
+  if (b != nullptr) y = __fadd_rn(y, to_f32(b[c]));
+  return y;
+}
+
+template <typename T, int VPT>
+__global__ void __launch_bounds__(512) layer_norm_vec_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                                             const T* __restrict__ b, T* __restrict__ y,
+                                                             int64_t rows, int64_t cols, float eps) {
+  __shared__ float smem[32 * 32];
+  constexpr int E = Vec<T>::E;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.y + threadIdx.y;
+  const bool active = row < rows;
+  const int64_t nvec = cols / E;
+  const T* xr = x + row * cols;
+  float v[VPT][E];
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t vi = threadIdx.x + static_cast<int64_t>(j) * blockDim.x;
+    if (active && vi < nvec) {
+      load_vec<T>(xr + vi * E, v[j]);
+#pragma unroll
+      for (int i = 0; i < E; ++i) sum += v[j][i];
+    }
+  }
+  const float mean = row_allreduce<false>(sum, smem) / static_cast<float>(cols);
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t vi = threadIdx.x + static_cast<int64_t>(j) * blockDim.x;
+    if (active && vi < nvec) {
+#pragma unroll
+      for (int i = 0; i < E; ++i) {
+        v[j][i] = __fsub_rn(v[j][i], mean);
+        ss = fmaf(v[j][i], v[j][i], ss);
+      }
+    }
+  }
+  const float var = row_allreduce<false>(ss, smem) / static_cast<float>(cols);
+  const float r = 1.0f / sqrtf(var + eps);
+  if (!active) return;
+  T* yr = y + row * cols;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t vi = threadIdx.x + static_cast<int64_t>(j) * blockDim.x;
+    if (vi < nvec) {
+      float o[E];
+#pragma unroll
+      for (int i = 0; i < E; ++i) o[i] = ln_out<T>(__fmul_rn(v[j][i], r), w, b, vi * E + i);
+      store_vec<T>(yr + vi * E, o);
+    }
+  }
+}
+
+template <typename T>
+__global__ void layer_norm_loop_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                       const T* __restrict__ b, T* __restrict__ y, int64_t rows,
+                                       int64_t cols, float eps) {
+  __shared__ float smem[32 * 32];
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.y + threadIdx.y;
+  const bool active = row < rows;
+  const T* xr = x + row * cols;
+  float sum = 0.f;
+  if (active)
+    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) sum += to_f32(xr[c]);
+  const float mean = row_allreduce<false>(sum, smem) / static_cast<float>(cols);
+  float ss = 0.f;
+  if (active)
+    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+      const float d = __fsub_rn(to_f32(xr[c]), mean);
+      ss = fmaf(d, d, ss);
+    }
+  const float var = row_allreduce<false>(ss, smem) / static_cast<float>(cols);
+  const float r = 1.0f / sqrtf(var + eps);
+  if (!active) return;
+  T* yr = y + row * cols;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x)
+    yr[c] = from_f32<T>(ln_out<T>(__fmul_rn(__fsub_rn(to_f32(xr[c]), mean), r), w, b, c));
 }
 
 // ---------------------------------------------------------------------------
@@ -324,6 +412,36 @@ int rms_norm_typed(const void* x, const void* w, void* y, int64_t rows, int64_t 
 }
 
 template <typename T>
+int layer_norm_typed(const void* x, const void* w, const void* b, void* y, int64_t rows, int64_t cols,
+                     float eps, cudaStream_t st) {
+  constexpr int E = Vec<T>::E;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+  const int64_t nvec = cols / E;
+  const T* xp = static_cast<const T*>(x);
+  const T* wp = static_cast<const T*>(w);
+  const T* bp = static_cast<const T*>(b);
+  T* yp = static_cast<T*>(y);
+  if (aligned && cols % E == 0 && nvec <= static_cast<int64_t>(kMaxTPR) * kMaxVPT) {
+    RowLaunch L = plan_rows(nvec);
+    dim3 block(L.tpr, L.rpb), grid(static_cast<unsigned>((rows + L.rpb - 1) / L.rpb));
+    switch (L.vpt) {
+#define PHEW_CASE(N) \
+  case N: layer_norm_vec_kernel<T, N><<<grid, block, 0, st>>>(xp, wp, bp, yp, rows, cols, eps); break;
+      PHEW_CASE(1) PHEW_CASE(2) PHEW_CASE(3) PHEW_CASE(4)
+      PHEW_CASE(5) PHEW_CASE(6) PHEW_CASE(7) PHEW_CASE(8)
+#undef PHEW_CASE
+      default: return set_error(PHEW_ERR_INVALID, "layer_norm: bad plan");
+    }
+    return launch_status("layer_norm_vec_kernel");
+  }
+  const int tpr = cols >= 1024 ? 256 : 32;
+  const int rpb = tpr == 32 ? 4 : 1;
+  dim3 block(tpr, rpb), grid(static_cast<unsigned>((rows + rpb - 1) / rpb));
+  layer_norm_loop_kernel<T><<<grid, block, 0, st>>>(xp, wp, bp, yp, rows, cols, eps);
+  return launch_status("layer_norm_loop_kernel");
+}
+
+template <typename T>
 int softmax_typed(const void* x, void* y, int64_t rows, int64_t cols, cudaStream_t st) {
   constexpr int E = Vec<T>::E;
   const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
@@ -348,6 +466,69 @@ int softmax_typed(const void* x, void* y, int64_t rows, int64_t cols, cudaStream
   dim3 block(tpr, rpb), grid(static_cast<unsigned>((rows + rpb - 1) / rpb));
   softmax_loop_kernel<T><<<grid, block, 0, st>>>(xp, yp, rows, cols);
   return launch_status("softmax_loop_kernel");
+}
+
+// Variance over the middle axis: fp32 mean, then the fp32 sum of squared
+// deviations divided by (red - ddof), rounded once to T.
+template <typename T>
+__global__ void var_rows_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t rows, int64_t red,
+                                float denom) {
+  __shared__ float smem[32 * 32];
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.y + threadIdx.y;
+  const bool active = row < rows;
+  const T* xr = x + row * red;
+  float sum = 0.f;
+  if (active)
+    for (int64_t c = threadIdx.x; c < red; c += blockDim.x) sum += to_f32(xr[c]);
+  const float mean = row_allreduce<false>(sum, smem) / static_cast<float>(red);
+  float ss = 0.f;
+  if (active)
+    for (int64_t c = threadIdx.x; c < red; c += blockDim.x) {
+      const float d = __fsub_rn(to_f32(xr[c]), mean);
+      ss = fmaf(d, d, ss);
+    }
+  ss = row_allreduce<false>(ss, smem);
+  if (active && threadIdx.x == 0) y[row] = from_f32<T>(__fdiv_rn(ss, denom));
+}
+
+template <typename T>
+__global__ void var_cols_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t outer, int64_t red,
+                                int64_t inner, float denom) {
+  const int64_t total = outer * inner;
+  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t o = idx / inner, i = idx % inner;
+    const T* p = x + o * red * inner + i;
+    float sum = 0.f;
+    for (int64_t r = 0; r < red; ++r) sum += to_f32(p[r * inner]);
+    const float mean = sum / static_cast<float>(red);
+    float ss = 0.f;
+    for (int64_t r = 0; r < red; ++r) {
+      const float d = __fsub_rn(to_f32(p[r * inner]), mean);
+      ss = fmaf(d, d, ss);
+    }
+    y[idx] = from_f32<T>(__fdiv_rn(ss, denom));
+  }
+}
+
+template <typename T>
+int var_typed(const void* x, void* y, int64_t outer, int64_t red, int64_t inner, float denom,
+              cudaStream_t st) {
+  const T* xp = static_cast<const T*>(x);
+  T* yp = static_cast<T*>(y);
+  if (inner == 1) {
+    const int tpr = red >= 1024 ? 256 : 32;
+    const int rpb = tpr == 32 ? 4 : 1;
+    dim3 block(tpr, rpb), grid(static_cast<unsigned>((outer + rpb - 1) / rpb));
+    var_rows_kernel<T><<<grid, block, 0, st>>>(xp, yp, outer, red, denom);
+    return launch_status("var_rows_kernel");
+  }
+  const int64_t total = outer * inner;
+  int64_t blocks = (total + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(sm_count_current()) * 16;
+  if (blocks > cap) blocks = cap;
+  var_cols_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, st>>>(xp, yp, outer, red, inner, denom);
+  return launch_status("var_cols_kernel");
 }
 
 template <typename T>
@@ -390,6 +571,21 @@ extern "C" int phew_rms_norm(const void* x, const void* w, void* y, int64_t rows
   }
 }
 
+extern "C" int phew_layer_norm(const void* x, const void* w, const void* b, void* y, int64_t rows,
+                               int64_t cols, float eps, int dtype, void* stream) {
+  PHEW_REQUIRE(x && y, "phew_layer_norm: null pointer");
+  PHEW_REQUIRE(rows >= 0 && cols > 0, "phew_layer_norm: bad shape");
+  PHEW_REQUIRE(rows < (1LL << 31) * 1024, "phew_layer_norm: too many rows");
+  if (rows == 0) return PHEW_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case PHEW_F32: return layer_norm_typed<float>(x, w, b, y, rows, cols, eps, st);
+    case PHEW_F16: return layer_norm_typed<f16>(x, w, b, y, rows, cols, eps, st);
+    case PHEW_BF16: return layer_norm_typed<bf16>(x, w, b, y, rows, cols, eps, st);
+    default: return set_error(PHEW_ERR_INVALID, "phew_layer_norm: bad dtype");
+  }
+}
+
 extern "C" int phew_softmax(const void* x, void* y, int64_t rows, int64_t cols, int dtype,
                             void* stream) {
   PHEW_REQUIRE(x && y, "phew_softmax: null pointer");
@@ -401,6 +597,21 @@ extern "C" int phew_softmax(const void* x, void* y, int64_t rows, int64_t cols, 
     case PHEW_F16: return softmax_typed<f16>(x, y, rows, cols, st);
     case PHEW_BF16: return softmax_typed<bf16>(x, y, rows, cols, st);
     default: return set_error(PHEW_ERR_INVALID, "phew_softmax: bad dtype");
+  }
+}
+
+extern "C" int phew_reduce_var(const void* x, void* y, int64_t outer, int64_t red, int64_t inner,
+                               int ddof, int dtype, void* stream) {
+  PHEW_REQUIRE(x && y, "phew_reduce_var: null pointer");
+  PHEW_REQUIRE(outer >= 0 && red > 0 && inner > 0, "phew_reduce_var: bad shape");
+  if (outer == 0) return PHEW_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float denom = static_cast<float>(red - ddof);
+  switch (dtype) {
+    case PHEW_F32: return var_typed<float>(x, y, outer, red, inner, denom, st);
+    case PHEW_F16: return var_typed<f16>(x, y, outer, red, inner, denom, st);
+    case PHEW_BF16: return var_typed<bf16>(x, y, outer, red, inner, denom, st);
+    default: return set_error(PHEW_ERR_INVALID, "phew_reduce_var: bad dtype");
   }
 }
 

@@ -267,13 +267,27 @@ _LOGICAL = {"logical_and": "&&", "logical_or": "||"}
 
 _INT_BINARY = {"add": "+", "sub": "-", "mul": "*"}
 
+# Bool-valued tests of a float (NaN / infinity classification).
+_PREDICATE = {
+    "isnan": "isnan({a})",
+    "isinf": "isinf({a})",
+    "isfinite": "isfinite({a})",
+    "isposinf": "({a} == __int_as_float(0x7f800000))",
+    "isneginf": "({a} == __int_as_float(0xff800000u))",
+}
+# Integer / bool bit operations.
+_BITWISE = {"bitwise_and": "&", "bitwise_or": "|", "bitwise_xor": "^", "left_shift": "<<",
+            "right_shift": ">>"}
+
 SUPPORTED_OPS = (
     set(_UNARY_F)
     | set(_UNARY_F_PRECISE)
     | set(_BINARY_F)
     | set(_COMPARE)
     | set(_LOGICAL)
-    | {"logical_not", "where"}
+    | {"logical_not", "where", "bitwise_invert"}
+    | set(_PREDICATE)
+    | set(_BITWISE)
     | set(ALIASES)
 )
 
@@ -343,6 +357,16 @@ def scalar_expr(
         return f"(({ct})(!{args[0]}))"
     if op == "where":
         return f"(({ct})({args[0]} ? {args[1]} : {args[2]}))"
+    if op in _PREDICATE:
+        return f"(({ct}){_PREDICATE[op].format(a=_to_float(args[0], arg_dtypes[0]))})"
+    if op in _BITWISE:
+        if arg_dtypes[0] in FLOAT_TYPES or arg_dtypes[1] in FLOAT_TYPES:
+            raise ValueError(f"cuda_codegen: {op} of floating-point values")
+        return f"(({ct})({args[0]} {_BITWISE[op]} {args[1]}))"
+    if op == "bitwise_invert":
+        if arg_dtypes[0] in FLOAT_TYPES:
+            raise ValueError("cuda_codegen: bitwise_invert of floating-point values")
+        return f"(({ct})(!{args[0]}))" if out_dt == "bool" else f"(({ct})(~{args[0]}))"
     if out_dt == "bool":
         raise ValueError(f"cuda_codegen: unhandled bool op {op!r}")
     if op in _INT_BINARY and len(args) == 2:
@@ -935,7 +959,7 @@ def _check_arity(op: str, n: int) -> None:
     if op == "where":
         if n != 3:
             raise ValueError("cuda_codegen: where needs 3 inputs")
-    elif op in _BINARY_F or op in _COMPARE or op in _LOGICAL:
+    elif op in _BINARY_F or op in _COMPARE or op in _LOGICAL or op in _BITWISE:
         if n != 2:
             raise ValueError(f"cuda_codegen: {op} needs 2 inputs, got {n}")
     elif n != 1:

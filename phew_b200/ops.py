@@ -42,6 +42,163 @@ def rms_norm(x, weight=None, eps: float = 1e-5) -> array:
     return out
 
 
+def _param(p, x, cols: int, what: str):
+    if p is None:
+        return None, None
+    a = asarray_device(p)
+    if a.dtype is not x.dtype:
+        a = a.astype(x.dtype)
+    if a.shape != (cols,):
+        raise ValueError(f"{what} shape {a.shape} != ({cols},)")
+    return a, ctypes.c_void_p(a._t.data_ptr())
+
+
+def layer_norm(x, weight=None, bias=None, eps: float = 1e-5) -> array:
+    """``mx.fast.layer_norm(x, weight, bias, eps)`` over the last axis.
+
+    n = cast((x - mean) * rsqrt(var + eps)) with fp32 mean and biased
+    variance, y = cast(weight * n + bias); weight / bias None -> omitted.
+    Node FastLayerNorm (phew ``ir/ops.py:165-168``), matched by
+    ``rules/primitive_subst.py:246-333``, emitted at ``emit/codegen.py:406-411``.
+    """
+    x = asarray_device(x)
+    if x.dtype.code is None:
+        raise TypeError(f"layer_norm: unsupported dtype {x.dtype.name}")
+    cols = x.shape[-1]
+    rows = x.size // max(cols, 1)
+    w, wptr = _param(weight, x, cols, "layer_norm: weight")
+    b, bptr = _param(bias, x, cols, "layer_norm: bias")
+    out = empty(x.shape, x.dtype)
+    if x.size:
+        _native.call(
+            "phew_layer_norm", ctypes.c_void_p(x._t.data_ptr()), wptr, bptr,
+            ctypes.c_void_p(out._t.data_ptr()), rows, cols, ctypes.c_float(eps), x.dtype.code,
+            _stream(),
+        )
+    _ = (w, b)
+    return out
+
+
+def rope(x, dims: int, *, traditional: bool = False, base: float = 10000.0, scale: float = 1.0,
+         offset: int = 0) -> array:
+    """``mx.fast.rope(x, dims, traditional=, base=, scale=, offset=)``.
+
+    Positions run along the second-to-last axis from `offset`; the first
+    `dims` features of the last axis rotate in pairs (i, i + dims/2), or
+    (2i, 2i+1) when `traditional`, by position * scale * base^(-2i/dims).
+    Node FastRoPE (phew ``ir/ops.py:172-179``), matched by
+    ``rules/primitive_subst.py:339-407``, emitted at ``emit/codegen.py:413-419``.
+    """
+    x = asarray_device(x)
+    if x.dtype.code is None:
+        raise TypeError(f"rope: unsupported dtype {x.dtype.name}")
+    D = x.shape[-1] if x.ndim else 1
+    L = x.shape[-2] if x.ndim >= 2 else 1
+    rows = x.size // max(D, 1)
+    out = empty(x.shape, x.dtype)
+    if x.size:
+        _native.call(
+            "phew_rope", ctypes.c_void_p(x._t.data_ptr()), ctypes.c_void_p(out._t.data_ptr()),
+            rows, D, L, int(dims), 1 if traditional else 0, ctypes.c_float(base),
+            ctypes.c_float(scale), int(offset), x.dtype.code, _stream(),
+        )
+    return out
+
+
+def dequantize(w, scales, biases, group_size: int = 64, bits: int = 4) -> array:
+    """``mx.dequantize``: affine group-wise codes packed 32/bits per uint32
+    along the last axis -> scales * q + biases in the scales' dtype."""
+    import torch
+
+    w = asarray_device(w)
+    s = asarray_device(scales)
+    b = asarray_device(biases)
+    if s.dtype.code is None:
+        raise TypeError(f"dequantize: unsupported scale dtype {s.dtype.name}")
+    if b.dtype is not s.dtype:
+        b = b.astype(s.dtype)
+    per = 32 // int(bits)
+    cols = w.shape[-1] * per
+    rows = w.size // max(w.shape[-1], 1)
+    if s.shape[-1] * int(group_size) != cols or s.size != rows * (cols // int(group_size)):
+        raise ValueError(f"dequantize: scales {s.shape} do not match codes {w.shape} at "
+                         f"group_size {group_size}, bits {bits}")
+    wt = w._t if w._t.dtype in (torch.uint32, torch.int32) else w._t.to(torch.int32)
+    out = empty(tuple(w.shape[:-1]) + (cols,), s.dtype)
+    if out.size:
+        _native.call(
+            "phew_dequantize", ctypes.c_void_p(wt.data_ptr()), ctypes.c_void_p(s._t.data_ptr()),
+            ctypes.c_void_p(b._t.data_ptr()), ctypes.c_void_p(out._t.data_ptr()), rows, cols,
+            int(group_size), int(bits), s.dtype.code, _stream(),
+        )
+    return out
+
+
+def quantized_matmul(x, w, scales=None, biases=None, transpose: bool = True, group_size: int = 64,
+                     bits: int = 4, **_) -> array:
+    """``mx.quantized_matmul(x, w, scales, biases, transpose=, group_size=, bits=)``:
+    x @ dequantize(w).T (transpose) or x @ dequantize(w).  The weight is
+    expanded by ``phew_dequantize`` and the product runs on the tcgen05
+    GEMM.  Like MLX it needs the scales (the reference's QuantizationPass
+    emits two-argument calls, ``rules/quantization.py:62-69``, which raise
+    here as they would in MLX)."""
+    from .mx.core import swapaxes
+
+    if scales is None or biases is None:
+        raise TypeError("quantized_matmul: scales and biases are required for affine quantization")
+    wd = dequantize(w, scales, biases, group_size, bits)
+    xd = asarray_device(x)
+    if xd.dtype is not wd.dtype:
+        xd = xd.astype(wd.dtype)
+    return matmul(xd, swapaxes(wd, -1, -2) if transpose else wd)
+
+
+def quantized_sdpa(q, k, v, scale_k, biases_k, scale_v, biases_v, *, scale: float = 1.0,
+                   bits: int = 4, group_size: int = 64, mask=None) -> array:
+    """``mx.fast.quantized_scaled_dot_product_attention``: k and v quantised
+    along the head dimension, expanded by ``phew_dequantize``, then the
+    attention kernel."""
+    kd = dequantize(k, scale_k, biases_k, group_size, bits)
+    vd = dequantize(v, scale_v, biases_v, group_size, bits)
+    qd = asarray_device(q)
+    if qd.dtype is not kd.dtype:
+        qd = qd.astype(kd.dtype)
+    return scaled_dot_product_attention(qd, kd, vd, scale=scale, mask=mask)
+
+
+def quantize(w, group_size: int = 64, bits: int = 4):
+    """``mx.quantize``: affine group-wise quantisation along the last axis ->
+    (codes packed 32/bits per uint32, scales, biases).  Per group:
+    scale = (max - min) / (2^bits - 1), bias = min, q = round((w - bias) /
+    scale) clipped to [0, 2^bits - 1].  An input-preparation helper (torch
+    ops on the device buffer), not on the candidate path."""
+    import torch
+
+    from .mx.core import array as _array
+
+    w = asarray_device(w)
+    g, nb = int(group_size), int(bits)
+    per = 32 // nb
+    cols = w.shape[-1]
+    if cols % g or cols % per:
+        raise ValueError("quantize: the last axis must be a multiple of group_size and of 32/bits")
+    t = w._t.float().reshape(-1, cols // g, g)
+    lo = t.amin(-1, keepdim=True)
+    hi = t.amax(-1, keepdim=True)
+    n_bins = (1 << nb) - 1
+    sc = torch.clamp((hi - lo) / n_bins, min=1e-8)
+    sc = sc.to(w._t.dtype).float()
+    bi = lo.to(w._t.dtype).float()
+    qv = torch.clamp(torch.round((t - bi) / sc), 0, n_bins).to(torch.int64).reshape(-1, cols // per, per)
+    shifts = (torch.arange(per, device=qv.device, dtype=torch.int64) * nb)
+    words = (qv << shifts).sum(-1).to(torch.int64)
+    words = torch.where(words >= 2**31, words - 2**32, words).to(torch.int32).view(torch.uint32)
+    shp = tuple(w.shape[:-1])
+    return (_array._wrap(words.reshape(shp + (cols // per,))),
+            _array._wrap(sc.to(w._t.dtype).reshape(shp + (cols // g,))),
+            _array._wrap(bi.to(w._t.dtype).reshape(shp + (cols // g,))))
+
+
 _error_flags: dict[int, object] = {}
 
 

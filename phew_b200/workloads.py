@@ -64,6 +64,31 @@ def rms_norm_fn(mx):
     return fn
 
 
+def layer_norm_fn(mx):
+    """A layer norm written out with mean / var, the shape the reference's
+    primitive substitution rewrites to ``mx.fast.layer_norm``
+    (``rules/primitive_subst.py:246-333``)."""
+    def fn(x, w, b):
+        mu = mx.mean(x, axis=-1, keepdims=True)
+        var = mx.var(x, axis=-1, keepdims=True)
+        return (x - mu) / mx.sqrt(var + 1e-5) * w + b
+
+    return fn
+
+
+def rope_fn(mx, half: int = 64):
+    """Rotary embedding written out with cos / sin of a position-angle table
+    and a concatenation of the rotated halves, the shape the reference's
+    substitution rewrites to ``mx.fast.rope`` (``rules/primitive_subst.py:339-407``;
+    the rewrite keeps only x and uses the default base and positions)."""
+    def fn(x, angles):
+        c, s = mx.cos(angles), mx.sin(angles)
+        x1, x2 = x[..., :half], x[..., half:]
+        return mx.concatenate([x1 * c - x2 * s, x1 * s + x2 * c], axis=-1)
+
+    return fn
+
+
 def rms_norm_inputs(size: str, seed: int):
     rng = np.random.default_rng(seed)
     x = rng.standard_normal((RMS_ROWS[size], RMS_COLS)).astype(np.float32)

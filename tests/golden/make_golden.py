@@ -24,7 +24,10 @@ Writes
   candidates of the verification sweep (rms_norm / SDPA / normed-matmul
   substitution x elementwise fusion, on or off);
 * sources/cuda_chains.json -- for every fused kernel body in those sources,
-  the chain it was emitted from, so the oracle can evaluate it on the CPU.
+  the chain it was emitted from, so the oracle can evaluate it on the CPU;
+* op_registry.json -- the mlx.core / mlx.core.fast op names the reference's
+  tracer records (ir/op_registry.py), which the backend's mx namespace must
+  provide.
 """
 
 from __future__ import annotations
@@ -176,6 +179,9 @@ def graphs(core):
                                    [((2048, 2048), bf)]),
         "normed_matmul": lambda: trace(W.normed_matmul_fn(core), [((8192, 4096), bf),
                                                                   ((4096, 4096), bf)]),
+        "layer_norm": lambda: trace(W.layer_norm_fn(core), [((1024, 2048), f32), ((2048,), f32),
+                                                             ((2048,), f32)]),
+        "rope": lambda: trace(W.rope_fn(core), [((8, 32, 2048, 128), bf), ((2048, 64), bf)]),
         "decoder_full": lambda: trace(W.decoder_block_fn(core, W.DECODER_FULL), [(s, bf) for s in dec_full]),
         "decoder_tiny": lambda: trace(W.decoder_block_fn(core, W.DECODER_TINY), [(s, bf) for s in dec_tiny]),
     }
@@ -302,7 +308,7 @@ def make_sources(core):
     phew.emit.msl_codegen.SubgraphMSLCodegen = rec.cls
     builders = graphs(core)
     srcs = {}
-    for name in ("rms_norm", "gelu_chain", "attention", "normed_matmul"):
+    for name in ("rms_norm", "gelu_chain", "attention", "normed_matmul", "layer_norm", "rope"):
         classes = {SC.fp32_to_fp32}
         if name == "normed_matmul":
             classes.add(SC.normed_matmul)
@@ -319,8 +325,17 @@ def make_sources(core):
     return srcs, rec.chains
 
 
+def make_op_registry():
+    """The reference tracer's op coverage (ir/op_registry.py): the mlx.core
+    and mlx.core.fast names it records, which this backend must provide."""
+    from phew.ir import op_registry as R
+
+    return {"IMPLEMENTED": sorted(R.IMPLEMENTED), "FAST_IMPLEMENTED": sorted(R.FAST_IMPLEMENTED)}
+
+
 def main() -> int:
     core = fake_mlx()
+    (HERE / "op_registry.json").write_text(json.dumps(make_op_registry(), indent=1))
     SOURCES.mkdir(exist_ok=True)
     (HERE / "verdicts.json").write_text(json.dumps(make_verdicts(), indent=1))
     (HERE / "allclose.json").write_text(json.dumps(make_allclose()))

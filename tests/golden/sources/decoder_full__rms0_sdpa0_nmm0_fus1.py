@@ -5,8 +5,8 @@ from phew_b200.mx import fast
 def optimized(x0, x1, x2, x3, x4, x5, x6, x7, *_, **__):
     t1 = x0 * x0
     t2 = mx.mean(t1, axis=[2], keepdims=True)
-    _kernel_263 = mx.fast.cuda_kernel(
-        name="kernel_263",
+    _kernel_348 = mx.fast.cuda_kernel(
+        name="kernel_348",
         input_names=['inp0', 'inp1', 'inp2'],
         output_names=['out0'],
         source="""    // fused elementwise chain: 4 ops, 3 inputs, 1 outputs, 67108864 elements
@@ -51,7 +51,7 @@ def optimized(x0, x1, x2, x3, x4, x5, x6, x7, *_, **__):
       out0[elem] = phew_st_bf16(v8);
     }""",
     )
-    kernel3_out = _kernel_263(
+    kernel3_out = _kernel_348(
         inputs=[t2, x0, x1],
         output_shapes=[x0.shape],
         output_dtypes=[mx.bfloat16],
@@ -81,8 +81,8 @@ def optimized(x0, x1, x2, x3, x4, x5, x6, x7, *_, **__):
     t22 = mx.mean(t21, axis=[2], keepdims=True)
     t23 = t20 @ x4
     t24 = t20 @ x5
-    _kernel_264 = mx.fast.cuda_kernel(
-        name="kernel_264",
+    _kernel_349 = mx.fast.cuda_kernel(
+        name="kernel_349",
         input_names=['inp0', 'inp1', 'inp2'],
         output_names=['out0'],
         source="""    // fused elementwise chain: 7 ops, 3 inputs, 1 outputs, 234881024 elements
@@ -133,7 +133,7 @@ def optimized(x0, x1, x2, x3, x4, x5, x6, x7, *_, **__):
       out0[elem] = phew_st_bf16(v11);
     }""",
     )
-    kernel25_out = _kernel_264(
+    kernel25_out = _kernel_349(
         inputs=[t22, t23, t24],
         output_shapes=[t23.shape],
         output_dtypes=[mx.bfloat16],

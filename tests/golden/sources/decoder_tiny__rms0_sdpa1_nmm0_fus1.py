@@ -5,8 +5,8 @@ from phew_b200.mx import fast
 def optimized(x0, x1, x2, x3, x4, x5, x6, x7, *_, **__):
     t1 = x0 * x0
     t2 = mx.mean(t1, axis=[2], keepdims=True)
-    _kernel_1264 = mx.fast.cuda_kernel(
-        name="kernel_1264",
+    _kernel_1349 = mx.fast.cuda_kernel(
+        name="kernel_1349",
         input_names=['inp0', 'inp1', 'inp2'],
         output_names=['out0'],
         source="""    // fused elementwise chain: 4 ops, 3 inputs, 1 outputs, 131072 elements
@@ -51,7 +51,7 @@ def optimized(x0, x1, x2, x3, x4, x5, x6, x7, *_, **__):
       out0[elem] = phew_st_bf16(v8);
     }""",
     )
-    kernel3_out = _kernel_1264(
+    kernel3_out = _kernel_1349(
         inputs=[t2, x0, x1],
         output_shapes=[x0.shape],
         output_dtypes=[mx.bfloat16],

@@ -3,8 +3,8 @@ from phew_b200.mx import fast
 
 @mx.compile
 def optimized(x0, x1, x2, x3, *_, **__):
-    _kernel_119 = mx.fast.cuda_kernel(
-        name="kernel_119",
+    _kernel_144 = mx.fast.cuda_kernel(
+        name="kernel_144",
         input_names=['inp0', 'inp1', 'inp2', 'inp3'],
         output_names=['out0'],
         source="""    // fused elementwise chain: 14 ops, 4 inputs, 1 outputs, 33554432 elements
@@ -78,7 +78,7 @@ def optimized(x0, x1, x2, x3, *_, **__):
       out0[elem] = phew_st_f16(v22);
     }""",
     )
-    kernel1_out = _kernel_119(
+    kernel1_out = _kernel_144(
         inputs=[x0, x1, x2, x3],
         output_shapes=[x0.shape],
         output_dtypes=[mx.float16],

@@ -1,0 +1,72 @@
+import phew_b200.mx as mx
+from phew_b200.mx import fast
+
+@mx.compile
+def optimized(x0, x1, x2, *_, **__):
+    t1 = mx.mean(x0, axis=[1], keepdims=True)
+    t2 = mx.var(x0, axis=[1], keepdims=True)
+    _kernel_221 = mx.fast.cuda_kernel(
+        name="kernel_221",
+        input_names=['inp0', 'inp1', 'inp2', 'inp3', 'inp4'],
+        output_names=['out0'],
+        source="""    // fused elementwise chain: 6 ops, 5 inputs, 1 outputs, 2097152 elements
+    // phew-io: idx32 out=1024x2048 inp0=full inp1=prefix:2048 inp2=prefix:2048 inp3=suffix:2048 inp4=suffix:2048
+    const unsigned int phew_n = (unsigned int)out0_size;
+    const unsigned int phew_tid = (unsigned int)blockIdx.x * blockDim.x + threadIdx.x;
+    const unsigned int phew_nthreads = (unsigned int)gridDim.x * blockDim.x;
+    unsigned int phew_tail = 0;
+    const float v7 = __int_as_float(0x3727c5ac) /* 9.999999747378752e-06 */;
+    if (((reinterpret_cast<phew_uptr>(inp0) | reinterpret_cast<phew_uptr>(inp1) | reinterpret_cast<phew_uptr>(inp2) | reinterpret_cast<phew_uptr>(inp3) | reinterpret_cast<phew_uptr>(inp4) | reinterpret_cast<phew_uptr>(out0)) & 15u) == 0u) {
+      const unsigned int phew_nvec = phew_n / 4u;
+      for (unsigned int phew_v = phew_tid; phew_v < phew_nvec; phew_v += phew_nthreads) {
+        const unsigned int elem = phew_v * 4u;
+        const phew_vec<float, 4> ld0 = phew_ldv<float, 4>(inp0 + elem);
+        const float ld1 = inp1[elem / 2048u];
+        const float ld2 = inp2[elem / 2048u];
+        const phew_vec<float, 4> ld3 = phew_ldv<float, 4>(inp3 + elem % 2048u);
+        const phew_vec<float, 4> ld4 = phew_ldv<float, 4>(inp4 + elem % 2048u);
+        phew_vec<float, 4> st0;
+        #pragma unroll
+        for (int l = 0; l < 4; ++l) {
+          const float v1 = phew_ld(ld0.v[l]);
+          const float v2 = phew_ld(ld1);
+          const float v3 = phew_ld(ld2);
+          const float v4 = phew_ld(ld3.v[l]);
+          const float v5 = phew_ld(ld4.v[l]);
+          const float v6 = __fsub_rn(v1, v2);
+          const float v8 = __fadd_rn(v3, v7);
+          const float v9 = __fsqrt_rn(v8);
+          const float v10 = __fdiv_rn(v6, v9);
+          const float v11 = __fmul_rn(v10, v4);
+          const float v12 = __fadd_rn(v11, v5);
+          st0.v[l] = phew_st_f32(v12);
+        }
+        phew_stv<float, 4>(out0 + elem, st0);
+      }
+      phew_tail = phew_nvec * 4u;
+    }
+    for (unsigned int elem = phew_tail + phew_tid; elem < phew_n; elem += phew_nthreads) {
+      const float v1 = phew_ld(inp0[elem]);
+      const float v2 = phew_ld(inp1[elem / 2048u]);
+      const float v3 = phew_ld(inp2[elem / 2048u]);
+      const float v4 = phew_ld(inp3[elem % 2048u]);
+      const float v5 = phew_ld(inp4[elem % 2048u]);
+      const float v6 = __fsub_rn(v1, v2);
+      const float v8 = __fadd_rn(v3, v7);
+      const float v9 = __fsqrt_rn(v8);
+      const float v10 = __fdiv_rn(v6, v9);
+      const float v11 = __fmul_rn(v10, v4);
+      const float v12 = __fadd_rn(v11, v5);
+      out0[elem] = phew_st_f32(v12);
+    }""",
+    )
+    kernel3_out = _kernel_221(
+        inputs=[x0, t1, t2, x1, x2],
+        output_shapes=[x0.shape],
+        output_dtypes=[mx.float32],
+        grid=(mx.elementwise_threads(x0.size), 1, 1),
+        threadgroup=(256, 1, 1),
+        template=[],
+    )
+    kernel3 = kernel3_out[0]
+    return kernel3

@@ -6,8 +6,8 @@ def optimized(x0, x1, *_, **__):
     t1 = x0 * x0
     t2 = mx.mean(t1, axis=[1], keepdims=True)
     t3 = x0 @ x1
-    _kernel_168 = mx.fast.cuda_kernel(
-        name="kernel_168",
+    _kernel_193 = mx.fast.cuda_kernel(
+        name="kernel_193",
         input_names=['inp0', 'inp1'],
         output_names=['out0'],
         source="""    // fused elementwise chain: 3 ops, 2 inputs, 1 outputs, 33554432 elements
@@ -47,7 +47,7 @@ def optimized(x0, x1, *_, **__):
       out0[elem] = phew_st_bf16(v6);
     }""",
     )
-    kernel4_out = _kernel_168(
+    kernel4_out = _kernel_193(
         inputs=[t2, t3],
         output_shapes=[t3.shape],
         output_dtypes=[mx.bfloat16],

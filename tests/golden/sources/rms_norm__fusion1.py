@@ -5,8 +5,8 @@ from phew_b200.mx import fast
 def optimized(x0, x1, *_, **__):
     t1 = x0 * x0
     t2 = mx.mean(t1, axis=[1], keepdims=True)
-    _kernel_72 = mx.fast.cuda_kernel(
-        name="kernel_72",
+    _kernel_97 = mx.fast.cuda_kernel(
+        name="kernel_97",
         input_names=['inp0', 'inp1', 'inp2'],
         output_names=['out0'],
         source="""    // fused elementwise chain: 4 ops, 3 inputs, 1 outputs, 2097152 elements
@@ -50,7 +50,7 @@ def optimized(x0, x1, *_, **__):
       out0[elem] = phew_st_f32(v8);
     }""",
     )
-    kernel3_out = _kernel_72(
+    kernel3_out = _kernel_97(
         inputs=[t2, x0, x1],
         output_shapes=[x0.shape],
         output_dtypes=[mx.float32],

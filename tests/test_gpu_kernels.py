@@ -189,3 +189,36 @@ def test_fast_path_full_size_chain_properties(mx):
     c2, i2, o2 = gelu_chain_nodes(len(rows))
     ref = mlx_cpu.eval_chain(c2, i2, o2, sub)[0]
     assert_close(got1[rows], ref, "float16", max_ulps=8, frac_exact=0.97)
+
+
+@pytest.mark.parametrize("dtype", ["float32", "float16", "bfloat16"])
+@pytest.mark.parametrize("rows,cols", [(256, 2048), (3, 100), (5, 8192), (2, 40000)])
+@pytest.mark.parametrize("affine", ["none", "weight", "both"])
+def test_layer_norm(mx, dtype, rows, cols, affine):
+    rng = np.random.default_rng(rows + cols)
+    npd = mlx_cpu._NP[dtype]
+    x = (rng.standard_normal((rows, cols)).astype(np.float32) * 2 + 0.5).astype(npd)
+    w = rng.standard_normal(cols).astype(np.float32).astype(npd) if affine != "none" else None
+    b = rng.standard_normal(cols).astype(np.float32).astype(npd) if affine == "both" else None
+    got = mx.fast.layer_norm(mx.array(x), None if w is None else mx.array(w),
+                             None if b is None else mx.array(b), eps=1e-5)
+    ref = mlx_cpu.layer_norm(mlx_cpu.array(x), None if w is None else mlx_cpu.array(w),
+                             None if b is None else mlx_cpu.array(b), 1e-5)
+    assert_close(np.asarray(got), np.asarray(ref), dtype)
+
+
+@pytest.mark.parametrize("dtype", ["float32", "float16", "bfloat16"])
+@pytest.mark.parametrize("shape,dims,kw", [
+    ((2, 4, 64, 128), 128, {}),
+    ((2, 4, 64, 128), 128, {"traditional": True}),
+    ((1, 3, 100, 96), 64, {"base": 500000.0, "scale": 0.5, "offset": 7}),
+    ((8, 2048, 64), 64, {}),
+    ((5, 40), 16, {"traditional": True, "offset": 3}),
+])
+def test_rope(mx, dtype, shape, dims, kw):
+    rng = np.random.default_rng(dims + len(shape))
+    npd = mlx_cpu._NP[dtype]
+    x = rng.standard_normal(shape).astype(np.float32).astype(npd)
+    got = mx.fast.rope(mx.array(x), dims, **kw)
+    ref = mlx_cpu.rope(mlx_cpu.array(x), dims, **kw)
+    assert_close(np.asarray(got), np.asarray(ref), dtype)

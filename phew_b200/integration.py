@@ -105,3 +105,13 @@ def install(mx_module: bool = True) -> None:
     phew.bench.benchmark = bbench.benchmark
     phew.bench.compare = bbench.compare
     phew.verify.EquivalenceChecker = bverify.EquivalenceChecker
+    # Phase-2 launch search (optimizer.py:250-279 imports it from phew.emit)
+    from .emit.autotune import KernelParamSearch
+
+    phew.emit.KernelParamSearch = KernelParamSearch
+    try:
+        import phew.emit.metal_kernel
+
+        phew.emit.metal_kernel.KernelParamSearch = KernelParamSearch
+    except ImportError:
+        pass

@@ -719,6 +719,117 @@ class SubgraphCUDACodegen:
         source = "\n".join(f"    {line}" if line else "" for line in L)
         return source, inp_names, out_names
 
+    # -- elementwise prologue fused into a row reduction ------------------------
+
+    _REDUCE_INIT = {"sum": "0.0f", "mean": "0.0f", "prod": "1.0f",
+                    "max": "__int_as_float(0xff800000u)", "min": "__int_as_float(0x7f800000u)"}
+
+    def emit_reduce_rows(self, subgraph_nodes, external_inputs, root, op: str, keepdims: bool,
+                         tpr: int, rpb: int) -> tuple[str, list[str], list[str]]:
+        """Body of ``op(root, axis=-1)`` (sum / mean / max / min / prod) where
+        `root` is the value of the elementwise DAG `subgraph_nodes`: each
+        element is computed (rounded per node) as the reduction reads it and
+        never written to HBM.  Thread mapping, accumulation order and the
+        shuffle / shared-memory tree are those of ``csrc/rows.cu``'s
+        ``reduce_rows_kernel`` (`tpr` threads per row striding over it, `rpb`
+        rows per block), so the result has the bits of materialising `root`
+        and then calling ``phew_reduce``.  Raises ``ValueError`` when it
+        cannot (the caller then materialises `root`)."""
+        out_shape = tuple(int(x) for x in root.shape)
+        if not out_shape or op not in self._REDUCE_INIT:
+            raise ValueError("cuda_codegen: not a row reduction")
+        red = out_shape[-1]
+        out_dt = dtype_name(root.dtype)
+        if out_dt not in ("float32", "float16", "bfloat16"):
+            raise ValueError(f"cuda_codegen: reduction over {out_dt}")
+        in_dts = [dtype_name(x.dtype) for x in external_inputs]
+        classes = []
+        for x in external_inputs:
+            shp = tuple(int(v) for v in x.shape)
+            if len(shp) > 0 and not broadcast_compatible(shp, out_shape):
+                raise ValueError("cuda_codegen: input not broadcast-compatible with output")
+            cls = classify_input(shp, out_shape)
+            if cls[0] == "general":
+                raise ValueError("cuda_codegen: general broadcast in a fused reduction")
+            classes.append(cls)
+        plan = _Plan(subgraph_nodes, external_inputs, [root],
+                     precise16=getattr(self, "precise_16bit", False))
+        inp_names = [f"inp{i}" for i in range(len(external_inputs))]
+        n = _numel(out_shape)
+        it = "unsigned int" if n < 2**30 else "unsigned long long"
+        u = "u" if it == "unsigned int" else "ull"
+        env = {}
+        body = []
+        for node, nm, dt, (cls, ext) in zip(external_inputs, inp_names, in_dts, classes):
+            v = plan.var(node)
+            idx = self._index(cls, ext, nm, node, out_shape, it, u)
+            body.append(f"const {VALUE_CTYPE[dt]} {v} = phew_ld({nm}[{idx}]);")
+            env[node.id] = (v, dt)
+        body += plan.scalar_lines(env)
+        rv, rdt = env[root.id]
+        if rdt != out_dt:
+            raise ValueError("cuda_codegen: reduction dtype differs from its input's")
+        if op in ("max", "min"):
+            cmp = ">" if op == "max" else "<"
+            comb = ("phew_acc = ((phew_x {c} phew_acc || isnan(phew_x)) && !isnan(phew_acc)) ? phew_x : phew_acc;"
+                    .format(c=cmp))
+        elif op == "prod":
+            comb = "phew_acc = phew_acc * phew_x;"
+        else:
+            comb = "phew_acc = phew_acc + phew_x;"
+        shfl_comb = comb.replace("phew_x", "phew_y")
+        L: list[str] = []
+        L.append(f"// elementwise prologue ({len(plan.compute_nodes)} ops) + {op} over rows of {red}")
+        L.append(io_contract_line(classes, out_shape, [tuple(x.shape) for x in external_inputs], it)
+                 + f" rowred={red}")
+        L += plan.constant_lines(packed_type=None)
+        L += [
+            "__shared__ float phew_smem[32 * 32];",
+            f"const {it} phew_red = {red}{u};",
+            f"const {it} phew_rows = ({it})out0_size;",
+            f"const {it} phew_row = ({it})blockIdx.x * blockDim.y + threadIdx.y;",
+            "const bool phew_active = phew_row < phew_rows;",
+            f"float phew_acc = {self._REDUCE_INIT[op]};",
+            "if (phew_active) {",
+            f"  for ({it} phew_c = threadIdx.x; phew_c < phew_red; phew_c += blockDim.x) {{",
+            f"    const {it} elem = phew_row * phew_red + phew_c;",
+        ]
+        L += ["    " + b for b in body]
+        L += [
+            f"    const float phew_x = {rv};",
+            "    " + comb,
+            "  }",
+            "}",
+            "#pragma unroll",
+            "for (int phew_o = 16; phew_o > 0; phew_o >>= 1) {",
+            "  const float phew_y = __shfl_xor_sync(0xffffffffu, phew_acc, phew_o);",
+            "  " + shfl_comb,
+            "}",
+            "{",
+            "  const int phew_wpr = blockDim.x / 32;",
+            "  if (phew_wpr > 1) {",
+            "    const int phew_lane = threadIdx.x & 31, phew_warp = threadIdx.x >> 5;",
+            "    float* phew_rs = phew_smem + threadIdx.y * 32;",
+            "    __syncthreads();",
+            "    if (phew_lane == 0) phew_rs[phew_warp] = phew_acc;",
+            "    __syncthreads();",
+            f"    phew_acc = phew_lane < phew_wpr ? phew_rs[phew_lane] : {self._REDUCE_INIT[op]};",
+            "    #pragma unroll",
+            "    for (int phew_o = 16; phew_o > 0; phew_o >>= 1) {",
+            "      const float phew_y = __shfl_xor_sync(0xffffffffu, phew_acc, phew_o);",
+            "      " + shfl_comb,
+            "    }",
+            "  }",
+            "}",
+            "if (phew_active && threadIdx.x == 0) {",
+            ("  phew_acc = __fdiv_rn(phew_acc, (float)phew_red);" if op == "mean" else ""),
+            f"  out0[phew_row] = phew_st_{_suffix(out_dt)}(phew_acc);",
+            "}",
+        ]
+        _ = keepdims
+        source = "\n".join(f"    {line}" if line else "" for line in L)
+        return source, inp_names, ["out0"]
+
     # -- per-element form -----------------------------------------------------
 
     def _index(self, cls, ext, name, node, out_shape, it, u, elem="elem") -> str:

@@ -374,6 +374,13 @@ def check_io_contract(source: str, in_shapes, out_shapes, name: str = "kernel") 
     for o in out_shapes:
         if _numel(o) != n:
             raise ValueError(f"{name}: fused outputs must all have {n} elements, got {o}")
+    # A fused row reduction writes one value per row of `rowred` elements:
+    # its inputs are indexed over rows x rowred.
+    for tok in line:
+        if tok.startswith("rowred="):
+            n *= int(tok[len("rowred="):])
+            if any(t.startswith("inp") and "=general" in t for t in line):
+                raise ValueError(f"{name}: general broadcasts are not fused into reductions")
     for tok in line:
         if tok == "idx32" and n >= 2**31 - 2**20:
             raise ValueError(f"{name}: {n} elements overflow the kernel's 32-bit indexing")

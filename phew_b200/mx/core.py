@@ -827,10 +827,45 @@ def _norm_axes(a: array, axis) -> tuple:
     return (int(axis) % a.ndim,)
 
 
+def _fused_reduce(opname: str, a: "_Lazy", keepdims: bool):
+    """`opname` over the last axis of a pending elementwise DAG, in one kernel
+    that computes each element as the reduction reads it; None when it
+    cannot (the caller then materialises `a`)."""
+    red = a.shape[-1]
+    if red == 0 or a.size == 0:
+        return None
+    tpr = 256 if red >= 1024 else 32
+    rpb = 4 if tpr == 32 else 1
+    chain, ext_specs, ext_arrays, root_spec, key = _fused_dag(a)
+    ckey = ("fused_reduce", opname, key)
+    kern = _kernel_cache.get(ckey)
+    if kern is None:
+        try:
+            src, in_names, out_names = SubgraphCUDACodegen().emit_reduce_rows(
+                chain, ext_specs, root_spec, opname, keepdims, tpr, rpb)
+        except ValueError:
+            _kernel_cache[ckey] = False
+            return None
+        kern = CudaKernel(f"phew_fused_{opname}_{len(chain)}", in_names, out_names, src)
+        _kernel_cache[ckey] = kern
+    if kern is False:
+        return None
+    rows = a.size // red
+    out_shape = tuple(a.shape[:-1]) + ((1,) if keepdims else ())
+    blocks = -(-rows // rpb)
+    return kern(inputs=[asarray_device(x) for x in ext_arrays], output_shapes=[out_shape],
+                output_dtypes=[a.dtype], grid=(blocks * tpr, rpb, 1), threadgroup=(tpr, rpb, 1))[0]
+
+
 def _reduce(opname: str, a, axis=None, keepdims=False) -> array:
     a = a if isinstance(a, array) else array(a)
     if a.dtype.code is None:
         raise NotImplementedError(f"{opname} over {a.dtype.name} arrays")
+    if (isinstance(a, _Lazy) and a.pending and a.ndim >= 1
+            and _norm_axes(a, axis) == (a.ndim - 1,)):
+        fused = _fused_reduce(opname, a, keepdims)
+        if fused is not None:
+            return fused
     axes = _norm_axes(a, axis)
     shape = a.shape
     out_shape_keep = tuple(1 if i in axes else s for i, s in enumerate(shape))

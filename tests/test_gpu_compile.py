@@ -133,3 +133,24 @@ def test_fused_softmax_of_mixed_width_inputs_falls_back(mx):
         return mx.softmax((s + 1.0).astype(mx.bfloat16) * b, axis=-1)
 
     _same(mx, f, s, b)
+
+
+@pytest.mark.parametrize("op", ["sum", "mean", "max", "min", "prod"])
+@pytest.mark.parametrize("dtype,cols", [("bfloat16", 4096), ("float32", 2048), ("float16", 300),
+                                        ("float32", 33)])
+def test_fused_row_reduction_matches_materialised(mx, op, dtype, cols):
+    """A reduction over the last axis of a pending elementwise value reads
+    the prologue's inputs once, with the bits of materialise-then-reduce."""
+    rng = np.random.default_rng(cols)
+    x = _rand(mx, rng, (5, 9, cols), dtype)
+    s = _rand(mx, rng, (5, 9, 1), dtype)
+    if op == "max":
+        xv = np.asarray(x).copy()
+        xv[0, 0, 3] = np.nan
+        x = mx.array(xv)
+
+    def f(x, s):
+        y = x * s + 0.25 if op != "prod" else 1.0 + x * 0.01
+        return getattr(mx, op)(y, axis=-1, keepdims=(op == "mean")), getattr(mx, op)(y * y, axis=2)
+
+    _same(mx, f, x, s)

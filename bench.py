@@ -606,6 +606,19 @@ def decoder_specs(dims, seqs):
     return specs
 
 
+def _sweep_store(d):
+    """The process group's key-value store (host-side counters for the
+    sweep's work stealing), or None on one process."""
+    if not d.dist or d.world == 1:
+        return None
+    try:
+        from torch.distributed import distributed_c10d
+
+        return distributed_c10d._get_default_store()
+    except Exception:  # noqa: BLE001  (fall back to static blocks)
+        return None
+
+
 def _exception_kinds(verdicts) -> dict:
     kinds: dict[str, int] = {}
     for v in verdicts.values():
@@ -646,9 +659,11 @@ def run_sweep(args) -> None:
     journal = jdir / f"journal.rank{d.rank}.jsonl"
     ev = sweep.DeviceEvaluator(baseline, cands, sweep.DeviceInputs(decoder_specs(dims, seqs)))
 
-    # warm-up: compile every kernel the candidates use on the smallest size
-    for c in names:
-        ev(c, 99, "small", variants[0])
+    # warm-up: compile every kernel the candidates use (generated kernels
+    # specialise on row length, so each size compiles its own), untimed
+    for size in sizes:
+        for c in names:
+            ev(c, 99, size, variants[0])
     ev.release()
     torch.cuda.synchronize()
 
@@ -658,7 +673,12 @@ def run_sweep(args) -> None:
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         e0.record()
-        recs = sweep.run_shards(mine, ev, sizes, variants, journal=journal, rank=d.rank)
+        store = _sweep_store(d)
+        if store is not None:
+            recs = sweep.run_shards_dynamic(shards, ev, sizes, variants, store, d.rank, d.world,
+                                            journal=journal, run_id=f"sweep/{jdir.name}")
+        else:
+            recs = sweep.run_shards(mine, ev, sizes, variants, journal=journal, rank=d.rank)
         e1.record()
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
@@ -678,7 +698,9 @@ def run_sweep(args) -> None:
             "config": {"workload": f"{tag} verification sweep: {len(names)} candidates x {len(seeds)} "
                                    f"seeds x sizes {[seqs[s] for s in sizes]} x variants {list(variants)}",
                        "dims": vars(dims) if hasattr(dims, "__dict__") else str(dims),
-                       "parallelism": f"shards x{d.world}, no collective"},
+                       "warmup": "each candidate once at every size (runtime kernel compilation)",
+                       "parallelism": f"shards x{d.world}, no collective"
+                                      + (", work stealing over the store" if d.world > 1 else "")},
             "units_per_s": units / max_s, "units": units, "wall_s": max_wall,
             "passed": sorted(c for c, v in verdicts.items() if v["passed"]),
             "failed": sorted(c for c, v in verdicts.items() if not v["passed"]),

@@ -15,8 +15,11 @@ against one baseline:
 
 Shards are ordered seed-major and split into contiguous blocks, one block
 per process (one process per GPU); each process draws the inputs of a
-(seed, size) once on its own device, evaluates the baseline once per
-(seed, size, variant) and reuses it for every candidate of its block.
+(seed, size, variant) on its own device, evaluates the baseline once per
+(seed, size, variant) and reuses it for every candidate it verifies.  With
+several processes, a process that finishes its block takes the remaining
+shards of the fullest other block from a host-side counter
+(``run_shards_dynamic``).
 There is no data-path collective: processes append verdict records to
 per-rank journals, and the merge reads them back (a rerun skips shards
 already journalled, and shards missing from a dead rank's journal are
@@ -229,6 +232,79 @@ def run_shards(
     return out
 
 
+def _run_one(shard: Shard, evaluate, sizes, variants, rank: int) -> ShardVerdict:
+    v = ShardVerdict(shard.candidate, shard.seed, True, rank=rank)
+    t0 = time.perf_counter()
+    for size in sizes:
+        for variant in variants:
+            ok, failure = evaluate(shard.candidate, shard.seed, size, variant)
+            v.units += 1
+            if not ok:
+                v.passed = False
+                v.failures.append(failure)
+    v.seconds = time.perf_counter() - t0
+    return v
+
+
+def run_shards_dynamic(
+    shards: Sequence[Shard],
+    evaluate: Callable[[str, int, str, str], tuple[bool, str | None]],
+    sizes: Sequence[str],
+    variants: Sequence[str],
+    store: Any,
+    rank: int,
+    world: int,
+    journal: Path | None = None,
+    run_id: str = "sweep",
+) -> list[ShardVerdict]:
+    """Shards taken from a shared host-side counter per block, so no rank
+    idles while another still has work (shard costs differ several-fold:
+    an unfused attention candidate costs 4x a substituted one).
+
+    The shards are split into `world` contiguous seed-major blocks as in
+    :func:`partition`; block b's next shard is ``store.add(f"{run_id}/next/b", 1) - 1``.
+    Rank r drains its own block first, then takes shards from the block
+    with the most left (the next shard of a block shares its seed, and so
+    its baseline, with the owner's current one).  `store` is any key-value
+    store with an atomic ``add`` (torch.distributed's TCP / file store):
+    host control only, no device data moves between ranks.  Shards already
+    in `journal` count as done; a shard taken by a rank that then dies is
+    missing from the journals and ``merge`` returns it for reassignment."""
+    done: dict[tuple, ShardVerdict] = {}
+    if journal:  # any rank may have run any shard: resume from every journal beside ours
+        for p in sorted(Path(journal).parent.glob("*.jsonl")):
+            done.update(load_journal(p))
+    blocks = [partition(shards, world, b) for b in range(world)]
+    key = [f"{run_id}/next/{b}" for b in range(world)]
+    out: list[ShardVerdict] = []
+
+    def take(b: int) -> Shard | None:
+        i = store.add(key[b], 1) - 1
+        return blocks[b][i] if i < len(blocks[b]) else None
+
+    def work(shard: Shard) -> None:
+        if (shard.candidate, shard.seed) in done:
+            out.append(done[(shard.candidate, shard.seed)])
+            return
+        v = _run_one(shard, evaluate, sizes, variants, rank)
+        out.append(v)
+        if journal:
+            with open(journal, "a") as f:
+                f.write(v.to_json() + "\n")
+
+    while (sh := take(rank)) is not None:
+        work(sh)
+    while True:
+        left = [(len(blocks[b]) - store.add(key[b], 0), b) for b in range(world) if b != rank]
+        left = [x for x in left if x[0] > 0]
+        if not left:
+            break
+        sh = take(max(left)[1])
+        if sh is not None:
+            work(sh)
+    return out
+
+
 def merge(journal_dir: Path, shards: Sequence[Shard]) -> tuple[dict[str, dict], list[Shard]]:
     """Per-candidate verdicts from every rank's journal, plus the shards no
     journal holds (to be reassigned)."""
@@ -271,6 +347,10 @@ class DeviceEvaluator:
         self._args = None
         self._base_out = None
         self._base_exc = None
+        # baseline results of every (size, variant) of the current seed, so a
+        # rank that evaluates shards one at a time computes each baseline once
+        self._base_seed = None
+        self._base_cache: dict[tuple, tuple] = {}
 
     def _prepare(self, seed: int, size: str, variant: str) -> None:
         key = (seed, size, variant)
@@ -281,10 +361,18 @@ class DeviceEvaluator:
             self._base_args = None
             self._base_args = self.inputs.base(size, seed)
         self._args = self.inputs.variant(variant, self._base_args, size, seed)
-        try:
-            self._base_out = self.baseline(*self._args)
-        except Exception as exc:  # noqa: BLE001
-            self._base_exc = exc
+        if self._base_seed != seed:
+            self._base_cache = {}
+            self._base_seed = seed
+        hit = self._base_cache.get(key)
+        if hit is None:
+            out, err = None, None
+            try:
+                out = self.baseline(*self._args)
+            except Exception as exc:  # noqa: BLE001
+                err = exc
+            hit = self._base_cache[key] = (out, err)
+        self._base_out, self._base_exc = hit
         self._key = key
 
     def __call__(self, candidate: str, seed: int, size: str, variant: str):
@@ -303,6 +391,7 @@ class DeviceEvaluator:
 
     def release(self) -> None:
         self._key = self._base_args = self._args = self._base_out = None
+        self._base_seed, self._base_cache = None, {}
 
 
 def load_candidates(sources: dict[str, str]) -> dict[str, Callable]:

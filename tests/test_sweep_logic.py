@@ -135,3 +135,84 @@ def test_two_rank_gloo_sweep(tmp_path, crash_rank):
     res = json.loads((tmp_path / "result.json").read_text())
     assert res["missing"] == 0
     assert res["passed"] == sorted(c for c in CANDS if c != "c3")
+
+
+def _journaled(jdir: Path) -> list[tuple]:
+    out = []
+    for p in sorted(jdir.glob("journal.rank*.jsonl")):
+        out += [(d["candidate"], d["seed"], d["rank"]) for d in map(json.loads, p.read_text().splitlines())]
+    return out
+
+
+def test_dynamic_lone_rank_drains_every_block(tmp_path):
+    """A rank whose peers never start takes every block's shards from the
+    shared counters, each exactly once."""
+    from torch.distributed import HashStore
+
+    shards = sweep.make_shards(CANDS[:5], SEEDS[:3])
+    recs = sweep.run_shards_dynamic(shards, fake_eval(set()), SIZES, VARIANTS, HashStore(), rank=1,
+                                    world=3, journal=tmp_path / "journal.rank1.jsonl")
+    assert sorted((r.candidate, r.seed) for r in recs) == sorted((s.candidate, s.seed) for s in shards)
+    # own block first, then the others
+    assert [(r.candidate, r.seed) for r in recs[:5]] == [(s.candidate, s.seed) for s in sweep.partition(shards, 3, 1)]
+    verdicts, missing = sweep.merge(tmp_path, shards)
+    assert not missing and all(v["passed"] for v in verdicts.values())
+
+
+def test_dynamic_resume_reads_every_rank_journal(tmp_path):
+    from torch.distributed import HashStore
+
+    shards = sweep.make_shards(CANDS[:4], SEEDS[:2])
+    # a previous run: rank 1 finished the first three shards, then stopped
+    sweep.run_shards(shards[:3], fake_eval(set()), SIZES, VARIANTS,
+                     journal=tmp_path / "journal.rank1.jsonl", rank=1)
+    ev = fake_eval(set())
+    recs = sweep.run_shards_dynamic(shards, ev, SIZES, VARIANTS, HashStore(), rank=0, world=2,
+                                    journal=tmp_path / "journal.rank0.jsonl")
+    assert len(recs) == len(shards)
+    assert {(c[0], c[1]) for c in ev.calls} == {(s.candidate, s.seed) for s in shards[3:]}
+    assert len(_journaled(tmp_path)) == len(shards)
+
+
+def _dyn_worker(rank, world, port, jdir):
+    import datetime
+    import time
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    from torch.distributed import distributed_c10d
+
+    store = distributed_c10d._get_default_store()
+    shards = sweep.make_shards(CANDS, SEEDS[:2])
+    base = fake_eval({("c3", "subnormal")})
+
+    def evaluate(cand, seed, size, variant):
+        # the second half of the shards (rank 1's block) is 20x as costly
+        if seed == 1 and size == "small" and variant == VARIANTS[0]:
+            time.sleep(0.04)
+        return base(cand, seed, size, variant)
+
+    sweep.run_shards_dynamic(shards, evaluate, SIZES, VARIANTS, store, rank, world,
+                             journal=Path(jdir) / f"journal.rank{rank}.jsonl", run_id="t")
+    dist.barrier()
+    if rank == 0:
+        verdicts, missing = sweep.merge(Path(jdir), shards)
+        (Path(jdir) / "result.json").write_text(json.dumps(
+            {"missing": len(missing), "passed": sorted(c for c, v in verdicts.items() if v["passed"])}))
+    dist.destroy_process_group()
+
+
+def test_two_rank_gloo_dynamic_sweep(tmp_path):
+    port = _free_port()
+    mp.spawn(_dyn_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    res = json.loads((tmp_path / "result.json").read_text())
+    assert res["missing"] == 0
+    assert res["passed"] == sorted(c for c in CANDS if c != "c3")
+    done = _journaled(tmp_path)
+    keys = [(c, s) for c, s, _ in done]
+    assert len(keys) == len(set(keys)) == 32  # every shard exactly once
+    # rank 0 finished its cheap block and took shards of rank 1's costly one
+    assert any(r == 0 and s == 1 for _, s, r in done)

@@ -607,16 +607,15 @@ def decoder_specs(dims, seqs):
 
 
 def _sweep_store(d):
-    """The process group's key-value store (host-side counters for the
-    sweep's work stealing), or None on one process."""
-    if not d.dist or d.world == 1:
-        return None
-    try:
-        from torch.distributed import distributed_c10d
+    """The key-value store holding the sweep's shared work counter: the
+    process group's store across ranks, an in-process one on one process."""
+    from torch.distributed import HashStore
 
-        return distributed_c10d._get_default_store()
-    except Exception:  # noqa: BLE001  (fall back to static blocks)
-        return None
+    if not d.dist or d.world == 1:
+        return HashStore()
+    from torch.distributed import distributed_c10d
+
+    return distributed_c10d._get_default_store()
 
 
 def _exception_kinds(verdicts) -> dict:
@@ -649,7 +648,8 @@ def run_sweep(args) -> None:
     sizes = ["small", "typical", "large"]
     variants = sweep.VARIANT_SETS[args.variants]
     shards = sweep.make_shards(names, seeds)
-    mine = sweep.partition(shards, d.world, d.rank)
+    groups = sweep.make_groups(seeds, sizes, variants)
+    store = _sweep_store(d)
     jdir = Path(args.journal_dir) if args.journal_dir else Path(tempfile.mkdtemp(prefix="sweep_"))
     if d.dist:  # every rank journals into rank 0's directory
         obj = [str(jdir)]
@@ -673,12 +673,8 @@ def run_sweep(args) -> None:
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         e0.record()
-        store = _sweep_store(d)
-        if store is not None:
-            recs = sweep.run_shards_dynamic(shards, ev, sizes, variants, store, d.rank, d.world,
-                                            journal=journal, run_id=f"sweep/{jdir.name}")
-        else:
-            recs = sweep.run_shards(mine, ev, sizes, variants, journal=journal, rank=d.rank)
+        recs = sweep.run_groups(groups, names, ev, store, d.rank, journal=journal,
+                                run_id=f"sweep/{jdir.name}")
         e1.record()
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
@@ -688,7 +684,7 @@ def run_sweep(args) -> None:
     max_s = d.max(dev_s)
     max_wall = d.max(wall)
     if d.rank == 0:
-        verdicts, missing = sweep.merge(jdir, shards)
+        verdicts, missing = sweep.merge(jdir, shards, sizes, variants)
         units = len(shards) * len(sizes) * len(variants)
         line = {
             "metric": "verified_candidates_per_s", "value": len(names) / max_s,
@@ -699,8 +695,8 @@ def run_sweep(args) -> None:
                                    f"seeds x sizes {[seqs[s] for s in sizes]} x variants {list(variants)}",
                        "dims": vars(dims) if hasattr(dims, "__dict__") else str(dims),
                        "warmup": "each candidate once at every size (runtime kernel compilation)",
-                       "parallelism": f"shards x{d.world}, no collective"
-                                      + (", work stealing over the store" if d.world > 1 else "")},
+                       "parallelism": f"(seed, size, variant) groups over {d.world} rank(s) from one "
+                                      "host-side counter, no data-path collective"},
             "units_per_s": units / max_s, "units": units, "wall_s": max_wall,
             "passed": sorted(c for c, v in verdicts.items() if v["passed"]),
             "failed": sorted(c for c, v in verdicts.items() if not v["passed"]),

@@ -9,20 +9,20 @@ against one baseline:
 
 * unit   = (candidate, seed, size, variant): one baseline/candidate pair
            compared on the device (``phew_compare``);
-* shard  = (candidate, seed): every size and variant of one seed;
+* group  = (seed, size, variant): every candidate's unit of it, sharing
+           one baseline evaluation (the unit of scheduling, ``run_groups``);
+* shard  = (candidate, seed): every size and variant of one seed (the unit
+           of verdicts and of reassignment, ``run_shards``);
 * verdict per candidate = all of its shards passed (one failing unit fails
   the candidate, as in the reference).
 
-Shards are ordered seed-major and split into contiguous blocks, one block
-per process (one process per GPU); each process draws the inputs of a
-(seed, size, variant) on its own device, evaluates the baseline once per
-(seed, size, variant) and reuses it for every candidate it verifies.  With
-several processes, a process that finishes its block takes the remaining
-shards of the fullest other block from a host-side counter
-(``run_shards_dynamic``).
-There is no data-path collective: processes append verdict records to
-per-rank journals, and the merge reads them back (a rerun skips shards
-already journalled, and shards missing from a dead rank's journal are
+Processes (one per GPU) take groups, largest size first, from one counter
+in a host-side key-value store, so the baseline of each group runs once in
+the whole job and ranks finish within about one group of each other.  Each
+process draws a group's inputs on its own device.  There is no data-path
+collective: processes append records to per-rank journals, and the merge
+folds them back into per-candidate verdicts (a rerun skips groups already
+journalled, and the shards that a dead rank's missing groups leave open are
 returned for reassignment).
 
 Two variant sets:
@@ -182,7 +182,8 @@ def load_journal(path: Path) -> dict[tuple, ShardVerdict]:
         for line in path.read_text().splitlines():
             if line.strip():
                 d = json.loads(line)
-                done[(d["candidate"], d["seed"])] = ShardVerdict(**d)
+                if "group" not in d:
+                    done[(d["candidate"], d["seed"])] = ShardVerdict(**d)
     return done
 
 
@@ -232,85 +233,117 @@ def run_shards(
     return out
 
 
-def _run_one(shard: Shard, evaluate, sizes, variants, rank: int) -> ShardVerdict:
-    v = ShardVerdict(shard.candidate, shard.seed, True, rank=rank)
-    t0 = time.perf_counter()
-    for size in sizes:
-        for variant in variants:
-            ok, failure = evaluate(shard.candidate, shard.seed, size, variant)
-            v.units += 1
-            if not ok:
-                v.passed = False
-                v.failures.append(failure)
-    v.seconds = time.perf_counter() - t0
-    return v
+@dataclass(frozen=True)
+class Group:
+    """Every candidate's unit of one (seed, size, variant): the baseline runs
+    once for the whole group."""
+
+    seed: int
+    size: str
+    variant: str
 
 
-def run_shards_dynamic(
-    shards: Sequence[Shard],
+@dataclass
+class GroupRecord:
+    seed: int
+    size: str
+    variant: str
+    results: dict = field(default_factory=dict)  # candidate -> failure string, or None if it passed
+    seconds: float = 0.0
+    rank: int = 0
+
+    def to_json(self) -> str:
+        return json.dumps({"group": [self.seed, self.size, self.variant], "results": self.results,
+                           "seconds": self.seconds, "rank": self.rank})
+
+
+def make_groups(seeds: Sequence[int], sizes: Sequence[str], variants: Sequence[str]) -> list[Group]:
+    """Largest size first (`sizes` runs smallest to largest; cost grows with
+    it), then seed, then variant: taken in this order from one shared queue
+    the groups form a longest-processing-time-first list schedule."""
+    return [Group(seed, size, v) for size in reversed(sizes) for seed in seeds for v in variants]
+
+
+def load_groups(path: Path) -> dict[tuple, GroupRecord]:
+    done = {}
+    if path.exists():
+        for line in path.read_text().splitlines():
+            if line.strip():
+                d = json.loads(line)
+                if "group" in d:
+                    seed, size, variant = d["group"]
+                    done[(seed, size, variant)] = GroupRecord(seed, size, variant, d["results"],
+                                                              d["seconds"], d["rank"])
+    return done
+
+
+def run_groups(
+    groups: Sequence[Group],
+    candidates: Sequence[str],
     evaluate: Callable[[str, int, str, str], tuple[bool, str | None]],
-    sizes: Sequence[str],
-    variants: Sequence[str],
     store: Any,
-    rank: int,
-    world: int,
+    rank: int = 0,
     journal: Path | None = None,
     run_id: str = "sweep",
-) -> list[ShardVerdict]:
-    """Shards taken from a shared host-side counter per block, so no rank
-    idles while another still has work (shard costs differ several-fold:
-    an unfused attention candidate costs 4x a substituted one).
+) -> list[GroupRecord]:
+    """Evaluate groups taken from one shared counter, in list order, until
+    the list is exhausted.
 
-    The shards are split into `world` contiguous seed-major blocks as in
-    :func:`partition`; block b's next shard is ``store.add(f"{run_id}/next/b", 1) - 1``.
-    Rank r drains its own block first, then takes shards from the block
-    with the most left (the next shard of a block shares its seed, and so
-    its baseline, with the owner's current one).  `store` is any key-value
-    store with an atomic ``add`` (torch.distributed's TCP / file store):
-    host control only, no device data moves between ranks.  Shards already
-    in `journal` count as done; a shard taken by a rank that then dies is
-    missing from the journals and ``merge`` returns it for reassignment."""
-    done: dict[tuple, ShardVerdict] = {}
-    if journal:  # any rank may have run any shard: resume from every journal beside ours
+    The next group is ``store.add(f"{run_id}/next", 1) - 1``; `store` is any
+    key-value store with an atomic ``add`` (torch.distributed's TCP / file /
+    hash store): host control only, no device data moves between ranks.  A
+    group costs one baseline plus every candidate, and a rank that is free
+    takes the next one, so ranks finish within about one group of each other
+    and no baseline is computed twice.  Groups already journalled (by any
+    rank: every ``*.jsonl`` beside `journal` is read) are not re-evaluated;
+    each finished group is appended to `journal`."""
+    done: dict[tuple, GroupRecord] = {}
+    if journal:
         for p in sorted(Path(journal).parent.glob("*.jsonl")):
-            done.update(load_journal(p))
-    blocks = [partition(shards, world, b) for b in range(world)]
-    key = [f"{run_id}/next/{b}" for b in range(world)]
-    out: list[ShardVerdict] = []
-
-    def take(b: int) -> Shard | None:
-        i = store.add(key[b], 1) - 1
-        return blocks[b][i] if i < len(blocks[b]) else None
-
-    def work(shard: Shard) -> None:
-        if (shard.candidate, shard.seed) in done:
-            out.append(done[(shard.candidate, shard.seed)])
-            return
-        v = _run_one(shard, evaluate, sizes, variants, rank)
-        out.append(v)
+            done.update(load_groups(p))
+    out: list[GroupRecord] = []
+    key = f"{run_id}/next"
+    while (i := store.add(key, 1) - 1) < len(groups):
+        g = groups[i]
+        k = (g.seed, g.size, g.variant)
+        if k in done:
+            out.append(done[k])
+            continue
+        t0 = time.perf_counter()
+        rec = GroupRecord(g.seed, g.size, g.variant, rank=rank)
+        for c in candidates:
+            ok, failure = evaluate(c, g.seed, g.size, g.variant)
+            rec.results[c] = None if ok else failure
+        rec.seconds = time.perf_counter() - t0
+        out.append(rec)
         if journal:
             with open(journal, "a") as f:
-                f.write(v.to_json() + "\n")
-
-    while (sh := take(rank)) is not None:
-        work(sh)
-    while True:
-        left = [(len(blocks[b]) - store.add(key[b], 0), b) for b in range(world) if b != rank]
-        left = [x for x in left if x[0] > 0]
-        if not left:
-            break
-        sh = take(max(left)[1])
-        if sh is not None:
-            work(sh)
+                f.write(rec.to_json() + "\n")
     return out
 
 
-def merge(journal_dir: Path, shards: Sequence[Shard]) -> tuple[dict[str, dict], list[Shard]]:
+def merge(journal_dir: Path, shards: Sequence[Shard], sizes: Sequence[str] = (),
+          variants: Sequence[str] = ()) -> tuple[dict[str, dict], list[Shard]]:
     """Per-candidate verdicts from every rank's journal, plus the shards no
-    journal holds (to be reassigned)."""
+    journal holds (to be reassigned).  Group records count towards a shard
+    (candidate, seed) once the groups of all `sizes` x `variants` of its seed
+    are journalled."""
     recs: dict[tuple, ShardVerdict] = {}
+    groups: dict[tuple, GroupRecord] = {}
     for p in sorted(Path(journal_dir).glob("journal.rank*.jsonl")):
         recs.update(load_journal(p))
+        groups.update(load_groups(p))
+    if groups:
+        for sh in shards:
+            if (sh.candidate, sh.seed) in recs:
+                continue
+            found = [groups.get((sh.seed, z, v)) for z in sizes for v in variants]
+            if not found or any(g is None or sh.candidate not in g.results for g in found):
+                continue
+            fails = [g.results[sh.candidate] for g in found if g.results[sh.candidate] is not None]
+            recs[(sh.candidate, sh.seed)] = ShardVerdict(
+                sh.candidate, sh.seed, not fails, fails, len(found),
+                sum(g.seconds for g in found) / max(len(g.results) for g in found), found[0].rank)
     missing = [s for s in shards if (s.candidate, s.seed) not in recs]
     cands: dict[str, dict] = {}
     for s in shards:
@@ -347,10 +380,6 @@ class DeviceEvaluator:
         self._args = None
         self._base_out = None
         self._base_exc = None
-        # baseline results of every (size, variant) of the current seed, so a
-        # rank that evaluates shards one at a time computes each baseline once
-        self._base_seed = None
-        self._base_cache: dict[tuple, tuple] = {}
 
     def _prepare(self, seed: int, size: str, variant: str) -> None:
         key = (seed, size, variant)
@@ -361,18 +390,10 @@ class DeviceEvaluator:
             self._base_args = None
             self._base_args = self.inputs.base(size, seed)
         self._args = self.inputs.variant(variant, self._base_args, size, seed)
-        if self._base_seed != seed:
-            self._base_cache = {}
-            self._base_seed = seed
-        hit = self._base_cache.get(key)
-        if hit is None:
-            out, err = None, None
-            try:
-                out = self.baseline(*self._args)
-            except Exception as exc:  # noqa: BLE001
-                err = exc
-            hit = self._base_cache[key] = (out, err)
-        self._base_out, self._base_exc = hit
+        try:
+            self._base_out = self.baseline(*self._args)
+        except Exception as exc:  # noqa: BLE001
+            self._base_exc = exc
         self._key = key
 
     def __call__(self, candidate: str, seed: int, size: str, variant: str):
@@ -391,7 +412,6 @@ class DeviceEvaluator:
 
     def release(self) -> None:
         self._key = self._base_args = self._args = self._base_out = None
-        self._base_seed, self._base_cache = None, {}
 
 
 def load_candidates(sources: dict[str, str]) -> dict[str, Callable]:

@@ -137,44 +137,57 @@ def test_two_rank_gloo_sweep(tmp_path, crash_rank):
     assert res["passed"] == sorted(c for c in CANDS if c != "c3")
 
 
-def _journaled(jdir: Path) -> list[tuple]:
-    out = []
-    for p in sorted(jdir.glob("journal.rank*.jsonl")):
-        out += [(d["candidate"], d["seed"], d["rank"]) for d in map(json.loads, p.read_text().splitlines())]
-    return out
+
+def test_groups_are_largest_size_first():
+    g = sweep.make_groups(SEEDS[:2], SIZES, VARIANTS)
+    assert len(g) == 2 * len(SIZES) * len(VARIANTS)
+    assert [x.size for x in g[:8]] == ["large"] * 8
+    assert g[0] == sweep.Group(0, "large", VARIANTS[0]) and g[-1].size == "small"
 
 
-def test_dynamic_lone_rank_drains_every_block(tmp_path):
-    """A rank whose peers never start takes every block's shards from the
-    shared counters, each exactly once."""
+def test_lone_rank_runs_every_group_and_merge_folds_them(tmp_path):
+    """A rank whose peers never start takes every group from the shared
+    counter; the merge folds the group records into shard verdicts."""
     from torch.distributed import HashStore
 
-    shards = sweep.make_shards(CANDS[:5], SEEDS[:3])
-    recs = sweep.run_shards_dynamic(shards, fake_eval(set()), SIZES, VARIANTS, HashStore(), rank=1,
-                                    world=3, journal=tmp_path / "journal.rank1.jsonl")
-    assert sorted((r.candidate, r.seed) for r in recs) == sorted((s.candidate, s.seed) for s in shards)
-    # own block first, then the others
-    assert [(r.candidate, r.seed) for r in recs[:5]] == [(s.candidate, s.seed) for s in sweep.partition(shards, 3, 1)]
-    verdicts, missing = sweep.merge(tmp_path, shards)
+    cands = CANDS[:5]
+    groups = sweep.make_groups(SEEDS[:3], SIZES, VARIANTS)
+    ev = fake_eval({("c1", "pm1e4")})
+    recs = sweep.run_groups(groups, cands, ev, HashStore(), rank=1, journal=tmp_path / "journal.rank1.jsonl")
+    assert [(r.seed, r.size, r.variant) for r in recs] == [(g.seed, g.size, g.variant) for g in groups]
+    assert len(ev.calls) == len(groups) * len(cands)  # one evaluation per unit
+    shards = sweep.make_shards(cands, SEEDS[:3])
+    verdicts, missing = sweep.merge(tmp_path, shards, SIZES, VARIANTS)
+    assert not missing
+    assert {c for c, v in verdicts.items() if not v["passed"]} == {"c1"}
+    assert verdicts["c1"]["shards"] == 3 and len(verdicts["c1"]["failures"]) == 3 * len(SIZES)
+    assert verdicts["c1"]["failures"][0].startswith("size=small seed=0 variant=pm1e4")
+
+
+def test_group_resume_and_missing_groups(tmp_path):
+    from torch.distributed import HashStore
+
+    cands = CANDS[:4]
+    groups = sweep.make_groups(SEEDS[:2], SIZES, VARIANTS)
+    shards = sweep.make_shards(cands, SEEDS[:2])
+    # a previous run finished the first 5 groups (all large, seed 0 and one of seed 1)
+    store = HashStore()
+    store.add("x/next", 0)
+    part = sweep.run_groups(groups[:5], cands, fake_eval(set()), store, rank=1,
+                            journal=tmp_path / "journal.rank1.jsonl", run_id="x")
+    assert len(part) == 5
+    verdicts, missing = sweep.merge(tmp_path, shards, SIZES, VARIANTS)
+    assert set(missing) == set(shards)  # no seed has all its groups yet
+    assert not any(v["passed"] for v in verdicts.values())
+    ev = fake_eval(set())
+    recs = sweep.run_groups(groups, cands, ev, HashStore(), rank=0, journal=tmp_path / "journal.rank0.jsonl")
+    assert len(recs) == len(groups)
+    assert len(ev.calls) == (len(groups) - 5) * len(cands)
+    verdicts, missing = sweep.merge(tmp_path, shards, SIZES, VARIANTS)
     assert not missing and all(v["passed"] for v in verdicts.values())
 
 
-def test_dynamic_resume_reads_every_rank_journal(tmp_path):
-    from torch.distributed import HashStore
-
-    shards = sweep.make_shards(CANDS[:4], SEEDS[:2])
-    # a previous run: rank 1 finished the first three shards, then stopped
-    sweep.run_shards(shards[:3], fake_eval(set()), SIZES, VARIANTS,
-                     journal=tmp_path / "journal.rank1.jsonl", rank=1)
-    ev = fake_eval(set())
-    recs = sweep.run_shards_dynamic(shards, ev, SIZES, VARIANTS, HashStore(), rank=0, world=2,
-                                    journal=tmp_path / "journal.rank0.jsonl")
-    assert len(recs) == len(shards)
-    assert {(c[0], c[1]) for c in ev.calls} == {(s.candidate, s.seed) for s in shards[3:]}
-    assert len(_journaled(tmp_path)) == len(shards)
-
-
-def _dyn_worker(rank, world, port, jdir):
+def _group_worker(rank, world, port, jdir, crash_rank):
     import datetime
     import time
 
@@ -186,33 +199,57 @@ def _dyn_worker(rank, world, port, jdir):
     from torch.distributed import distributed_c10d
 
     store = distributed_c10d._get_default_store()
+    groups = sweep.make_groups(SEEDS[:2], SIZES, VARIANTS)
     shards = sweep.make_shards(CANDS, SEEDS[:2])
     base = fake_eval({("c3", "subnormal")})
 
     def evaluate(cand, seed, size, variant):
-        # the second half of the shards (rank 1's block) is 20x as costly
-        if seed == 1 and size == "small" and variant == VARIANTS[0]:
-            time.sleep(0.04)
+        if rank == 1:  # a slower rank: the other one takes more groups
+            time.sleep(0.002)
         return base(cand, seed, size, variant)
 
-    sweep.run_shards_dynamic(shards, evaluate, SIZES, VARIANTS, store, rank, world,
-                             journal=Path(jdir) / f"journal.rank{rank}.jsonl", run_id="t")
+    jpath = Path(jdir) / f"journal.rank{rank}.jsonl"
+    lost = None
+    if rank == crash_rank:
+        # take the first group, then fail before journalling it (a host-side
+        # failure between steps); the others start once it holds the group
+        lost = store.add("t/next", 1) - 1
+        dist.barrier()
+    else:
+        if crash_rank is not None:
+            dist.barrier()
+        sweep.run_groups(groups, CANDS, evaluate, store, rank, journal=jpath, run_id="t")
     dist.barrier()
     if rank == 0:
-        verdicts, missing = sweep.merge(Path(jdir), shards)
+        verdicts, missing = sweep.merge(Path(jdir), shards, SIZES, VARIANTS)
+        n_missing = len(missing)
+        if missing:  # the lost group's seed is open for every candidate: reassign
+            sweep.run_shards(missing, evaluate, SIZES, VARIANTS, journal=jpath, rank=0)
+            verdicts, missing = sweep.merge(Path(jdir), shards, SIZES, VARIANTS)
         (Path(jdir) / "result.json").write_text(json.dumps(
-            {"missing": len(missing), "passed": sorted(c for c, v in verdicts.items() if v["passed"])}))
+            {"reassigned": n_missing, "missing": len(missing),
+             "passed": sorted(c for c, v in verdicts.items() if v["passed"])}))
+    _ = lost
     dist.destroy_process_group()
 
 
-def test_two_rank_gloo_dynamic_sweep(tmp_path):
+@pytest.mark.parametrize("crash_rank", [None, 1])
+def test_two_rank_gloo_group_sweep(tmp_path, crash_rank):
     port = _free_port()
-    mp.spawn(_dyn_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_group_worker, args=(2, port, str(tmp_path), crash_rank), nprocs=2, join=True)
     res = json.loads((tmp_path / "result.json").read_text())
     assert res["missing"] == 0
     assert res["passed"] == sorted(c for c in CANDS if c != "c3")
-    done = _journaled(tmp_path)
-    keys = [(c, s) for c, s, _ in done]
-    assert len(keys) == len(set(keys)) == 32  # every shard exactly once
-    # rank 0 finished its cheap block and took shards of rank 1's costly one
-    assert any(r == 0 and s == 1 for _, s, r in done)
+    done = []
+    for p in sorted(tmp_path.glob("journal.rank*.jsonl")):
+        done += [(tuple(d["group"]), d["rank"]) for d in map(json.loads, p.read_text().splitlines())
+                 if "group" in d]
+    keys = [g for g, _ in done]
+    assert len(keys) == len(set(keys))  # no group ran twice
+    n_groups = 2 * len(SIZES) * len(VARIANTS)
+    if crash_rank is None:
+        assert len(keys) == n_groups and res["reassigned"] == 0
+    else:
+        # the held group (largest size, seed 0) never ran; its seed's shards were reassigned
+        assert len(keys) == n_groups - 1 and (0, "large", VARIANTS[0]) not in keys
+        assert res["reassigned"] == len(CANDS)

@@ -721,6 +721,8 @@ class SubgraphCUDACodegen:
 
     # -- elementwise prologue fused into a row reduction ------------------------
 
+    ROW_STAGE_BYTES = 32 * 1024  # static shared memory for a row map's staged input rows
+
     _REDUCE_INIT = {"sum": "0.0f", "mean": "0.0f", "prod": "1.0f",
                     "max": "__int_as_float(0xff800000u)", "min": "__int_as_float(0x7f800000u)"}
 
@@ -758,16 +760,52 @@ class SubgraphCUDACodegen:
         n = _numel(out_shape)
         it = "unsigned int" if n < 2**30 else "unsigned long long"
         u = "u" if it == "unsigned int" else "ull"
+        L: list[str] = []
+        L.append(f"// elementwise prologue ({len(plan.compute_nodes)} ops) + {op} over rows of {red}")
+        L.append(io_contract_line(classes, out_shape, [tuple(x.shape) for x in external_inputs], it)
+                 + f" rowred={red}")
+        L += plan.constant_lines(packed_type=None)
+        L.append("__shared__ float phew_smem[32 * 32];")
+        L += self._row_reduce_lines(plan, external_inputs, inp_names, in_dts, classes, out_shape,
+                                    op, f"({it})out0_size", it, u)
+        L += [
+            "if (phew_active && threadIdx.x == 0) {",
+            ("  phew_acc = __fdiv_rn(phew_acc, (float)phew_red);" if op == "mean" else ""),
+            f"  out0[phew_row] = phew_st_{_suffix(out_dt)}(phew_acc);",
+            "}",
+        ]
+        _ = keepdims
+        source = "\n".join(f"    {line}" if line else "" for line in L)
+        return source, inp_names, ["out0"]
+
+    def _row_reduce_lines(self, plan, ext_in, names, in_dts, classes, out_shape, op: str,
+                          rows_expr: str, it: str, u: str, staged: dict | None = None,
+                          after_header=()) -> list[str]:
+        """Rows of `out_shape[-1]` elements of `plan`'s single output, reduced
+        with ``op`` into ``phew_acc`` (valid in every thread of the row after
+        the code): `blockDim.x` threads per row, thread t accumulating
+        elements t, t + blockDim.x, ... in order, then a butterfly over the
+        warp and, across warps, over their partials in shared memory
+        (``phew_smem``, declared by the caller).  The order of
+        ``csrc/rows.cu``'s ``reduce_rows_kernel``.  Inputs named in `staged`
+        are read from that shared-memory copy of the row (``phew_lrow`` is
+        the row's offset in it); `after_header` lines go between the row
+        bookkeeping and the accumulation."""
+        red = out_shape[-1]
+        staged = staged or {}
         env = {}
         body = []
-        for node, nm, dt, (cls, ext) in zip(external_inputs, inp_names, in_dts, classes):
+        for node, nm, dt, (cls, ext) in zip(ext_in, names, in_dts, classes):
             v = plan.var(node)
-            idx = self._index(cls, ext, nm, node, out_shape, it, u)
-            body.append(f"const {VALUE_CTYPE[dt]} {v} = phew_ld({nm}[{idx}]);")
+            if nm in staged and cls == "full":
+                src = f"{staged[nm]}[phew_lrow + phew_c]"
+            else:
+                src = f"{nm}[{self._index(cls, ext, nm, node, out_shape, it, u)}]"
+            body.append(f"const {VALUE_CTYPE[dt]} {v} = phew_ld({src});")
             env[node.id] = (v, dt)
         body += plan.scalar_lines(env)
-        rv, rdt = env[root.id]
-        if rdt != out_dt:
+        rv, rdt = env[plan.outputs[0].id]
+        if rdt != dtype_name(plan.outputs[0].dtype):
             raise ValueError("cuda_codegen: reduction dtype differs from its input's")
         if op in ("max", "min"):
             cmp = ">" if op == "max" else "<"
@@ -778,17 +816,12 @@ class SubgraphCUDACodegen:
         else:
             comb = "phew_acc = phew_acc + phew_x;"
         shfl_comb = comb.replace("phew_x", "phew_y")
-        L: list[str] = []
-        L.append(f"// elementwise prologue ({len(plan.compute_nodes)} ops) + {op} over rows of {red}")
-        L.append(io_contract_line(classes, out_shape, [tuple(x.shape) for x in external_inputs], it)
-                 + f" rowred={red}")
-        L += plan.constant_lines(packed_type=None)
-        L += [
-            "__shared__ float phew_smem[32 * 32];",
+        L = [
             f"const {it} phew_red = {red}{u};",
-            f"const {it} phew_rows = ({it})out0_size;",
+            f"const {it} phew_rows = {rows_expr};",
             f"const {it} phew_row = ({it})blockIdx.x * blockDim.y + threadIdx.y;",
             "const bool phew_active = phew_row < phew_rows;",
+            *after_header,
             f"float phew_acc = {self._REDUCE_INIT[op]};",
             "if (phew_active) {",
             f"  for ({it} phew_c = threadIdx.x; phew_c < phew_red; phew_c += blockDim.x) {{",
@@ -821,14 +854,178 @@ class SubgraphCUDACodegen:
             "    }",
             "  }",
             "}",
-            "if (phew_active && threadIdx.x == 0) {",
-            ("  phew_acc = __fdiv_rn(phew_acc, (float)phew_red);" if op == "mean" else ""),
-            f"  out0[phew_row] = phew_st_{_suffix(out_dt)}(phew_acc);",
-            "}",
         ]
-        _ = keepdims
+        return L
+
+    # -- row reduction broadcast back into an elementwise chain ----------------
+
+    def emit_row_map(self, reduce_nodes, reduce_ext, reduce_root, op: str, map_nodes, map_ext,
+                     map_root, row_value, slots: dict, tpr: int, rpb: int
+                     ) -> tuple[str, list[str], list[str]]:
+        """Body of ``map_root`` where the elementwise DAG `map_nodes` reads
+        `row_value` = ``op(reduce_root, axis=-1, keepdims=True)`` of the
+        elementwise DAG `reduce_nodes` over the same rows (the
+        ``x * x -> mean -> rsqrt(. + eps) * x * w`` shape of an RMS norm):
+        one block row computes its row's reduction, then the mapped chain over
+        the row, so the reduced value never goes through HBM.
+
+        Bits: the reduction is ``_row_reduce_lines`` (the order of
+        ``reduce_rows_kernel``); row thread 0's result is rounded to the
+        reduction's dtype -- the value ``emit_reduce_rows`` would store --
+        and handed to the row's threads through shared memory; the mapped
+        chain then runs the per-element code of ``emit`` with that value in
+        place of its load.  So the result has the bits of materialising the
+        reduction and then the chain.
+
+        `slots` maps the id of every external spec of both DAGs except
+        `row_value` to its kernel input index.  Launch: block (tpr, rpb), one
+        block per `rpb` rows.  Raises ``ValueError`` when it cannot."""
+        out_shape = tuple(int(x) for x in map_root.shape)
+        if not out_shape or op not in self._REDUCE_INIT:
+            raise ValueError("cuda_codegen: not a row map")
+        if tuple(int(x) for x in reduce_root.shape) != out_shape:
+            raise ValueError("cuda_codegen: reduction rows differ from the mapped rows")
+        if tuple(int(x) for x in row_value.shape) != out_shape[:-1] + (1,):
+            raise ValueError("cuda_codegen: row value is not one per row")
+        red = out_shape[-1]
+        red_dt = dtype_name(reduce_root.dtype)
+        out_dt = dtype_name(map_root.dtype)
+        if red_dt not in ("float32", "float16", "bfloat16") or dtype_name(row_value.dtype) != red_dt:
+            raise ValueError("cuda_codegen: row map over a non-float reduction")
+        if out_dt not in CTYPE:
+            raise ValueError(f"cuda_codegen: unsupported dtype {out_dt!r}")
+        n_in = max(slots.values()) + 1 if slots else 0
+        in_shape: list = [None] * n_in
+        in_dt: list = [None] * n_in
+        for x in list(reduce_ext) + [m for m in map_ext if m is not row_value]:
+            k = slots[x.id]
+            in_shape[k] = tuple(int(v) for v in x.shape)
+            in_dt[k] = dtype_name(x.dtype)
+        if any(s is None for s in in_shape):
+            raise ValueError("cuda_codegen: unused kernel input slot")
+        classes = []
+        for shp in in_shape:
+            if len(shp) > 0 and not broadcast_compatible(shp, out_shape):
+                raise ValueError("cuda_codegen: input not broadcast-compatible with output")
+            cls = classify_input(shp, out_shape)
+            if cls[0] == "general":
+                raise ValueError("cuda_codegen: general broadcast in a row map")
+            classes.append(cls)
+        for d in in_dt:
+            if d not in CTYPE:
+                raise ValueError(f"cuda_codegen: unsupported dtype {d!r}")
+        names = [f"inp{k}" for k in range(n_in)]
+        n = _numel(out_shape)
+        it = "unsigned int" if n < 2**30 else "unsigned long long"
+        u = "u" if it == "unsigned int" else "ull"
+        precise = getattr(self, "precise_16bit", False)
+        rplan = _Plan(reduce_nodes, reduce_ext, [reduce_root], precise16=precise)
+        mplan = _Plan(map_nodes, map_ext, [map_root], precise16=precise, prefix="w")
+        r_names = [names[slots[x.id]] for x in reduce_ext]
+        r_dts = [in_dt[slots[x.id]] for x in reduce_ext]
+        r_classes = [classes[slots[x.id]] for x in reduce_ext]
+
+        # The mapped chain reads the row value as a one-element local array
+        # (the "scalar" load form), every other input as the chain kernel does.
+        m_names, m_dts, m_classes = [], [], []
+        for x in map_ext:
+            if x is row_value:
+                m_names.append("phew_rowv")
+                m_dts.append(red_dt)
+                m_classes.append(("scalar", 1))
+            else:
+                m_names.append(names[slots[x.id]])
+                m_dts.append(in_dt[slots[x.id]])
+                m_classes.append(classes[slots[x.id]])
+        itemsizes = [ITEMSIZE[d] for d, (c, _) in zip(m_dts, m_classes) if c in ("full", "suffix")]
+        itemsizes.append(ITEMSIZE[out_dt])
+        V = max(1, min(8, 16 // min(itemsizes)))
+        half_t = mplan.pure_half_type(m_dts, [out_dt])
+        vec_ok = red % V == 0 and all(c in ("full", "scalar") or ext % V == 0 for c, ext in m_classes)
+        packed = vec_ok and half_t is not None and V == 8
+
+        # Rows of the full-size inputs are staged in shared memory with
+        # 16-byte loads: the reduction then reads them in its (fixed, strided)
+        # order and the chain reads them again, with one pass over HBM.
+        full = [k for k in range(n_in) if classes[k][0] == "full"]
+        stage_bytes = rpb * red * sum(ITEMSIZE[in_dt[k]] for k in full)
+        staged = ({names[k]: f"phew_stg{k}" for k in full}
+                  if full and stage_bytes <= self.ROW_STAGE_BYTES else {})
+        stage_lines: list[str] = []
+        if staged:
+            stage_lines.append(f"const {it} phew_lrow = ({it})threadIdx.y * phew_red;")
+            stage_lines.append("if (phew_active) {")
+            for k in full:
+                ct, isz = CTYPE[in_dt[k]], ITEMSIZE[in_dt[k]]
+                E = 16 // isz
+                stage_lines.append("  {")
+                stage_lines.append(f"    const {ct}* phew_src = {names[k]} + phew_row * phew_red;")
+                if (red * isz) % 16 == 0:
+                    stage_lines += [
+                        "    if ((reinterpret_cast<phew_uptr>(phew_src) & 15u) == 0u) {",
+                        f"      for ({it} phew_q = threadIdx.x; phew_q < {red // E}{u}; phew_q += blockDim.x)",
+                        f"        *reinterpret_cast<phew_vec<{ct}, {E}>*>(phew_stg{k} + phew_lrow + phew_q * {E}{u}) =",
+                        f"            phew_ldv<{ct}, {E}>(phew_src + phew_q * {E}{u});",
+                        "    } else {",
+                    ]
+                else:
+                    stage_lines.append("    {")
+                stage_lines += [
+                    f"      for ({it} phew_c = threadIdx.x; phew_c < phew_red; phew_c += blockDim.x)",
+                    f"        phew_stg{k}[phew_lrow + phew_c] = phew_src[phew_c];",
+                    "    }",
+                    "  }",
+                ]
+            stage_lines.append("}")
+            stage_lines.append("__syncthreads();")
+
+        L: list[str] = []
+        L.append(f"// {op} over rows of {red} ({len(rplan.compute_nodes)}-op prologue), broadcast into "
+                 f"a {len(mplan.compute_nodes)}-op chain over the same rows")
+        L.append(io_contract_line(classes, out_shape, in_shape, it) + f" rowlen={red}")
+        L += rplan.constant_lines(packed_type=None)
+        L += mplan.constant_lines(packed_type=half_t if packed else None)
+        L.append("__shared__ float phew_smem[32 * 32];")
+        L.append(f"__shared__ {CTYPE[red_dt]} phew_rowv_s[32];")
+        for k in (full if staged else []):
+            L.append(f"__shared__ __align__(16) {CTYPE[in_dt[k]]} phew_stg{k}[{rpb * red}];")
+        L += self._row_reduce_lines(rplan, reduce_ext, r_names, r_dts, r_classes, out_shape, op,
+                                    f"({it})out0_size / {red}{u}", it, u, staged=staged,
+                                    after_header=stage_lines)
+        L += [
+            "if (threadIdx.x == 0) {",
+            ("  phew_acc = __fdiv_rn(phew_acc, (float)phew_red);" if op == "mean" else ""),
+            f"  phew_rowv_s[threadIdx.y] = phew_st_{_suffix(red_dt)}(phew_acc);",
+            "}",
+            "__syncthreads();",
+            "if (!phew_active) return;",
+            f"const {CTYPE[red_dt]} phew_rowv[1] = {{phew_rowv_s[threadIdx.y]}};",
+            f"const {it} phew_base = phew_row * phew_red;",
+        ]
+        scalar = self._scalar_body(mplan, map_ext, m_names, ["out0"], m_dts, [out_dt], m_classes,
+                                   out_shape, it, u, staged=staged)
+        if vec_ok:
+            ptrs = " | ".join(f"reinterpret_cast<phew_uptr>({nm})" for nm in names + ["out0"]
+                              if nm not in staged)
+            body = self._vector_body(mplan, map_ext, m_names, ["out0"], m_dts, [out_dt], m_classes,
+                                     out_shape, V, it, u, half_t, staged=staged)
+            L.append(f"if ((({ptrs}) & 15u) == 0u) {{")
+            L.append(f"  for ({it} phew_v = threadIdx.x; phew_v < phew_red / {V}{u}; phew_v += blockDim.x) {{")
+            L.append(f"    const {it} phew_off = phew_v * {V}{u};")
+            L.append(f"    const {it} elem = phew_base + phew_off;")
+            L += ["    " + b for b in body]
+            L.append("  }")
+            L.append("} else {")
+        else:
+            L.append("{")
+        L.append(f"  for ({it} phew_c = threadIdx.x; phew_c < phew_red; phew_c += blockDim.x) {{")
+        L.append(f"    const {it} phew_off = phew_c;")
+        L.append(f"    const {it} elem = phew_base + phew_c;")
+        L += ["    " + b for b in scalar]
+        L.append("  }")
+        L.append("}")
         source = "\n".join(f"    {line}" if line else "" for line in L)
-        return source, inp_names, ["out0"]
+        return source, names, ["out0"]
 
     # -- per-element form -----------------------------------------------------
 
@@ -844,11 +1041,19 @@ class SubgraphCUDACodegen:
         return general_index(elem, out_shape, tuple(int(s) for s in node.shape), it)
 
     def _scalar_body(self, plan, ext_in, inp_names, out_names, in_dts, out_dts, classes,
-                     out_shape, it, u) -> list[str]:
+                     out_shape, it, u, staged: dict | None = None) -> list[str]:
+        """Per-element statements for `elem`; a full-size input named in
+        `staged` is read from its shared-memory row copy at
+        ``phew_lrow + phew_off`` instead."""
+        staged = staged or {}
         lines = []
         env = {}
         for node, nm, dt, (cls, ext) in zip(ext_in, inp_names, in_dts, classes):
             v = plan.var(node)
+            if nm in staged and cls == "full":
+                lines.append(f"const {VALUE_CTYPE[dt]} {v} = phew_ld({staged[nm]}[phew_lrow + phew_off]);")
+                env[node.id] = (v, dt)
+                continue
             idx = self._index(cls, ext, nm, node, out_shape, it, u)
             lines.append(f"const {VALUE_CTYPE[dt]} {v} = phew_ld({nm}[{idx}]);")
             env[node.id] = (v, dt)
@@ -861,13 +1066,17 @@ class SubgraphCUDACodegen:
     # -- vector form ----------------------------------------------------------
 
     def _vector_body(self, plan, ext_in, inp_names, out_names, in_dts, out_dts, classes,
-                     out_shape, V, it, u, half_t) -> list[str]:
+                     out_shape, V, it, u, half_t, staged: dict | None = None) -> list[str]:
+        staged = staged or {}
         lines = []
         packed = half_t is not None and V == 8
         # Loads.
         for k, (node, nm, dt, (cls, ext)) in enumerate(zip(ext_in, inp_names, in_dts, classes)):
             ct = CTYPE[dt]
-            if cls == "full":
+            if cls == "full" and nm in staged:
+                lines.append(
+                    f"const phew_vec<{ct}, {V}> ld{k} = phew_ldv_s<{ct}, {V}>({staged[nm]} + phew_lrow + phew_off);")
+            elif cls == "full":
                 lines.append(f"const phew_vec<{ct}, {V}> ld{k} = phew_ldv<{ct}, {V}>({nm} + elem);")
             elif cls == "suffix":
                 lines.append(
@@ -933,8 +1142,9 @@ def _convert(v: str, src: str, dst: str) -> str:
 class _Plan:
     """Resolved chain: variable names, node order and dtype bookkeeping."""
 
-    def __init__(self, nodes, ext_in, ext_out, precise16: bool = False) -> None:
+    def __init__(self, nodes, ext_in, ext_out, precise16: bool = False, prefix: str = "v") -> None:
         self.precise16 = precise16
+        self.prefix = prefix
         self.nodes = list(nodes)
         self.ext_in = list(ext_in)
         self.outputs = list(ext_out)
@@ -980,7 +1190,7 @@ class _Plan:
     def var(self, node) -> str:
         if node.id not in self._names:
             self._ctr += 1
-            self._names[node.id] = f"v{self._ctr}"
+            self._names[node.id] = f"{self.prefix}{self._ctr}"
         return self._names[node.id]
 
     def pure_half_type(self, in_dts, out_dts) -> str | None:

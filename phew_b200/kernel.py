@@ -113,6 +113,12 @@ __device__ __forceinline__ phew_vec<T, V> phew_ldv(const T* p) {
   return r;
 }
 
+// A vector from shared (or any generic) memory, 16-byte aligned.
+template <typename T, int V>
+__device__ __forceinline__ phew_vec<T, V> phew_ldv_s(const T* p) {
+  return *reinterpret_cast<const phew_vec<T, V>*>(p);
+}
+
 template <typename T, int V>
 __device__ __forceinline__ void phew_stv(T* p, const phew_vec<T, V>& r) {
   constexpr int B = sizeof(T) * V;
@@ -381,6 +387,11 @@ def check_io_contract(source: str, in_shapes, out_shapes, name: str = "kernel") 
             n *= int(tok[len("rowred="):])
             if any(t.startswith("inp") and "=general" in t for t in line):
                 raise ValueError(f"{name}: general broadcasts are not fused into reductions")
+        # A row map reduces and rewrites rows of exactly `rowlen` elements.
+        if tok.startswith("rowlen="):
+            k = int(tok[len("rowlen="):])
+            if not out_shapes or not out_shapes[0] or int(out_shapes[0][-1]) != k:
+                raise ValueError(f"{name}: the kernel maps rows of {k} elements, output {out_shapes}")
     for tok in line:
         if tok == "idx32" and n >= 2**31 - 2**20:
             raise ValueError(f"{name}: {n} elements overflow the kernel's 32-bit indexing")

@@ -478,6 +478,11 @@ class _Lazy(array):
         return self._mt is None
 
     @property
+    def _pending_dag(self) -> bool:
+        """Pending, and an elementwise node (not a deferred row reduction)."""
+        return self._mt is None and self._op[0] != _ROW_REDUCE
+
+    @property
     def shape(self) -> tuple:
         return self._shape
 
@@ -498,6 +503,21 @@ class _Lazy(array):
         return self._dtype.size
 
 
+# A last-axis keepdims reduction of a pending DAG is deferred as well (its
+# `_op` is (_ROW_REDUCE, opname, source)): when the DAG that reads it covers
+# the same rows (the tail of an RMS or layer norm), reduction and tail run as
+# one row kernel (`_fused_row_map`); any other read computes it alone.
+_ROW_REDUCE = "__row_reduce__"
+
+
+def _row_reduce_plan(red: int) -> tuple[int, int]:
+    """(threads per row, rows per block) of ``reduce_rows_kernel`` in
+    csrc/rows.cu for rows of `red` elements: the fused forms use the same
+    mapping, so their sums are added in the same order."""
+    tpr = 256 if red >= 1024 else 32
+    return tpr, (4 if tpr == 32 else 1)
+
+
 def _fused_dag(root: "_Lazy"):
     """NodeSpecs of the pending DAG under `root` (topological order), its
     external inputs (specs and arrays, in first-visit order) and a key that
@@ -512,7 +532,7 @@ def _fused_dag(root: "_Lazy"):
         hit = memo.get(id(x))
         if hit is not None:
             return hit
-        if isinstance(x, _Lazy) and x._mt is None:
+        if isinstance(x, _Lazy) and x._pending_dag:
             op, operands, cdt, ndt = x._op
             args, arg_keys = [], []
             for o in operands:
@@ -552,7 +572,21 @@ def _fused_dag(root: "_Lazy"):
 
 
 def _materialize(root: "_Lazy") -> None:
+    if root._op[0] == _ROW_REDUCE:
+        _, opname, src = root._op
+        out = _fused_reduce(opname, src, True) if isinstance(src, _Lazy) and src._pending_dag else None
+        if out is None:
+            out = _reduce_now(opname, array._wrap(asarray_device(src)._t), -1, True)
+        object.__setattr__(root, "_mt", out._t)
+        object.__setattr__(root, "_op", None)
+        return
     chain, ext_specs, ext_arrays, root_spec, key = _fused_dag(root)
+    # Deferred row reductions read by this DAG: the last one whose rows are
+    # the DAG's own runs inside its kernel; the others are computed first.
+    rows = [i for i, x in enumerate(ext_arrays) if isinstance(x, _Lazy) and x.pending]
+    for i in reversed(rows):
+        if _fused_row_map(root, chain, ext_specs, ext_arrays, root_spec, key, i):
+            return
     ckey = ("fused", key)
     kern = _kernel_cache.get(ckey)
     if kern is None:
@@ -568,6 +602,66 @@ def _materialize(root: "_Lazy") -> None:
     )
     object.__setattr__(root, "_mt", out[0]._t)
     object.__setattr__(root, "_op", None)
+
+
+def _row_map_parts(root, chain, ext_specs, ext_arrays, root_spec, key, i):
+    """(cache key, ``emit_row_map`` arguments, kernel input arrays) for
+    `root`, whose DAG reads the deferred row reduction ``ext_arrays[i]``; None
+    when the reduction's source does not cover the same rows."""
+    m = ext_arrays[i]
+    _, opname, src = m._op
+    if root.ndim < 1 or tuple(src.shape) != tuple(root.shape) or root.size == 0:
+        return None
+    if isinstance(src, _Lazy) and src.pending and not src._pending_dag:
+        return None  # a reduction of a deferred reduction: computed on its own
+    tpr, rpb = _row_reduce_plan(root.shape[-1])
+    rchain, rext_specs, rext_arrays, rroot_spec, rkey = _fused_dag(src)
+    slots: dict = {}
+    arrays: list = []
+    where: dict = {}
+    pairs = list(zip(rext_specs, rext_arrays)) + [
+        (sp, x) for k, (sp, x) in enumerate(zip(ext_specs, ext_arrays)) if k != i]
+    for sp, x in pairs:
+        j = where.get(id(x))
+        if j is None:
+            j = where[id(x)] = len(arrays)
+            arrays.append(x)
+        slots[sp.id] = j
+    layout = (tuple(slots[sp.id] for sp in rext_specs),
+              tuple(slots.get(sp.id, -1) for sp in ext_specs))
+    ckey = ("row_map", opname, rkey, key, i, layout, tpr, rpb)
+    args = (rchain, rext_specs, rroot_spec, opname, chain, ext_specs, root_spec, ext_specs[i],
+            slots, tpr, rpb)
+    return ckey, args, arrays
+
+
+def _fused_row_map(root, chain, ext_specs, ext_arrays, root_spec, key, i) -> bool:
+    """Materialise `root`, whose DAG reads the deferred row reduction
+    ``ext_arrays[i]``, as one row kernel (``emit_row_map``): the reduction
+    and the chain that reads it over the same rows; False when it cannot."""
+    parts = _row_map_parts(root, chain, ext_specs, ext_arrays, root_spec, key, i)
+    if parts is None:
+        return False
+    ckey, args, arrays = parts
+    kern = _kernel_cache.get(ckey)
+    if kern is None:
+        try:
+            src_code, in_names, out_names = SubgraphCUDACodegen().emit_row_map(*args)
+        except ValueError:
+            _kernel_cache[ckey] = False
+            return False
+        kern = CudaKernel(f"phew_row_{args[3]}_map_{len(args[0])}_{len(chain)}", in_names,
+                          out_names, src_code)
+        _kernel_cache[ckey] = kern
+    if kern is False:
+        return False
+    tpr, rpb = args[-2], args[-1]
+    blocks = -(-(root.size // root.shape[-1]) // rpb)
+    out = kern(inputs=[asarray_device(x) for x in arrays], output_shapes=[root._shape],
+               output_dtypes=[root._dtype], grid=(blocks * tpr, rpb, 1), threadgroup=(tpr, rpb, 1))
+    object.__setattr__(root, "_mt", out[0]._t)
+    object.__setattr__(root, "_op", None)
+    return True
 
 
 def _softmax_row_plan(cols: int, itemsize: int):
@@ -834,8 +928,7 @@ def _fused_reduce(opname: str, a: "_Lazy", keepdims: bool):
     red = a.shape[-1]
     if red == 0 or a.size == 0:
         return None
-    tpr = 256 if red >= 1024 else 32
-    rpb = 4 if tpr == 32 else 1
+    tpr, rpb = _row_reduce_plan(red)
     chain, ext_specs, ext_arrays, root_spec, key = _fused_dag(a)
     ckey = ("fused_reduce", opname, key)
     kern = _kernel_cache.get(ckey)
@@ -861,7 +954,22 @@ def _reduce(opname: str, a, axis=None, keepdims=False) -> array:
     a = a if isinstance(a, array) else array(a)
     if a.dtype.code is None:
         raise NotImplementedError(f"{opname} over {a.dtype.name} arrays")
-    if (isinstance(a, _Lazy) and a.pending and a.ndim >= 1
+    last_axis = a.ndim >= 1 and _norm_axes(a, axis) == (a.ndim - 1,)
+    if (_tracing() and last_axis and keepdims and a.size > 0
+            and a.dtype in (float32, float16, bfloat16)
+            and not (isinstance(a, _Lazy) and a.pending and not a._pending_dag)):
+        m = object.__new__(_Lazy)
+        object.__setattr__(m, "_op", (_ROW_REDUCE, opname, a))
+        object.__setattr__(m, "_shape", tuple(a.shape[:-1]) + (1,))
+        object.__setattr__(m, "_dtype", a.dtype)
+        object.__setattr__(m, "_mt", None)
+        return m
+    return _reduce_now(opname, a, axis, keepdims)
+
+
+def _reduce_now(opname: str, a: array, axis, keepdims: bool) -> array:
+    """`opname` of `a` computed now (never deferred)."""
+    if (isinstance(a, _Lazy) and a._pending_dag and a.ndim >= 1
             and _norm_axes(a, axis) == (a.ndim - 1,)):
         fused = _fused_reduce(opname, a, keepdims)
         if fused is not None:
@@ -929,7 +1037,7 @@ def softmax(a, axis=-1, precise=False, **_) -> array:
     if ax != a.ndim - 1:
         moved = swapaxes(a, ax, a.ndim - 1)
         return swapaxes(softmax(moved, axis=-1), ax, a.ndim - 1)
-    if isinstance(a, _Lazy) and a.pending:
+    if isinstance(a, _Lazy) and a._pending_dag:
         fused = _fused_softmax(a)
         if fused is not None:
             return fused

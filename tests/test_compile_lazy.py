@@ -140,3 +140,128 @@ def test_dag_walk_leaves_no_reference_cycle(core):
         assert ref() is None
     finally:
         gc.enable()
+
+
+def _rms_tail(core, shape, dtype=torch.bfloat16):
+    x = _arr(core, shape, dtype)
+    w = _arr(core, shape[-1:], dtype)
+    eps = core.array._wrap(torch.tensor(1e-5, dtype=dtype))
+    core.trace_enter()
+    try:
+        m = core.mean(x * x, axis=[len(shape) - 1], keepdims=True)
+        y = x * core.rsqrt(m + eps) * w
+        parts = core._fused_dag(y)
+    finally:
+        core.trace_exit()
+    return m, y, parts
+
+
+def test_keepdims_row_reduction_is_deferred(core):
+    m, y, (chain, ext_specs, ext_arrays, root, key) = _rms_tail(core, (2, 3, 64))
+    assert isinstance(m, core._Lazy) and m.pending and not m._pending_dag
+    assert m.shape == (2, 3, 1) and m.dtype.name == "bfloat16"
+    assert m._op[0] == core._ROW_REDUCE and m._op[1] == "mean"
+    # the tail's DAG reads the deferred mean as an external input
+    assert sum(1 for a in ext_arrays if a is m) == 1
+
+
+@pytest.mark.parametrize("shape,dtype", [((8, 16, 4096), torch.bfloat16), ((3, 7, 1000), torch.float16),
+                                         ((5, 256), torch.float32), ((4, 96), torch.bfloat16)])
+def test_row_map_source_compiles(core, shape, dtype):
+    from test_cuda_codegen import nvrtc_compile
+
+    from phew_b200.emit.cuda_codegen import SubgraphCUDACodegen
+    from phew_b200.kernel import check_io_contract, full_source
+
+    m, y, (chain, ext_specs, ext_arrays, root, key) = _rms_tail(core, shape, dtype)
+    i = [k for k, a in enumerate(ext_arrays) if a is m][0]
+    ckey, args, arrays = core._row_map_parts(y, chain, ext_specs, ext_arrays, root, key, i)
+    src, ins, outs = SubgraphCUDACodegen().emit_row_map(*args)
+    # x is read by both the reduction and the tail: one kernel input (x, eps, w)
+    assert len(arrays) == 3 and len(ins) == 3
+    assert sum(1 for a in arrays if a.shape == shape) == 1
+    assert f"rowlen={shape[-1]}" in src and "phew_rowv" in src
+    dts = [a.dtype.name for a in arrays]
+    full = full_source("k", ins, outs, src, "", dts, [y.dtype.name])
+    rc, log = nvrtc_compile(full)
+    assert rc == 0, log
+    check_io_contract(src, [a.shape for a in arrays], [y.shape])
+    check_io_contract(src, [(11,) + shape[1:], (), shape[-1:]], [(11,) + shape[1:]])  # other row counts
+    with pytest.raises(ValueError, match="rows of"):  # other row lengths are refused
+        check_io_contract(src, [shape[:-1] + (shape[-1] * 2,), (), (shape[-1] * 2,)],
+                          [shape[:-1] + (shape[-1] * 2,)])
+
+
+def test_row_map_refuses_other_row_shapes(core):
+    x = _arr(core, (4, 64))
+    z = _arr(core, (2, 4, 64))
+    core.trace_enter()
+    try:
+        m = core.mean(x * x, axis=-1, keepdims=True)
+        y = z * m  # broadcasts over another leading axis: not the reduction's rows
+        chain, ext_specs, ext_arrays, root, key = core._fused_dag(y)
+    finally:
+        core.trace_exit()
+    i = [k for k, a in enumerate(ext_arrays) if a is m][0]
+    assert core._row_map_parts(y, chain, ext_specs, ext_arrays, root, key, i) is None
+
+
+def test_layer_norm_fuses_the_second_reduction(core):
+    """x - mean(x), then mean of its square, then the tail: the tail's DAG
+    reads two deferred reductions; the variance (whose rows are the tail's)
+    runs in the tail's kernel and reads the mean as an ordinary input."""
+    from test_cuda_codegen import nvrtc_compile
+
+    from phew_b200.emit.cuda_codegen import SubgraphCUDACodegen
+    from phew_b200.kernel import full_source
+
+    x = _arr(core, (4, 9, 512))
+    w = _arr(core, (512,))
+    core.trace_enter()
+    try:
+        m = core.mean(x, axis=-1, keepdims=True)  # a plain input's reduction is deferred too
+        assert isinstance(m, core._Lazy) and m._op[0] == core._ROW_REDUCE and m._op[2] is x
+        d = x - m
+        v = core.mean(d * d, axis=-1, keepdims=True)
+        y = d * core.rsqrt(v + 1e-5) * w
+        chain, ext_specs, ext_arrays, root, key = core._fused_dag(y)
+    finally:
+        core.trace_exit()
+    pend = [k for k, a in enumerate(ext_arrays) if isinstance(a, core._Lazy) and a.pending]
+    assert [ext_arrays[k] for k in pend] == [m, v]
+    parts = core._row_map_parts(y, chain, ext_specs, ext_arrays, root, key, pend[-1])
+    assert parts is not None
+    ckey, args, arrays = parts
+    assert any(a is m for a in arrays) and not any(a is v for a in arrays)
+    src, ins, outs = SubgraphCUDACodegen().emit_row_map(*args)
+    full = full_source("k", ins, outs, src, "", [a.dtype.name for a in arrays], ["bfloat16"])
+    rc, log = nvrtc_compile(full)
+    assert rc == 0, log
+    # the mean's own row map: its source (x) is a plain input, read once
+    mparts = core._row_map_parts(y, chain, ext_specs, ext_arrays, root, key, pend[0])
+    assert mparts is not None
+
+
+def test_deferred_reduction_materialises_without_deferring_again(core, monkeypatch):
+    """Reading a deferred reduction while tracing computes it (once) instead
+    of deferring it again."""
+    x = _arr(core, (3, 8))
+    calls = []
+
+    def fake_now(opname, a, axis, keepdims):
+        calls.append((opname, a.shape, axis, keepdims))
+        return core.array._wrap(torch.ones((3, 1), dtype=torch.bfloat16))
+
+    monkeypatch.setattr(core, "_reduce_now", fake_now)
+    core.trace_enter()
+    try:
+        m = core.max(x, axis=-1, keepdims=True)
+        assert isinstance(m, core._Lazy) and m.pending
+        t = m._t
+    finally:
+        core.trace_exit()
+    assert calls == [("max", (3, 8), -1, True)]
+    assert not m.pending and tuple(t.shape) == (3, 1)
+    # outside tracing nothing is deferred
+    core.max(x, axis=-1, keepdims=True)
+    assert len(calls) == 2

@@ -154,3 +154,83 @@ def test_fused_row_reduction_matches_materialised(mx, op, dtype, cols):
         return getattr(mx, op)(y, axis=-1, keepdims=(op == "mean")), getattr(mx, op)(y * y, axis=2)
 
     _same(mx, f, x, s)
+
+
+def _row_maps(op=None):
+    from phew_b200.mx import core
+
+    return [k for k, v in core._kernel_cache.items()
+            if isinstance(k, tuple) and k and k[0] == "row_map" and v and (op is None or k[1] == op)]
+
+
+@pytest.mark.parametrize("dtype,shape", [("bfloat16", (4, 512, 4096)), ("float16", (3, 7, 1000)),
+                                         ("float32", (5, 2048)), ("bfloat16", (4, 33, 96)),
+                                         ("bfloat16", (2, 3, 4100)), ("float32", (7, 33))])
+def test_row_map_rms_tail_one_kernel(mx, dtype, shape):
+    """x * rsqrt(mean(x * x) + eps) * w: the reduction and the tail run as one
+    row kernel, with the bits of op-by-op evaluation (vector and scalar
+    forms, one and several rows per block, a partial last block)."""
+    rng = np.random.default_rng(sum(shape))
+    x = _rand(mx, rng, shape, dtype, 2.0)
+    w = _rand(mx, rng, shape[-1:], dtype)
+    before = len(_row_maps("mean"))
+
+    def f(x, w):
+        t = mx.mean(x * x, axis=[len(shape) - 1], keepdims=True)
+        return x * mx.rsqrt(t + mx.array(1e-5, dtype=getattr(mx, dtype))) * w
+
+    _same(mx, f, x, w)
+    assert len(_row_maps("mean")) >= max(before, 1)
+
+
+@pytest.mark.parametrize("op", ["max", "min", "sum", "prod"])
+def test_row_map_other_reductions(mx, op):
+    """x - op(x) and x * op(x) over rows, with NaN, signed zeros and a row of
+    equal values (max / min keep the first of equal values, as the
+    materialised reduction does)."""
+    rng = np.random.default_rng(7)
+    xv = (rng.standard_normal((6, 40, 300)).astype(np.float32)).astype(np.float16)
+    xv[0, 0, 5] = np.nan
+    xv[1, 1, :] = 0.0
+    xv[1, 1, ::2] = -0.0
+    xv[2, 2, :] = 1.5
+    x = mx.array(xv)
+
+    def f(x):
+        y = x * 0.5 if op != "prod" else 1.0 + x * 0.001
+        r = getattr(mx, op)(y, axis=-1, keepdims=True)
+        return y - r, y * r
+
+    _same(mx, f, x)
+    assert _row_maps(op)
+
+
+def test_row_map_layer_norm_and_plain_input(mx):
+    """mean(x) of a plain input, x - mean, the variance and the tail: the
+    variance and tail run as one row kernel after the mean."""
+    rng = np.random.default_rng(11)
+    x = _rand(mx, rng, (8, 64, 1024), "bfloat16", 3.0)
+    w = _rand(mx, rng, (1024,), "bfloat16")
+    b = _rand(mx, rng, (1024,), "bfloat16")
+
+    def f(x, w, b):
+        m = mx.mean(x, axis=-1, keepdims=True)
+        d = x - m
+        v = mx.mean(d * d, axis=-1, keepdims=True)
+        return d * mx.rsqrt(v + 1e-5) * w + b
+
+    _same(mx, f, x, w, b)
+
+
+def test_deferred_reduction_read_elsewhere(mx):
+    """A deferred row reduction that is returned, reshaped or read by a DAG
+    over other rows is computed on its own, with the same bits."""
+    rng = np.random.default_rng(12)
+    x = _rand(mx, rng, (4, 16, 256), "bfloat16")
+    z = _rand(mx, rng, (2, 4, 16, 256), "bfloat16")
+
+    def f(x, z):
+        m = mx.mean(x * x, axis=-1, keepdims=True)
+        return m, mx.reshape(m, [4, 16]), z * m, x / m
+
+    _same(mx, f, x, z)

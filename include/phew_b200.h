@@ -180,10 +180,13 @@ int phew_l2_flush(void* buf, size_t bytes, void* stream);
  *   stride_a / stride_b / stride_c: element strides between batches; 0 on an
  *   operand broadcasts it over the batch.
  *   row_scale = 1 multiplies row m of the product by
- *   rsqrt(mean_k(A[m, k]^2) + eps), computed inside the kernel from the A tiles
- *   it already loads (the normed matmul (x @ W) * rsqrt(mean(x^2) + eps)).
+ *   rsqrt(mean_k(A[m, k]^2) + eps) (the normed matmul
+ *   (x @ W) * rsqrt(mean(x^2) + eps)): one pass over A computes the factor per
+ *   row into stream-ordered memory (cudaMallocAsync / cudaFreeAsync on
+ *   `stream`, so graph capture works), and the GEMM's epilogue applies it to
+ *   the fp32 accumulator.
  *   row_scale = 2 writes each row's sum of squares of A instead of the
- *   product (a diagnostic of the fused norm).
+ *   product (a diagnostic of the row statistic).
  *   error_flag (device int, may be NULL) receives PHEW_ERR_TIMEOUT if a
  *   bounded pipeline wait ran out.
  * in_dtype bf16/f16 use the tensor cores when every row stride and base is

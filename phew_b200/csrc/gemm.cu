@@ -26,12 +26,18 @@
 //               back to the producer and each finished tile to the epilogue
 //   warps 2-5   epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
 //               32*(w%4)..), hand it back to the MMA warp after the last
-//               read, scale, convert, store; with the fused row scale they
-//               also accumulate each row's sum of squares from the A tiles
-//               while the main loop runs, so the norm costs no extra HBM pass
+//               read, scale, convert, store
+// The row scale of the normed matmul comes from a short pass before the GEMM
+// (`row_stats_kernel`: one warp per row of A, 16-byte loads, 2 bytes of HBM
+// per element) that writes rsqrt(mean(A^2) + eps) per row; the epilogue
+// multiplies the fp32 accumulator by it.  Computing it inside the GEMM from
+// the A tiles in shared memory repeats it for every column block (16x at
+// N = 4096) and makes the epilogue warps gate the refill of every stage.
 // Every mbarrier wait is bounded; a wait that runs out sets *error_flag and the
 // kernel winds down instead of spinning.
 #include "tc_common.cuh"
+
+#include <string>
 
 namespace phew {
 namespace gemm {
@@ -66,11 +72,50 @@ struct Params {
   long long ldc;
   long long c_batch_stride;
   int out_dtype;  // PHEW_F32 / PHEW_F16 / PHEW_BF16
-  int row_scale;  // 1: fused rsqrt(mean(A^2) + eps) per row
+  int row_scale;  // 1: rows scaled by rsqrt(mean(A^2) + eps); 2: rows replaced by sum(A^2)
   int tma_store;  // 1: 16-bit C written by TMA stores through shared memory
   float eps;
   int* error_flag;
+  const float* row_vec;  // row_scale != 0: the per-row factor (or sum), [a_batched ? batch : 1][M]
 };
+
+// Per-row statistic of A for the row scale: mode 1 writes
+// rsqrt(sum(A[m, :]^2) / K + eps), mode 2 the sum of squares itself.  One
+// warp per row (16-byte loads when the row is 16-byte aligned), fp32
+// accumulation, lanes combined by a butterfly.
+template <typename T>
+__global__ void row_stats_kernel(const T* __restrict__ A, float* __restrict__ out, int M, int nb, int K,
+                                 long long lda, long long sa, int mode, float eps) {
+  const int warps = static_cast<int>(gridDim.x * blockDim.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const long long rows = static_cast<long long>(nb) * M;
+  for (long long r = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
+    const T* row = A + (r / M) * sa + (r % M) * lda;
+    float ss = 0.f;
+    int k0 = 0;
+    if ((reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+      constexpr int E = 16 / sizeof(T);
+      const int nv = K / E;
+      for (int v = lane; v < nv; v += 32) {
+        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(row) + v);
+        const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+          const float x = to_f32(e[i]);
+          ss = fmaf(x, x, ss);
+        }
+      }
+      k0 = nv * E;
+    }
+    for (int k = k0 + lane; k < K; k += 32) {
+      const float x = to_f32(row[k]);
+      ss = fmaf(x, x, ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) out[r] = mode == 2 ? ss : 1.0f / sqrtf(ss / static_cast<float>(K) + eps);
+  }
+}
 
 template <typename T>
 __device__ __forceinline__ void store_row32(T* dst, const float* v, int ncols) {
@@ -131,7 +176,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], p.row_scale ? 5 : 1);  // MMA commit (+ 4 epilogue warps)
+      mbar_init(&empty[s], 1);  // MMA commit
     }
     for (int a = 0; a < ACC; ++a) {
       mbar_init(&acc_full[a], 1);
@@ -227,69 +272,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       int bz, m0, n0;
       coords(t, bz, m0, n0);
       const int a = it % ACC;
-      float ss[MT];
-#pragma unroll
-      for (int h = 0; h < MT; ++h) ss[h] = 0.f;
-      if (p.row_scale) {
-        // Sum of squares of this warp's 32 rows (per 128-row half), read
-        // cooperatively: in read i, lanes 8g..8g+7 cover the 128-byte row
-        // 4i+g, 16 bytes each, so every read instruction touches 4 whole
-        // rows and no two lanes of a phase share a bank.  The order within
-        // a row does not matter, so the 128B swizzle needs no undoing.
-        float part[MT][8];
-#pragma unroll
-        for (int h = 0; h < MT; ++h)
-#pragma unroll
-          for (int i = 0; i < 8; ++i) part[h][i] = 0.f;
-        for (int kb = 0; kb < num_kb; ++kb, ++kg) {
-          const int s = kg % C::STAGES;
-          const uint32_t ph = (kg / C::STAGES) & 1;
-          if (!mbar_wait(&full[s], ph, p.error_flag)) {
-            ok = false;
-            break;
-          }
-#pragma unroll
-          for (int h = 0; h < MT; ++h) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int r = h * BM + quarter * 32 + 4 * i + (lane >> 3);
-              const uint4 raw = *reinterpret_cast<const uint4*>(smem + s * C::STAGE_BYTES + r * 128 + (lane & 7) * 16);
-              const uint16_t* hv = reinterpret_cast<const uint16_t*>(&raw);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                float x;
-                if (BF16) {
-                  x = __uint_as_float(static_cast<uint32_t>(hv[e]) << 16);
-                } else {
-                  asm("cvt.f32.f16 %0, %1;" : "=f"(x) : "h"(hv[e]));
-                }
-                part[h][i] = fmaf(x, x, part[h][i]);
-              }
-            }
-          }
-          // The next TMA write into this stage must be ordered after these
-          // generic-proxy reads.
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&empty[s]);
-        }
-        // Reduce over the 8 lanes that share a row, then give lane R the sum
-        // of row R (held by lanes 8 * (R % 4).., read i = R / 4).
-#pragma unroll
-        for (int h = 0; h < MT; ++h) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            part[h][i] += __shfl_xor_sync(0xffffffffu, part[h][i], 1);
-            part[h][i] += __shfl_xor_sync(0xffffffffu, part[h][i], 2);
-            part[h][i] += __shfl_xor_sync(0xffffffffu, part[h][i], 4);
-          }
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float v = __shfl_sync(0xffffffffu, part[h][i], 8 * (lane & 3));
-            if ((lane >> 2) == i) ss[h] = v;
-          }
-        }
-      }
       if (ok && !mbar_wait(&acc_full[a], (it / ACC) & 1, p.error_flag)) ok = false;
       if (!ok) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -300,7 +282,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         // distinct banks) -> one TMA store of the box, double-buffered.
         uint8_t* my_out = out_stage + (warp - 2) * (2 * 32 * 128);
         for (int h = 0; h < MT; ++h) {
-          const float scale = p.row_scale ? 1.0f / sqrtf(ss[h] / static_cast<float>(p.K) + p.eps) : 1.0f;
+          const int srow = m0 + h * BM + quarter * 32 + lane;
+          const float scale = (p.row_scale && srow < p.M) ? p.row_vec[(p.a_batched ? bz : 0) * p.M + srow] : 1.0f;
 #pragma unroll 1
           for (int c = 0; c < BN; c += 64, ++out_idx) {
             uint32_t r[64];
@@ -326,7 +309,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                   lo *= scale;
                   hi *= scale;
                 } else if (p.row_scale == 2) {  // diagnostic: the row's sum of squares
-                  lo = hi = ss[h];
+                  lo = hi = scale;
                 }
                 w[q] = pack_out(lo, hi, p.out_dtype == PHEW_BF16);
               }
@@ -344,8 +327,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         continue;
       }
       for (int h = 0; h < MT; ++h) {
-        const float scale = p.row_scale ? 1.0f / sqrtf(ss[h] / static_cast<float>(p.K) + p.eps) : 1.0f;
         const int row = m0 + h * BM + quarter * 32 + lane;
+        const float scale = (p.row_scale && row < p.M) ? p.row_vec[(p.a_batched ? bz : 0) * p.M + row] : 1.0f;
         const long long cbase = static_cast<long long>(bz) * p.c_batch_stride + static_cast<long long>(row) * p.ldc;
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
@@ -369,7 +352,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
               for (int i = 0; i < 32; ++i) v[i] *= scale;
             } else if (p.row_scale == 2) {  // diagnostic: the row's sum of squares
 #pragma unroll
-              for (int i = 0; i < 32; ++i) v[i] = ss[h];
+              for (int i = 0; i < 32; ++i) v[i] = scale;
             }
             const int ncols = p.N - (n0 + c);
             if (p.out_dtype == PHEW_BF16)
@@ -421,17 +404,9 @@ __global__ void gemm_simt_kernel(const T* A, const T* B, Params p, long long lda
     __syncthreads();
   }
   if (row < p.M && col < p.N) {
-    float scale = 1.f;
-    if (p.row_scale) {
-      float ss = 0.f;
-      for (int k = 0; k < p.K; ++k) {
-        const float x = to_f32(Ab[row * lda + k]);
-        ss = fmaf(x, x, ss);
-      }
-      scale = 1.0f / sqrtf(ss / static_cast<float>(p.K) + p.eps);
-    }
+    const float rv = p.row_scale ? p.row_vec[(p.a_batched ? bz : 0) * p.M + row] : 1.f;
     const long long o = static_cast<long long>(bz) * p.c_batch_stride + static_cast<long long>(row) * p.ldc + col;
-    const float v = acc * scale;
+    const float v = p.row_scale == 2 ? rv : acc * rv;
     if (p.out_dtype == PHEW_BF16) static_cast<bf16*>(p.C)[o] = from_f32<bf16>(v);
     else if (p.out_dtype == PHEW_F16) static_cast<f16*>(p.C)[o] = from_f32<f16>(v);
     else static_cast<float*>(p.C)[o] = v;
@@ -448,6 +423,18 @@ int make_map(CUtensorMap* tm, const void* base, bool bf16, uint64_t d0, uint64_t
   const uint64_t strides[2] = {s1_bytes, s2_bytes};
   const uint32_t box[3] = {b0, b1, 1};
   return make_map_16bit(tm, base, bf16, 3, dims, strides, box);
+}
+
+template <typename T>
+int launch_row_stats(const void* A, float* out, const Params& p, long long lda, long long sa, cudaStream_t st) {
+  const int nb = p.a_batched ? p.batch : 1;
+  const long long rows = static_cast<long long>(nb) * p.M;
+  long long blocks = (rows + 7) / 8;  // 8 warps (rows) per 256-thread block
+  const long long cap = static_cast<long long>(sm_count_current()) * 8;
+  if (blocks > cap) blocks = cap;
+  row_stats_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, st>>>(static_cast<const T*>(A), out, p.M, nb, p.K,
+                                                                     lda, sa, p.row_scale, p.eps);
+  return launch_status("row_stats_kernel");
 }
 
 // Persistent grid: one CTA per SM at most, each looping over tiles.
@@ -500,6 +487,9 @@ int launch_tc(const void* A, const void* B, const Params& p, long long lda, long
   return launch_status("gemm_tc_kernel");
 }
 
+int gemm_dispatch(const void* A, const void* B, const Params& p, int64_t lda, int64_t ldb, int64_t stride_a,
+                  int64_t stride_b, int in_dtype, cudaStream_t st);
+
 }  // namespace gemm
 }  // namespace phew
 
@@ -537,6 +527,35 @@ extern "C" int phew_gemm(const void* A, const void* B, void* Cout, int64_t M, in
   p.tma_store = 0;
   p.eps = eps;
   p.error_flag = error_flag;
+  p.row_vec = nullptr;
+  if (row_scale) {
+    // The per-row factor lives in stream-ordered memory allocated here and
+    // freed after the GEMM on the same stream: no sharing between streams,
+    // and graph capture records it as allocation / free nodes.
+    PHEW_REQUIRE(row_scale == 1 || row_scale == 2, "phew_gemm: row_scale must be 0, 1 or 2");
+    PHEW_REQUIRE(K > 0, "phew_gemm: the row scale needs K > 0");
+    float* w = nullptr;
+    const size_t bytes = static_cast<size_t>(stride_a != 0 ? batch : 1) * static_cast<size_t>(M) * sizeof(float);
+    PHEW_CHECK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&w), bytes, st));
+    p.row_vec = w;
+    int r = in_dtype == PHEW_BF16 ? launch_row_stats<bf16>(A, w, p, lda, stride_a, st)
+            : in_dtype == PHEW_F16 ? launch_row_stats<f16>(A, w, p, lda, stride_a, st)
+                                   : launch_row_stats<float>(A, w, p, lda, stride_a, st);
+    if (!r) r = gemm_dispatch(A, B, p, lda, ldb, stride_a, stride_b, in_dtype, st);
+    const cudaError_t fe = cudaFreeAsync(w, st);
+    if (!r && fe != cudaSuccess) r = set_error(PHEW_ERR_CUDA, std::string("phew_gemm: cudaFreeAsync: ") + cudaGetErrorString(fe));
+    return r;
+  }
+  return gemm_dispatch(A, B, p, lda, ldb, stride_a, stride_b, in_dtype, st);
+}
+
+namespace phew {
+namespace gemm {
+
+// Kernel choice for the validated call.
+int gemm_dispatch(const void* A, const void* B, const Params& p, int64_t lda, int64_t ldb, int64_t stride_a,
+                  int64_t stride_b, int in_dtype, cudaStream_t st) {
+  const int64_t K = p.K, M = p.M, N = p.N, batch = p.batch;
   const bool aligned16 =
       ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) == 0 &&
       (lda * 2) % 16 == 0 && (ldb * 2) % 16 == 0 && (stride_a * 2) % 16 == 0 &&
@@ -577,3 +596,6 @@ extern "C" int phew_gemm(const void* A, const void* B, void* Cout, int64_t M, in
                                                   stride_a, stride_b);
   return launch_status("gemm_simt_kernel");
 }
+
+}  // namespace gemm
+}  // namespace phew

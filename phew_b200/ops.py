@@ -247,8 +247,10 @@ def matmul(a, b, *, row_scale: bool = False, eps: float = 1e-5) -> array:
     """``a @ b`` with MLX semantics (batched, broadcast batch dims, 1-D
     operands promoted), on the tcgen05 GEMM.
 
-    ``row_scale=True`` returns ``(a @ b) * rsqrt(mean(a*a, -1) + eps)`` in one
-    kernel (the normed matmul of ``rules/primitive_subst.py:156-240``).
+    ``row_scale=True`` returns ``(a @ b) * rsqrt(mean(a*a, -1) + eps)`` (the
+    normed matmul of ``rules/primitive_subst.py:156-240``): one pass over
+    ``a`` for the per-row factor, then the GEMM with the factor applied in its
+    epilogue.
     """
     from . import dtypes as dt
     from .mx.core import _broadcast_shapes, astype, contiguous_copy, reshape

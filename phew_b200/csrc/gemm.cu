@@ -27,16 +27,20 @@
 //   warps 2-5   epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
 //               32*(w%4)..), hand it back to the MMA warp after the last
 //               read, scale, convert, store
-// The row scale of the normed matmul comes from a short pass before the GEMM
+// The row scale of the normed matmul comes from a short pass
 // (`row_stats_kernel`: one warp per row of A, 16-byte loads, 2 bytes of HBM
-// per element) that writes rsqrt(mean(A^2) + eps) per row; the epilogue
-// multiplies the fp32 accumulator by it.  Computing it inside the GEMM from
-// the A tiles in shared memory repeats it for every column block (16x at
-// N = 4096) and makes the epilogue warps gate the refill of every stage.
+// per element) that writes rsqrt(mean(A^2) + eps) per row; the GEMM is its
+// programmatic dependent launch, so the GEMM's main loop overlaps the pass
+// and only the epilogue waits for it (griddepcontrol.wait) before
+// multiplying the fp32 accumulator by the factor.  Computing the factor
+// inside the GEMM instead (from the A tiles in shared memory, or from HBM by
+// the epilogue warps) was measured slower: the epilogue warps then gate the
+// refill of every stage, or the next tile's main loop.
 // Every mbarrier wait is bounded; a wait that runs out sets *error_flag and the
 // kernel winds down instead of spinning.
 #include "tc_common.cuh"
 
+#include <mutex>
 #include <string>
 
 namespace phew {
@@ -79,41 +83,76 @@ struct Params {
   const float* row_vec;  // row_scale != 0: the per-row factor (or sum), [a_batched ? batch : 1][M]
 };
 
+// Sum of squares of one row of A (K elements) by one warp: 16-byte loads,
+// sixteen in flight per lane (a whole 4096-element 16-bit row per warp: the
+// loop is bound by memory latency, not bandwidth, otherwise) when the row
+// is 16-byte aligned, fp32 accumulation, lanes combined by a butterfly;
+// every lane gets the sum.
+template <typename T>
+__device__ __forceinline__ float row_sumsq(const T* __restrict__ row, int K, int lane) {
+  constexpr int U = 16;
+  float ss = 0.f;
+  int k0 = 0;
+  if ((reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+    constexpr int E = 16 / sizeof(T);
+    const int nv = K / E;
+    const uint4* rv = reinterpret_cast<const uint4*>(row);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    int v = lane;
+    for (; v + 32 * (U - 1) < nv; v += 32 * U) {
+      uint4 raw[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) raw[u] = __ldg(rv + v + 32 * u);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const T* e = reinterpret_cast<const T*>(&raw[u]);
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+          const float x = to_f32(e[i]);
+          acc[u & 3] = fmaf(x, x, acc[u & 3]);
+        }
+      }
+    }
+    for (; v < nv; v += 32) {
+      const uint4 raw = __ldg(rv + v);
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int i = 0; i < E; ++i) {
+        const float x = to_f32(e[i]);
+        acc[0] = fmaf(x, x, acc[0]);
+      }
+    }
+    ss = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+    k0 = nv * E;
+  }
+  for (int k = k0 + lane; k < K; k += 32) {
+    const float x = to_f32(row[k]);
+    ss = fmaf(x, x, ss);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  return ss;
+}
+
+__device__ __forceinline__ float row_stat_value(float ss, int K, int mode, float eps) {
+  return mode == 2 ? ss : 1.0f / sqrtf(ss / static_cast<float>(K) + eps);
+}
+
 // Per-row statistic of A for the row scale: mode 1 writes
 // rsqrt(sum(A[m, :]^2) / K + eps), mode 2 the sum of squares itself.  One
-// warp per row (16-byte loads when the row is 16-byte aligned), fp32
-// accumulation, lanes combined by a butterfly.
+// warp per row.
 template <typename T>
-__global__ void row_stats_kernel(const T* __restrict__ A, float* __restrict__ out, int M, int nb, int K,
+__global__ void __launch_bounds__(256, 1) row_stats_kernel(const T* __restrict__ A, float* __restrict__ out, int M, int nb, int K,
                                  long long lda, long long sa, int mode, float eps) {
+  // The GEMM that reads `out` may start now (it waits for this grid's
+  // completion before its first epilogue).
+  asm volatile("griddepcontrol.launch_dependents;");
   const int warps = static_cast<int>(gridDim.x * blockDim.x) >> 5;
   const int lane = threadIdx.x & 31;
   const long long rows = static_cast<long long>(nb) * M;
   for (long long r = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
-    const T* row = A + (r / M) * sa + (r % M) * lda;
-    float ss = 0.f;
-    int k0 = 0;
-    if ((reinterpret_cast<uintptr_t>(row) & 15) == 0) {
-      constexpr int E = 16 / sizeof(T);
-      const int nv = K / E;
-      for (int v = lane; v < nv; v += 32) {
-        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(row) + v);
-        const T* e = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-        for (int i = 0; i < E; ++i) {
-          const float x = to_f32(e[i]);
-          ss = fmaf(x, x, ss);
-        }
-      }
-      k0 = nv * E;
-    }
-    for (int k = k0 + lane; k < K; k += 32) {
-      const float x = to_f32(row[k]);
-      ss = fmaf(x, x, ss);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) out[r] = mode == 2 ? ss : 1.0f / sqrtf(ss / static_cast<float>(K) + eps);
+    const float ss = row_sumsq(A + (r / M) * sa + (r % M) * lda, K, lane);
+    if (lane == 0) out[r] = row_stat_value(ss, K, mode, eps);
   }
 }
 
@@ -267,13 +306,21 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     const int quarter = warp & 3;
-    uint32_t kg = 0, it = 0, out_idx = 0;
+    // With the row scale, the factors come from row_stats_kernel, launched
+    // just before this kernel as its programmatic-dependency primary: wait
+    // (once, before the first epilogue reads them) for it to complete.
+    bool rows_ready = !p.row_scale;
+    uint32_t it = 0, out_idx = 0;
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
       int bz, m0, n0;
       coords(t, bz, m0, n0);
       const int a = it % ACC;
       if (ok && !mbar_wait(&acc_full[a], (it / ACC) & 1, p.error_flag)) ok = false;
       if (!ok) break;
+      if (!rows_ready) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        rows_ready = true;
+      }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const uint32_t acc = tmem + a * (MT * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
       if (p.tma_store) {
@@ -425,12 +472,47 @@ int make_map(CUtensorMap* tm, const void* base, bool bf16, uint64_t d0, uint64_t
   return make_map_16bit(tm, base, bf16, 3, dims, strides, box);
 }
 
+// A memory pool per device for the row factors that keeps what it has
+// reserved (the default pool returns memory at every synchronisation and
+// maps it again on the next call).
+cudaMemPool_t row_pool() {
+  static std::mutex mu;
+  static cudaMemPool_t pools[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!pools[dev]) {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t pool = nullptr;
+    if (cudaMemPoolCreate(&pool, &props) != cudaSuccess) return nullptr;
+    uint64_t keep = ~0ull;
+    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    pools[dev] = pool;
+  }
+  return pools[dev];
+}
+
 template <typename T>
 int launch_row_stats(const void* A, float* out, const Params& p, long long lda, long long sa, cudaStream_t st) {
+  // Keep the SM's shared memory configured for the GEMM CTA that starts
+  // beside this kernel (a small carveout would hold the GEMM back until
+  // these blocks leave).
+  static bool carveout = false;
+  if (!carveout) {
+    PHEW_CHECK_CUDA(cudaFuncSetAttribute(row_stats_kernel<T>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                         static_cast<int>(cudaSharedmemCarveoutMaxShared)));
+    carveout = true;
+  }
   const int nb = p.a_batched ? p.batch : 1;
   const long long rows = static_cast<long long>(nb) * p.M;
-  long long blocks = (rows + 7) / 8;  // 8 warps (rows) per 256-thread block
-  const long long cap = static_cast<long long>(sm_count_current()) * 8;
+  // One 256-thread block per SM: 8 warps x a whole row each in flight
+  // saturate HBM, and the SM keeps room for the GEMM CTA that starts beside
+  // it (programmatic dependent launch).
+  long long blocks = (rows + 7) / 8;
+  const long long cap = static_cast<long long>(sm_count_current());
   if (blocks > cap) blocks = cap;
   row_stats_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, st>>>(static_cast<const T*>(A), out, p.M, nb, p.K,
                                                                      lda, sa, p.row_scale, p.eps);
@@ -483,12 +565,37 @@ int launch_tc(const void* A, const void* B, const Params& p, long long lda, long
   const long long tiles = static_cast<long long>((p.N + BN - 1) / BN) * ((p.M + C::ROWS - 1) / C::ROWS) * p.batch;
   PHEW_REQUIRE(tiles < (1LL << 31), "phew_gemm: too many tiles");
   const unsigned grid = static_cast<unsigned>(tiles < sm_count() ? tiles : sm_count());
+  if (q.row_scale) {
+    // Programmatic dependent launch after row_stats_kernel: the main loop
+    // overlaps that pass; the epilogue waits for it (griddepcontrol.wait).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kNumThreads);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    PHEW_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, MT, ACC, BF16>, ta, tb, tc, q));
+    return launch_status("gemm_tc_kernel");
+  }
   gemm_tc_kernel<BN, MT, ACC, BF16><<<grid, kNumThreads, C::SMEM, st>>>(ta, tb, tc, q);
   return launch_status("gemm_tc_kernel");
 }
 
 int gemm_dispatch(const void* A, const void* B, const Params& p, int64_t lda, int64_t ldb, int64_t stride_a,
                   int64_t stride_b, int in_dtype, cudaStream_t st);
+
+// The tensor-core kernels take 16-bit operands whose bases and row / batch
+// strides are 16-byte aligned (TMA); anything else goes to the SIMT kernel.
+inline bool uses_tensor_cores(const void* A, const void* B, int64_t lda, int64_t ldb, int64_t stride_a,
+                              int64_t stride_b, int64_t K, int in_dtype) {
+  return in_dtype != PHEW_F32 && K > 0 &&
+         ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) == 0 && (lda * 2) % 16 == 0 &&
+         (ldb * 2) % 16 == 0 && (stride_a * 2) % 16 == 0 && (stride_b * 2) % 16 == 0;
+}
 
 }  // namespace gemm
 }  // namespace phew
@@ -536,7 +643,9 @@ extern "C" int phew_gemm(const void* A, const void* B, void* Cout, int64_t M, in
     PHEW_REQUIRE(K > 0, "phew_gemm: the row scale needs K > 0");
     float* w = nullptr;
     const size_t bytes = static_cast<size_t>(stride_a != 0 ? batch : 1) * static_cast<size_t>(M) * sizeof(float);
-    PHEW_CHECK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&w), bytes, st));
+    cudaMemPool_t pool = row_pool();
+    PHEW_REQUIRE(pool != nullptr, "phew_gemm: no memory pool for the row factors");
+    PHEW_CHECK_CUDA(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&w), bytes, pool, st));
     p.row_vec = w;
     int r = in_dtype == PHEW_BF16 ? launch_row_stats<bf16>(A, w, p, lda, stride_a, st)
             : in_dtype == PHEW_F16 ? launch_row_stats<f16>(A, w, p, lda, stride_a, st)
@@ -556,11 +665,7 @@ namespace gemm {
 int gemm_dispatch(const void* A, const void* B, const Params& p, int64_t lda, int64_t ldb, int64_t stride_a,
                   int64_t stride_b, int in_dtype, cudaStream_t st) {
   const int64_t K = p.K, M = p.M, N = p.N, batch = p.batch;
-  const bool aligned16 =
-      ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) == 0 &&
-      (lda * 2) % 16 == 0 && (ldb * 2) % 16 == 0 && (stride_a * 2) % 16 == 0 &&
-      (stride_b * 2) % 16 == 0 && K > 0;
-  if (aligned16 && in_dtype != PHEW_F32) {
+  if (uses_tensor_cores(A, B, lda, ldb, stride_a, stride_b, K, in_dtype)) {
     const bool bf = in_dtype == PHEW_BF16;
     // Tile choice (every kernel is persistent: one CTA per SM looping over
     // tiles, TMA running ahead across tile boundaries):

@@ -133,3 +133,30 @@ def test_normed_matmul_fused(mx, M, K, N):
     bad = np.nonzero(np.abs(implied / r[:, 0] - 1) > 5e-3)[0]
     assert len(bad) == 0, f"rows with a wrong scale: {bad[:20]} ratios {(implied / r[:, 0])[bad[:8]]}"
     check(got, ref.astype(BF16), BF16)
+
+
+def test_normed_matmul_in_a_cuda_graph(mx):
+    """The row-factor pass, its stream-ordered workspace and the dependent
+    GEMM launch are captured into a CUDA graph and replayed; replays on new
+    inputs give the eager results."""
+    import torch
+
+    from phew_b200.ops import normed_matmul
+
+    rng = np.random.default_rng(77)
+    M, K, N = 512, 1024, 768
+    xs = [_rand(rng, (M, K), BF16) for _ in range(2)]
+    w = _rand(rng, (K, N), BF16, 1 / np.sqrt(K))
+    xd, wd = mx.array(xs[0]), mx.array(w)
+    eager = [np.asarray(normed_matmul(mx.array(x), wd, eps=1e-5)).view(np.uint16) for x in xs]
+    normed_matmul(xd, wd, eps=1e-5)  # warm up outside the capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = normed_matmul(xd, wd, eps=1e-5)
+    for x, want in zip(xs, eager):
+        xd._t.copy_(torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).to(xd._t.device))
+        g.replay()
+        torch.cuda.synchronize()
+        assert np.array_equal(np.asarray(out).view(np.uint16), want)
+    del g

@@ -616,6 +616,15 @@ def _row_map_parts(root, chain, ext_specs, ext_arrays, root_spec, key, i):
         return None  # a reduction of a deferred reduction: computed on its own
     tpr, rpb = _row_reduce_plan(root.shape[-1])
     rchain, rext_specs, rext_arrays, rroot_spec, rkey = _fused_dag(src)
+    # One kernel only pays when the chain re-reads a full-size input of the
+    # reduction (x in an RMS or layer norm): then that input crosses HBM once
+    # instead of twice.  With disjoint inputs the separate reduce and chain
+    # kernels move the same bytes, faster.
+    full = tuple(root.shape)
+    shared = {id(x) for x in rext_arrays if tuple(x.shape) == full} & {
+        id(x) for k, x in enumerate(ext_arrays) if k != i and tuple(x.shape) == full}
+    if not shared:
+        return None
     slots: dict = {}
     arrays: list = []
     where: dict = {}

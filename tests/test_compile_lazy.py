@@ -265,3 +265,19 @@ def test_deferred_reduction_materialises_without_deferring_again(core, monkeypat
     # outside tracing nothing is deferred
     core.max(x, axis=-1, keepdims=True)
     assert len(calls) == 2
+
+
+def test_row_map_needs_a_shared_full_size_input(core):
+    """(h @ W) * rsqrt(mean(h1 * h1) + eps): the reduction and the chain read
+    different full-size arrays, so they stay two kernels."""
+    h1 = _arr(core, (4, 64))
+    hw = _arr(core, (4, 64))
+    core.trace_enter()
+    try:
+        m = core.mean(h1 * h1, axis=-1, keepdims=True)
+        y = hw * core.rsqrt(m + 1e-5)
+        chain, ext_specs, ext_arrays, root, key = core._fused_dag(y)
+    finally:
+        core.trace_exit()
+    i = [k for k, a in enumerate(ext_arrays) if a is m][0]
+    assert core._row_map_parts(y, chain, ext_specs, ext_arrays, root, key, i) is None

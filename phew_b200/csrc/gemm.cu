@@ -183,7 +183,10 @@ __device__ __forceinline__ uint32_t pack_out(float lo, float hi, bool bf16) {
   return d;
 }
 
-template <int BN, int MT, int ACC, bool BF16>
+// RS: the row-scale variant (a separate instantiation, so the plain GEMM's
+// epilogue compiles without the factor read: with it in the same body the
+// write-bound QK^T-shaped GEMM ran 50 % slower).
+template <int BN, int MT, int ACC, bool BF16, bool RS>
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const Params p) {
@@ -309,7 +312,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // With the row scale, the factors come from row_stats_kernel, launched
     // just before this kernel as its programmatic-dependency primary: wait
     // (once, before the first epilogue reads them) for it to complete.
-    bool rows_ready = !p.row_scale;
+    bool rows_ready = !RS;
     uint32_t it = 0, out_idx = 0;
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
       int bz, m0, n0;
@@ -330,7 +333,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         uint8_t* my_out = out_stage + (warp - 2) * (2 * 32 * 128);
         for (int h = 0; h < MT; ++h) {
           const int srow = m0 + h * BM + quarter * 32 + lane;
-          const float scale = (p.row_scale && srow < p.M) ? p.row_vec[(p.a_batched ? bz : 0) * p.M + srow] : 1.0f;
+          const float scale = (RS && srow < p.M) ? p.row_vec[(p.a_batched ? bz : 0) * p.M + srow] : 1.0f;
 #pragma unroll 1
           for (int c = 0; c < BN; c += 64, ++out_idx) {
             uint32_t r[64];
@@ -352,11 +355,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
                 float lo = __uint_as_float(r[8 * j + 2 * q]), hi = __uint_as_float(r[8 * j + 2 * q + 1]);
-                if (p.row_scale == 1) {
-                  lo *= scale;
-                  hi *= scale;
-                } else if (p.row_scale == 2) {  // diagnostic: the row's sum of squares
-                  lo = hi = scale;
+                if (RS) {
+                  if (p.row_scale == 1) {
+                    lo *= scale;
+                    hi *= scale;
+                  } else {  // diagnostic: the row's sum of squares
+                    lo = hi = scale;
+                  }
                 }
                 w[q] = pack_out(lo, hi, p.out_dtype == PHEW_BF16);
               }
@@ -375,7 +380,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
       for (int h = 0; h < MT; ++h) {
         const int row = m0 + h * BM + quarter * 32 + lane;
-        const float scale = (p.row_scale && row < p.M) ? p.row_vec[(p.a_batched ? bz : 0) * p.M + row] : 1.0f;
+        const float scale = (RS && row < p.M) ? p.row_vec[(p.a_batched ? bz : 0) * p.M + row] : 1.0f;
         const long long cbase = static_cast<long long>(bz) * p.c_batch_stride + static_cast<long long>(row) * p.ldc;
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
@@ -394,10 +399,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             if (lane == 0) mbar_arrive(&acc_empty[a]);
           }
           if (row < p.M && n0 + c < p.N) {
-            if (p.row_scale == 1) {
+            if (RS && p.row_scale == 1) {
 #pragma unroll
               for (int i = 0; i < 32; ++i) v[i] *= scale;
-            } else if (p.row_scale == 2) {  // diagnostic: the row's sum of squares
+            } else if (RS) {  // diagnostic: the row's sum of squares
 #pragma unroll
               for (int i = 0; i < 32; ++i) v[i] = scale;
             }
@@ -558,7 +563,9 @@ int launch_tc(const void* A, const void* B, const Params& p, long long lda, long
   if (!q.tma_store) tc = ta;  // unused
   static bool attr_set = false;
   if (!attr_set) {
-    PHEW_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, MT, ACC, BF16>,
+    PHEW_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, MT, ACC, BF16, false>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    PHEW_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, MT, ACC, BF16, true>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr_set = true;
   }
@@ -578,10 +585,10 @@ int launch_tc(const void* A, const void* B, const Params& p, long long lda, long
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    PHEW_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, MT, ACC, BF16>, ta, tb, tc, q));
+    PHEW_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, MT, ACC, BF16, true>, ta, tb, tc, q));
     return launch_status("gemm_tc_kernel");
   }
-  gemm_tc_kernel<BN, MT, ACC, BF16><<<grid, kNumThreads, C::SMEM, st>>>(ta, tb, tc, q);
+  gemm_tc_kernel<BN, MT, ACC, BF16, false><<<grid, kNumThreads, C::SMEM, st>>>(ta, tb, tc, q);
   return launch_status("gemm_tc_kernel");
 }
 

@@ -721,7 +721,7 @@ class SubgraphCUDACodegen:
 
     # -- elementwise prologue fused into a row reduction ------------------------
 
-    ROW_STAGE_BYTES = 32 * 1024  # static shared memory for a row map's staged input rows
+    ROW_STAGE_BYTES = 32 * 1024  # static shared memory for a row map's staged input rows (both buffers)
 
     _REDUCE_INIT = {"sum": "0.0f", "mean": "0.0f", "prod": "1.0f",
                     "max": "__int_as_float(0xff800000u)", "min": "__int_as_float(0x7f800000u)"}
@@ -780,7 +780,7 @@ class SubgraphCUDACodegen:
 
     def _row_reduce_lines(self, plan, ext_in, names, in_dts, classes, out_shape, op: str,
                           rows_expr: str, it: str, u: str, staged: dict | None = None,
-                          after_header=()) -> list[str]:
+                          after_header=(), header: bool = True) -> list[str]:
         """Rows of `out_shape[-1]` elements of `plan`'s single output, reduced
         with ``op`` into ``phew_acc`` (valid in every thread of the row after
         the code): `blockDim.x` threads per row, thread t accumulating
@@ -821,6 +821,8 @@ class SubgraphCUDACodegen:
             f"const {it} phew_rows = {rows_expr};",
             f"const {it} phew_row = ({it})blockIdx.x * blockDim.y + threadIdx.y;",
             "const bool phew_active = phew_row < phew_rows;",
+        ] if header else []
+        L += [
             *after_header,
             f"float phew_acc = {self._REDUCE_INIT[op]};",
             "if (phew_active) {",
@@ -878,8 +880,9 @@ class SubgraphCUDACodegen:
         reduction and then the chain.
 
         `slots` maps the id of every external spec of both DAGs except
-        `row_value` to its kernel input index.  Launch: block (tpr, rpb), one
-        block per `rpb` rows.  Raises ``ValueError`` when it cannot."""
+        `row_value` to its kernel input index.  Launch: block (tpr, rpb), any
+        number of blocks (each walks groups of `rpb` rows with a grid
+        stride).  Raises ``ValueError`` when it cannot."""
         out_shape = tuple(int(x) for x in map_root.shape)
         if not out_shape or op not in self._REDUCE_INIT:
             raise ValueError("cuda_codegen: not a row map")
@@ -944,61 +947,91 @@ class SubgraphCUDACodegen:
         vec_ok = red % V == 0 and all(c in ("full", "scalar") or ext % V == 0 for c, ext in m_classes)
         packed = vec_ok and half_t is not None and V == 8
 
-        # Rows of the full-size inputs are staged in shared memory with
-        # 16-byte loads: the reduction then reads them in its (fixed, strided)
-        # order and the chain reads them again, with one pass over HBM.
+        # Rows of the full-size inputs are staged in shared memory, double
+        # buffered: each block walks row groups (rpb rows) with a grid
+        # stride and copies the next group's rows in with cp.async while it
+        # reduces and maps the current one, so loads stay in flight through
+        # the whole kernel.  The reduction reads the staged rows in its
+        # fixed (strided) order, the chain reads them again: one HBM pass.
         full = [k for k in range(n_in) if classes[k][0] == "full"]
-        stage_bytes = rpb * red * sum(ITEMSIZE[in_dt[k]] for k in full)
+        stage_bytes = 2 * rpb * red * sum(ITEMSIZE[in_dt[k]] for k in full)
         staged = ({names[k]: f"phew_stg{k}" for k in full}
                   if full and stage_bytes <= self.ROW_STAGE_BYTES else {})
-        stage_lines: list[str] = []
-        if staged:
-            stage_lines.append(f"const {it} phew_lrow = ({it})threadIdx.y * phew_red;")
-            stage_lines.append("if (phew_active) {")
-            for k in full:
-                ct, isz = CTYPE[in_dt[k]], ITEMSIZE[in_dt[k]]
-                E = 16 // isz
-                stage_lines.append("  {")
-                stage_lines.append(f"    const {ct}* phew_src = {names[k]} + phew_row * phew_red;")
-                if (red * isz) % 16 == 0:
-                    stage_lines += [
-                        "    if ((reinterpret_cast<phew_uptr>(phew_src) & 15u) == 0u) {",
-                        f"      for ({it} phew_q = threadIdx.x; phew_q < {red // E}{u}; phew_q += blockDim.x)",
-                        f"        *reinterpret_cast<phew_vec<{ct}, {E}>*>(phew_stg{k} + phew_lrow + phew_q * {E}{u}) =",
-                        f"            phew_ldv<{ct}, {E}>(phew_src + phew_q * {E}{u});",
-                        "    } else {",
-                    ]
-                else:
-                    stage_lines.append("    {")
-                stage_lines += [
-                    f"      for ({it} phew_c = threadIdx.x; phew_c < phew_red; phew_c += blockDim.x)",
-                    f"        phew_stg{k}[phew_lrow + phew_c] = phew_src[phew_c];",
-                    "    }",
-                    "  }",
-                ]
-            stage_lines.append("}")
-            stage_lines.append("__syncthreads();")
+        buf = rpb * red  # elements per buffer of one staged input
 
         L: list[str] = []
         L.append(f"// {op} over rows of {red} ({len(rplan.compute_nodes)}-op prologue), broadcast into "
-                 f"a {len(mplan.compute_nodes)}-op chain over the same rows")
+                 f"a {len(mplan.compute_nodes)}-op chain over the same rows; persistent row groups")
         L.append(io_contract_line(classes, out_shape, in_shape, it) + f" rowlen={red}")
         L += rplan.constant_lines(packed_type=None)
         L += mplan.constant_lines(packed_type=half_t if packed else None)
         L.append("__shared__ float phew_smem[32 * 32];")
         L.append(f"__shared__ {CTYPE[red_dt]} phew_rowv_s[32];")
         for k in (full if staged else []):
-            L.append(f"__shared__ __align__(16) {CTYPE[in_dt[k]]} phew_stg{k}[{rpb * red}];")
-        L += self._row_reduce_lines(rplan, reduce_ext, r_names, r_dts, r_classes, out_shape, op,
-                                    f"({it})out0_size / {red}{u}", it, u, staged=staged,
-                                    after_header=stage_lines)
+            L.append(f"__shared__ __align__(16) {CTYPE[in_dt[k]]} phew_stg{k}[{2 * buf}];")
         L += [
+            f"const {it} phew_red = {red}{u};",
+            f"const {it} phew_rows = ({it})out0_size / {red}{u};",
+            f"const {it} phew_groups = (phew_rows + blockDim.y - 1) / blockDim.y;",
+            f"const {it} phew_lrow0 = ({it})threadIdx.y * phew_red;",
+        ]
+        if staged:
+            L.append(f"auto phew_stage = [&]({it} phew_gs, int phew_bs) {{")
+            L.append(f"  const {it} phew_rs = phew_gs * blockDim.y + threadIdx.y;")
+            L.append("  if (phew_rs >= phew_rows) return;")
+            for k in full:
+                ct, isz = CTYPE[in_dt[k]], ITEMSIZE[in_dt[k]]
+                E = 16 // isz
+                L.append("  {")
+                L.append(f"    const {ct}* phew_src = {names[k]} + phew_rs * phew_red;")
+                L.append(f"    {ct}* phew_dst = phew_stg{k} + ({it})phew_bs * {buf}{u} + phew_lrow0;")
+                if (red * isz) % 16 == 0:
+                    L += [
+                        "    if ((reinterpret_cast<phew_uptr>(phew_src) & 15u) == 0u) {",
+                        f"      for ({it} phew_q = threadIdx.x; phew_q < {red // E}{u}; phew_q += blockDim.x)",
+                        f"        phew_cp_async16(phew_dst + phew_q * {E}{u}, phew_src + phew_q * {E}{u});",
+                        "    } else {",
+                    ]
+                else:
+                    L.append("    {")
+                L += [
+                    f"      for ({it} phew_c = threadIdx.x; phew_c < phew_red; phew_c += blockDim.x)",
+                    "        phew_dst[phew_c] = phew_src[phew_c];",
+                    "    }",
+                    "  }",
+                ]
+            L.append("};")
+        L += [
+            f"{it} phew_g = blockIdx.x;",
+            "int phew_buf = 0;",
+        ]
+        if staged:
+            L += ["if (phew_g < phew_groups) phew_stage(phew_g, 0);", "phew_cp_commit();"]
+        L.append("for (; phew_g < phew_groups; phew_g += gridDim.x, phew_buf ^= 1) {")
+        body_lines: list[str] = []
+        if staged:
+            body_lines += [
+                "if (phew_g + gridDim.x < phew_groups) phew_stage(phew_g + gridDim.x, phew_buf ^ 1);",
+                "phew_cp_commit();",
+                "phew_cp_wait1();  // this group's rows have landed (the next group's may be in flight)",
+                "__syncthreads();",
+            ]
+        body_lines += [
+            f"const {it} phew_row = phew_g * blockDim.y + threadIdx.y;",
+            "const bool phew_active = phew_row < phew_rows;",
+            f"const {it} phew_lrow = phew_lrow0 + ({it})phew_buf * {buf}{u};",
+        ]
+        body_lines += self._row_reduce_lines(rplan, reduce_ext, r_names, r_dts, r_classes, out_shape, op,
+                                             "", it, u, staged=staged, header=False)
+        body_lines += [
             "if (threadIdx.x == 0) {",
             ("  phew_acc = __fdiv_rn(phew_acc, (float)phew_red);" if op == "mean" else ""),
             f"  phew_rowv_s[threadIdx.y] = phew_st_{_suffix(red_dt)}(phew_acc);",
             "}",
             "__syncthreads();",
-            "if (!phew_active) return;",
+            "if (phew_active) {",
+        ]
+        inner: list[str] = [
             f"const {CTYPE[red_dt]} phew_rowv[1] = {{phew_rowv_s[threadIdx.y]}};",
             f"const {it} phew_base = phew_row * phew_red;",
         ]
@@ -1007,23 +1040,32 @@ class SubgraphCUDACodegen:
         if vec_ok:
             ptrs = " | ".join(f"reinterpret_cast<phew_uptr>({nm})" for nm in names + ["out0"]
                               if nm not in staged)
-            body = self._vector_body(mplan, map_ext, m_names, ["out0"], m_dts, [out_dt], m_classes,
-                                     out_shape, V, it, u, half_t, staged=staged)
-            L.append(f"if ((({ptrs}) & 15u) == 0u) {{")
-            L.append(f"  for ({it} phew_v = threadIdx.x; phew_v < phew_red / {V}{u}; phew_v += blockDim.x) {{")
-            L.append(f"    const {it} phew_off = phew_v * {V}{u};")
-            L.append(f"    const {it} elem = phew_base + phew_off;")
-            L += ["    " + b for b in body]
-            L.append("  }")
-            L.append("} else {")
+            vbody = self._vector_body(mplan, map_ext, m_names, ["out0"], m_dts, [out_dt], m_classes,
+                                      out_shape, V, it, u, half_t, staged=staged)
+            inner.append(f"if ((({ptrs}) & 15u) == 0u) {{")
+            inner.append(f"  for ({it} phew_v = threadIdx.x; phew_v < phew_red / {V}{u}; phew_v += blockDim.x) {{")
+            inner.append(f"    const {it} phew_off = phew_v * {V}{u};")
+            inner.append(f"    const {it} elem = phew_base + phew_off;")
+            inner += ["    " + b for b in vbody]
+            inner.append("  }")
+            inner.append("} else {")
         else:
-            L.append("{")
-        L.append(f"  for ({it} phew_c = threadIdx.x; phew_c < phew_red; phew_c += blockDim.x) {{")
-        L.append(f"    const {it} phew_off = phew_c;")
-        L.append(f"    const {it} elem = phew_base + phew_c;")
-        L += ["    " + b for b in scalar]
-        L.append("  }")
+            inner.append("{")
+        inner.append(f"  for ({it} phew_c = threadIdx.x; phew_c < phew_red; phew_c += blockDim.x) {{")
+        inner.append(f"    const {it} phew_off = phew_c;")
+        inner.append(f"    const {it} elem = phew_base + phew_c;")
+        inner += ["    " + b for b in scalar]
+        inner.append("  }")
+        inner.append("}")
+        body_lines += ["  " + b for b in inner]
+        body_lines += [
+            "}",
+            "__syncthreads();  // the buffer is refilled two groups from now",
+        ]
+        L += ["  " + b for b in body_lines]
         L.append("}")
+        if staged:
+            L.append("phew_cp_wait0();")
         source = "\n".join(f"    {line}" if line else "" for line in L)
         return source, names, ["out0"]
 

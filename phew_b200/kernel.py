@@ -113,6 +113,16 @@ __device__ __forceinline__ phew_vec<T, V> phew_ldv(const T* p) {
   return r;
 }
 
+// Asynchronous 16-byte global -> shared copies (cp.async): issue, close the
+// group, wait until at most N groups are still in flight.
+__device__ __forceinline__ void phew_cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+               :: "r"((unsigned)__cvta_generic_to_shared(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void phew_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void phew_cp_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void phew_cp_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // A vector from shared (or any generic) memory, 16-byte aligned.
 template <typename T, int V>
 __device__ __forceinline__ phew_vec<T, V> phew_ldv_s(const T* p) {

@@ -665,7 +665,9 @@ def _fused_row_map(root, chain, ext_specs, ext_arrays, root_spec, key, i) -> boo
     if kern is False:
         return False
     tpr, rpb = args[-2], args[-1]
-    blocks = -(-(root.size // root.shape[-1]) // rpb)
+    # persistent row groups: enough blocks to fill the SMs, each walking
+    # groups of rpb rows with a grid stride
+    blocks = builtins_min(-(-(root.size // root.shape[-1]) // rpb), sm_count() * 8)
     out = kern(inputs=[asarray_device(x) for x in arrays], output_shapes=[root._shape],
                output_dtypes=[root._dtype], grid=(blocks * tpr, rpb, 1), threadgroup=(tpr, rpb, 1))
     object.__setattr__(root, "_mt", out[0]._t)

@@ -356,8 +356,6 @@ class NormedMatmul:
     kernel_regex = "gemm_tc"
     profile = "gemm_tc_normed_matmul_bf16_8192x4096x4096"
 
-    launches_per_step = 2  # row statistic pass + GEMM
-
     def describe(self):
         return (f"normed matmul (x @ W) * rsqrt(mean(x*x,-1)+1e-5), bf16 x ({self.M},{self.K}), "
                 f"W ({self.K},{self.N}); a row-statistic pass over x, then one tcgen05 GEMM "
@@ -506,10 +504,14 @@ def run_phew(args) -> None:
     # The K timed launches are captured once into a CUDA graph, so the timed
     # region measures the device and not the Python host path (which the e2e
     # number below includes).
+    from phew_b200 import _native
+
     graph = torch.cuda.CUDAGraph()
+    n0 = _native.launch_count()
     with torch.cuda.graph(graph):
         for i in range(args.steps):
             w.launch(i)
+    graph_launches = _native.launch_count() - n0  # the kernels the timed replay runs
     graph.replay()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -574,7 +576,7 @@ def run_phew(args) -> None:
                      "peak_source": peaks["source"] + (" (burst)" if w.bound == "tensor" else "")},
         "e2e": {"value": e2e_val, "unit": w.unit, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps},
-        "gpu_launches": args.steps * getattr(w, "launches_per_step", 1),
+        "gpu_launches": graph_launches,
         "clocks": clk.summary(),
     }
     line.update(w.extras(mx))
@@ -635,7 +637,7 @@ def _exception_kinds(verdicts) -> dict:
 def run_sweep(args) -> None:
     import torch
 
-    from phew_b200 import mx, sweep
+    from phew_b200 import _native, mx, sweep
     from phew_b200.ops import check_device_errors
     from phew_b200.workloads import DECODER_FULL, DECODER_SEQ, DECODER_TINY, DECODER_TINY_SEQ, decoder_block_fn
 
@@ -675,12 +677,14 @@ def run_sweep(args) -> None:
         d.barrier()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
+        n0 = _native.launch_count()
         e0.record()
         recs = sweep.run_groups(groups, names, ev, store, d.rank, journal=journal,
                                 run_id=f"sweep/{jdir.name}")
         e1.record()
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
+        launches = _native.launch_count() - n0
         d.barrier()
     check_device_errors()
     dev_s = e0.elapsed_time(e1) / 1e3
@@ -708,7 +712,7 @@ def run_sweep(args) -> None:
             # would be a backend fault, not a verdict)
             "exception_units": _exception_kinds(verdicts),
             "clocks": clk.summary(), "journal": str(jdir),
-            "gpu_launches": None,
+            "gpu_launches": launches,  # rank 0's; every rank launches its own groups' kernels
         }
         print(json.dumps(line), flush=True)
     _ = recs

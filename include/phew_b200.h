@@ -98,6 +98,11 @@ int phew_launch(uint64_t handle, void** args, int nargs,
                 unsigned block_x, unsigned block_y, unsigned block_z,
                 size_t dynamic_smem, void* stream);
 
+/* Number of kernels this library has launched in this process (its own
+ * kernels and phew_launch'ed ones; launches recorded into a CUDA graph count
+ * once, when captured).  A harness reads it around a timed region. */
+int phew_launch_count(uint64_t* out);
+
 /* Number of kernels currently held in the compile cache. */
 int phew_compile_cache_size(void);
 

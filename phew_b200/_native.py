@@ -35,6 +35,7 @@ EXPORTED_SYMBOLS = (
     "phew_device_query",
     "phew_compile",
     "phew_launch",
+    "phew_launch_count",
     "phew_compile_cache_size",
     "phew_rms_norm",
     "phew_layer_norm",
@@ -115,6 +116,7 @@ _SIGNATURES = {
         + [ctypes.c_size_t, _vp],
         _int,
     ),
+    "phew_launch_count": ([ctypes.POINTER(ctypes.c_uint64)], _int),
     "phew_compile_cache_size": ([], _int),
     "phew_rms_norm": ([_vp, _vp, _vp, _i64, _i64, ctypes.c_float, _int, _vp], _int),
     "phew_layer_norm": ([_vp, _vp, _vp, _vp, _i64, _i64, ctypes.c_float, _int, _vp], _int),
@@ -204,3 +206,11 @@ def call(name: str, *args):
     """Call a status-returning entry point and raise on failure."""
     lib = load()
     check(getattr(lib, name)(*args), name)
+
+
+def launch_count() -> int:
+    """Kernels the native library has launched in this process (graph
+    captures count the launches they record)."""
+    n = ctypes.c_uint64(0)
+    call("phew_launch_count", ctypes.byref(n))
+    return int(n.value)

@@ -30,9 +30,15 @@ inline int cuda_status(cudaError_t e, const char* what) {
     if (!(cond)) return ::phew::set_error(PHEW_ERR_INVALID, msg); \
   } while (0)
 
-// Launch-error check used right after every <<<>>> launch.
+// Count of kernels this library launched (phew_launch_count).
+void count_launch();
+unsigned long long launch_counter();
+
+// Launch-error check used right after every <<<>>> launch; counts the launch.
 inline int launch_status(const char* what) {
-  return cuda_status(cudaGetLastError(), what);
+  const int s = cuda_status(cudaGetLastError(), what);
+  if (s == PHEW_OK) count_launch();
+  return s;
 }
 
 inline int dtype_bytes(int dtype) {

@@ -2,6 +2,7 @@
 // stands in for MLX's metal_kernel JIT, kernel launch and the L2 flush.
 #include <nvrtc.h>
 
+#include <atomic>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -18,6 +19,13 @@ int set_error(int code, const std::string& msg) {
   g_last_error = msg;
   return code;
 }
+
+namespace {
+std::atomic<unsigned long long> g_launches{0};
+}  // namespace
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+unsigned long long launch_counter() { return g_launches.load(std::memory_order_relaxed); }
 
 int sm_count_current() {
   static thread_local int cached_dev = -1;
@@ -186,6 +194,13 @@ int phew_launch(uint64_t handle, void** args, int nargs, unsigned grid_x, unsign
   PHEW_CHECK_CUDA(cudaLaunchKernel(fn, dim3(grid_x, grid_y, grid_z),
                                    dim3(block_x, block_y, block_z), args, dynamic_smem,
                                    static_cast<cudaStream_t>(stream)));
+  phew::count_launch();
+  return PHEW_OK;
+}
+
+int phew_launch_count(uint64_t* out) {
+  PHEW_REQUIRE(out != nullptr, "phew_launch_count: null output");
+  *out = phew::launch_counter();
   return PHEW_OK;
 }
 

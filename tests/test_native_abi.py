@@ -90,3 +90,10 @@ def test_mx_namespace_covers_the_reference_tracer():
     reg = json.loads((Path(__file__).parent / "golden" / "op_registry.json").read_text())
     assert [o for o in reg["IMPLEMENTED"] if not hasattr(mx, o)] == []
     assert [o for o in reg["FAST_IMPLEMENTED"] if not hasattr(mx.fast, o)] == []
+
+
+def test_launch_count_is_readable_without_a_device():
+    from phew_b200 import _native
+
+    n = _native.launch_count()
+    assert isinstance(n, int) and n >= 0

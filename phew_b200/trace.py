@@ -158,7 +158,7 @@ def profile(fn: Callable, *args: Any, warmup: int = 2, **kwargs: Any):
     return P(kernels=stats, total_ms=sum(k.duration_ms for k in stats), device_info=device_info())
 
 
-def ncu_command(cmd: str, out_csv: str = "gpurun_out/metrics.csv", kernel_regex: str | None = None,
+def ncu_command(cmd: str, out_csv: str = "ncu_metrics.csv", kernel_regex: str | None = None,
                 launch_count: int | None = None) -> str:
     """The Nsight Compute command whose CSV ``from_ncu_csv`` reads (clocks
     left alone: ``--clock-control none``)."""

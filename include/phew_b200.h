@@ -187,9 +187,10 @@ int phew_l2_flush(void* buf, size_t bytes, void* stream);
  *   row_scale = 1 multiplies row m of the product by
  *   rsqrt(mean_k(A[m, k]^2) + eps) (the normed matmul
  *   (x @ W) * rsqrt(mean(x^2) + eps)): one pass over A computes the factor per
- *   row into stream-ordered memory (cudaMallocAsync / cudaFreeAsync on
- *   `stream`, so graph capture works), and the GEMM's epilogue applies it to
- *   the fp32 accumulator.
+ *   row into stream-ordered memory (cudaMallocFromPoolAsync / cudaFreeAsync
+ *   on `stream`, from a pool the library keeps per device, so graph capture
+ *   records it), and the GEMM, launched as that pass's programmatic
+ *   dependent, applies it to the fp32 accumulator in its epilogue.
  *   row_scale = 2 writes each row's sum of squares of A instead of the
  *   product (a diagnostic of the row statistic).
  *   error_flag (device int, may be NULL) receives PHEW_ERR_TIMEOUT if a

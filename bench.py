@@ -17,7 +17,8 @@ Printed (one JSON line, rank 0):
               inputs resident in HBM and rotated so no step finds its inputs in
               the 126 MB L2
   e2e         the same metric through the public API with pinned host
-              buffers: H2D of the inputs and D2H of the output inside every step
+              buffers: H2D of the inputs and D2H of the output inside every
+              step (step i+1's H2D overlapping step i's compute and D2H)
   roofline    achieved vs the measured HBM copy bandwidth / cuBLAS bf16 peak
   cpu_baseline  the oracle (numpy restatement of the MLX-CPU evaluation)
               timed on a bounded sample on the host
@@ -530,31 +531,63 @@ def run_phew(args) -> None:
     value = work * args.steps * d.world / (max_ms / 1e3) / scale
     achieved = work / (local_ms / args.steps / 1e3) / scale
 
-    # e2e through the public API with pinned host buffers
+    # e2e through the public API with pinned host buffers.  Every step
+    # copies its inputs host -> device, runs the API call and copies the
+    # result device -> host, all inside the timed region; as a streaming
+    # caller would, step i + 1's host -> device copy runs on its own stream
+    # while step i computes and copies its result back on a third one
+    # (inputs double-buffered on the device, events order each buffer's
+    # reuse after the compute that read it).
     pinned_in = [torch.from_numpy(np.ascontiguousarray(h.view(np.int16) if h.dtype.itemsize == 2 and h.dtype.kind == "V" else h)).pin_memory()
                  for h in host]
-    dev_in = [torch.empty(p.shape, dtype=a._t.dtype, device=dev) for p, a in zip(pinned_in, w.sets[0])]
+    dev_in = [[torch.empty(p.shape, dtype=a._t.dtype, device=dev) for p, a in zip(pinned_in, w.sets[0])]
+              for _ in range(2)]
     out0 = w.api(w.sets[0])
-    pinned_out = torch.empty(out0._t.shape, dtype=out0._t.dtype).pin_memory()
+    pinned_out = [torch.empty(out0._t.shape, dtype=out0._t.dtype).pin_memory() for _ in range(2)]
     h2d = sum(p.numel() * p.element_size() for p in pinned_in)
-    d2h = pinned_out.numel() * pinned_out.element_size()
+    d2h = pinned_out[0].numel() * pinned_out[0].element_size()
+    s_h2d = torch.cuda.Stream(device=dev)
+    s_d2h = torch.cuda.Stream(device=dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]    # buffer b's inputs have landed
+    ev_used = [torch.cuda.Event() for _ in range(2)]  # the compute that read buffer b is done
+    used = [False, False]
 
-    def e2e_step():
-        for dst, srcp in zip(dev_in, pinned_in):
-            dst.view(srcp.dtype).copy_(srcp, non_blocking=True)
-        z = w.api([mx.array(t) for t in dev_in])
-        pinned_out.copy_(z._t, non_blocking=True)
+    def e2e_step(i):
+        b = i % 2
+        with torch.cuda.stream(s_h2d):
+            if used[b]:
+                s_h2d.wait_event(ev_used[b])
+            for dst, srcp in zip(dev_in[b], pinned_in):
+                dst.view(srcp.dtype).copy_(srcp, non_blocking=True)
+            ev_in[b].record(s_h2d)
+        stream.wait_event(ev_in[b])
+        z = w.api([mx.array(t) for t in dev_in[b]])
+        ev_used[b].record(stream)
+        used[b] = True
+        with torch.cuda.stream(s_d2h):
+            s_d2h.wait_event(ev_used[b])
+            z._t.record_stream(s_d2h)
+            pinned_out[b].copy_(z._t, non_blocking=True)
 
-    for _ in range(2):
-        e2e_step()
+    def join_copies():
+        for st in (s_h2d, s_d2h):
+            e = torch.cuda.Event()
+            e.record(st)
+            stream.wait_event(e)
+
+    for i in range(2):
+        e2e_step(i)
+    join_copies()
     torch.cuda.synchronize()
     e2e_steps = max(3, min(args.steps, 20))
     d.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
+    s_h2d.wait_event(e0)
+    for i in range(e2e_steps):
+        e2e_step(i)
+    join_copies()
     e1.record(stream)
     torch.cuda.synchronize()
     d.barrier()
@@ -575,7 +608,9 @@ def run_phew(args) -> None:
                      "frac": achieved / peak, "traffic": load_traffic(getattr(w, "profile", None)),
                      "peak_source": peaks["source"] + (" (burst)" if w.bound == "tensor" else "")},
         "e2e": {"value": e2e_val, "unit": w.unit, "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                "copies": "every step's H2D and D2H inside the timed region; step i+1's H2D "
+                          "overlaps step i's compute and D2H (separate streams)"},
         "gpu_launches": graph_launches,
         "clocks": clk.summary(),
     }

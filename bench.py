@@ -194,6 +194,18 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 
 
+def _opt_over_baseline(api, baseline_fn, opt_args, base_args) -> dict:
+    """optimized_ms / baseline_ms: the substituted call (the optimizer's
+    output) against the harness function evaluated op by op on this backend,
+    both timed by phew_b200.bench (CUDA events, cold L2)."""
+    from phew_b200.bench import benchmark
+
+    opt = benchmark(lambda *a: api(list(a)), *opt_args, n_warmup=3, n_bench=10, max_n_bench=30)
+    basel = benchmark(baseline_fn, *base_args, n_warmup=2, n_bench=5, max_n_bench=15)
+    return {"optimized_ms": opt.mean_ms, "baseline_ms": basel.mean_ms,
+            "optimized_over_baseline": opt.mean_ms / basel.mean_ms}
+
+
 class GeluChain:
     """Fused elementwise chain, fp16 (4096, 8192): HBM-bound."""
 
@@ -329,7 +341,10 @@ class Attention:
         self.api(self.sets[i % 2])
 
     def extras(self, mx):
-        return {}
+        from phew_b200.workloads import attention_fn, causal_mask
+
+        mask = mx.array(causal_mask(self.L))
+        return _opt_over_baseline(self.api, attention_fn(mx), self.sets[0], self.sets[0] + [mask])
 
     def cpu_sample(self, threads: int):
         import numpy as np
@@ -384,7 +399,9 @@ class NormedMatmul:
         self.api(self.sets[i % 3])
 
     def extras(self, mx):
-        return {}
+        from phew_b200.workloads import normed_matmul_fn
+
+        return _opt_over_baseline(self.api, normed_matmul_fn(mx), self.sets[0], self.sets[0])
 
     def cpu_sample(self, threads: int, rows: int = 1024):
         import numpy as np
@@ -433,7 +450,9 @@ class RmsNorm:
         self.api(self.sets[i % self.R])
 
     def extras(self, mx):
-        return {}
+        from phew_b200.workloads import rms_norm_fn
+
+        return _opt_over_baseline(self.api, rms_norm_fn(mx), self.sets[0], self.sets[0])
 
     def cpu_sample(self, threads: int):
         from oracle import mlx_cpu

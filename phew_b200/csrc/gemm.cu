@@ -12,7 +12,8 @@
 // [N, K] (K contiguous: a K-major operand, `b_layout = 1`, e.g. k.T in q @ k.T).
 // Batches are strided; a zero batch stride broadcasts the operand.
 //
-// Tiles are (MT x 128) x BN (BN = 128 or 256, MT = 1 or 2).  The kernel is
+// Tiles are (MT x 128) x BN (BN = 128 or 256, MT = 1 or 2; with MT = 2 the
+// last, partial round of tiles runs as 128-row half tiles).  The kernel is
 // persistent: at most one CTA per SM, each walking the tiles t = blockIdx.x,
 // blockIdx.x + gridDim.x, ... with ACC (1 or 2) accumulators in TMEM, so the
 // epilogue of one tile overlaps the main loop of the next when ACC = 2, and
@@ -214,6 +215,27 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     m0 = (r % n_mb) * C::ROWS;
     bz = r / n_mb;
   };
+  // Wave quantization: with two 128-row halves per tile (MT = 2), the last,
+  // partial round of tiles runs as twice as many 128-row half tiles when they
+  // fit in one round, so that round takes half as long.  Work item w -> tile
+  // coordinates and the number of 128-row halves it covers (mt); every role
+  // walks the same items.
+  const int rem = num_tiles % static_cast<int>(gridDim.x);
+  const bool split = MT == 2 && num_tiles > static_cast<int>(gridDim.x) && rem > 0 &&
+                     2 * rem <= static_cast<int>(gridDim.x);
+  const int first_half = split ? num_tiles - rem : num_tiles;
+  const int num_work = split ? num_tiles + rem : num_tiles;
+  auto work = [&](int w, int& bz, int& m0, int& n0, int& mt) {
+    if (w < first_half) {
+      coords(w, bz, m0, n0);
+      mt = MT;
+      return;
+    }
+    const int u = w - first_half;
+    coords(first_half + u / 2, bz, m0, n0);
+    m0 += (u & 1) * BM;
+    mt = 1;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -239,9 +261,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // ---------------- TMA producer: runs ahead across tiles ----------------
     if (lane == 0) {
       uint32_t kg = 0;  // k-blocks issued so far (ring position)
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        int bz, m0, n0;
-        coords(t, bz, m0, n0);
+      for (int t = blockIdx.x; t < num_work && ok; t += gridDim.x) {
+        int bz, m0, n0, mt;
+        work(t, bz, m0, n0, mt);  // a half tile loads the full box from its own first row
         const int ba = p.a_batched ? bz : 0;
         const int bb = p.b_batched ? bz : 0;
         for (int kb = 0; kb < num_kb; ++kb, ++kg) {
@@ -271,7 +293,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       constexpr uint32_t idesc = instr_desc_f16(BF16 ? 1 : 0, 0, BM, BN);
       const uint32_t idesc_b = p.b_mn_major ? instr_desc_f16(BF16 ? 1 : 0, 1, BM, BN) : idesc;
       uint32_t kg = 0, it = 0;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+      for (int t = blockIdx.x; t < num_work && ok; t += gridDim.x, ++it) {
+        int bz, m0, n0, mt;
+        work(t, bz, m0, n0, mt);
         const int a = it % ACC;
         // accumulator a is free once the epilogue has read the tile before
         if (!mbar_wait(&acc_empty[a], ((it / ACC) & 1) ^ 1, p.error_flag)) {
@@ -296,6 +320,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                                              : smem_desc(sb + kk * 32, 16, 1024);
 #pragma unroll
             for (int h = 0; h < MT; ++h) {
+              if (h >= mt) break;
               // rows h*128.. of the A tile start h*128*128 bytes in (1024-aligned)
               const uint64_t ad = smem_desc(sa + h * (BM * 128) + kk * 32, 16, 1024);
               mma_ss(acc + h * BN, ad, bd, idesc_b, (kb > 0 || kk > 0) ? 1u : 0u);
@@ -314,9 +339,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // (once, before the first epilogue reads them) for it to complete.
     bool rows_ready = !RS;
     uint32_t it = 0, out_idx = 0;
-    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
-      int bz, m0, n0;
-      coords(t, bz, m0, n0);
+    for (int t = blockIdx.x; t < num_work && ok; t += gridDim.x, ++it) {
+      int bz, m0, n0, mt;
+      work(t, bz, m0, n0, mt);
       const int a = it % ACC;
       if (ok && !mbar_wait(&acc_full[a], (it / ACC) & 1, p.error_flag)) ok = false;
       if (!ok) break;
@@ -331,7 +356,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         // staging box (128B-swizzled, so the 8 lanes of a store phase hit
         // distinct banks) -> one TMA store of the box, double-buffered.
         uint8_t* my_out = out_stage + (warp - 2) * (2 * 32 * 128);
-        for (int h = 0; h < MT; ++h) {
+        for (int h = 0; h < mt; ++h) {
           const int srow = m0 + h * BM + quarter * 32 + lane;
           const float scale = (RS && srow < p.M) ? p.row_vec[(p.a_batched ? bz : 0) * p.M + srow] : 1.0f;
 #pragma unroll 1
@@ -340,7 +365,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             tmem_ld32(acc + h * BN + c, r);
             tmem_ld32(acc + h * BN + c + 32, r + 32);
             tmem_ld_wait();
-            if (h == MT - 1 && c + 64 == BN) {
+            if (h == mt - 1 && c + 64 == BN) {
               // last read of this accumulator: hand it back to the MMA warp
               asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
               __syncwarp();
@@ -378,7 +403,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         continue;
       }
-      for (int h = 0; h < MT; ++h) {
+      for (int h = 0; h < mt; ++h) {
         const int row = m0 + h * BM + quarter * 32 + lane;
         const float scale = (RS && row < p.M) ? p.row_vec[(p.a_batched ? bz : 0) * p.M + row] : 1.0f;
         const long long cbase = static_cast<long long>(bz) * p.c_batch_stride + static_cast<long long>(row) * p.ldc;
@@ -392,7 +417,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
           }
-          if (h == MT - 1 && c + 32 == BN) {
+          if (h == mt - 1 && c + 32 == BN) {
             // last read of this accumulator: hand it back to the MMA warp
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();

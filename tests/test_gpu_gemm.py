@@ -160,3 +160,36 @@ def test_normed_matmul_in_a_cuda_graph(mx):
         torch.cuda.synchronize()
         assert np.array_equal(np.asarray(out).view(np.uint16), want)
     del g
+
+
+@pytest.mark.parametrize("M,N,K,batch", [(8192, 4096, 1024, 1), (8192 - 64, 4096, 640, 1), (4096, 4096, 1024, 2)])
+def test_gemm_last_round_as_half_tiles(mx, M, N, K, batch):
+    """Shapes with 512 tiles of 256 rows on a 148-SM B200: the last, partial
+    round runs as 128-row half tiles (a partial last row block and a batched
+    case included); every output row must still be computed once."""
+    import torch
+
+    g = torch.Generator(device="cuda").manual_seed(M + K)
+    a = torch.randn(batch, M, K, device="cuda", dtype=torch.bfloat16, generator=g)
+    b = (torch.randn(batch, K, N, device="cuda", dtype=torch.bfloat16, generator=g) / K ** 0.5)
+    got = (mx.array(a) @ mx.array(b))._t.float()
+    want = a.float() @ b.float()
+    err = ((got - want).abs().amax(dim=-1) / want.abs().amax(dim=-1)).max().item()
+    assert err < 1e-2, err
+    # rows of the half tiles at the end were written (no stale rows)
+    assert torch.isfinite(got).all()
+
+
+def test_normed_matmul_last_round_as_half_tiles(mx):
+    from phew_b200.ops import normed_matmul
+
+    rng = np.random.default_rng(91)
+    M, K, N = 8192, 1024, 4096
+    x = _rand(rng, (M, K), BF16)
+    w = _rand(rng, (K, N), BF16, 1 / np.sqrt(K))
+    got = np.asarray(normed_matmul(mx.array(x), mx.array(w), eps=1e-5)).astype(np.float32)
+    xf = x.astype(np.float32)
+    r = 1.0 / np.sqrt(np.mean(xf.astype(np.float64) ** 2, -1, keepdims=True) + 1e-5)
+    want = (xf @ w.astype(np.float32)) * r
+    err = np.max(np.abs(got - want).max(-1) / np.abs(want).max(-1))
+    assert err < 1e-2, err

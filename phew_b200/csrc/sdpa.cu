@@ -15,8 +15,9 @@
 // released as soon as both S products that read it are done, a value tile
 // after both P V products, so the next loads start early.
 //
-//   warp 0      TMA: Q_a, Q_b once, then K_j and V_j (128B-swizzled, each CTA
-//               loading its own tiles)
+//   warp 0      TMA: Q_a and K_0 first (all that S_a(0) needs), then Q_b,
+//               then K_j and V_j (128B-swizzled, each CTA loading its own
+//               tiles); Q_a and Q_b land on separate barriers
 //   warp 1      TMEM owner + MMA issuer.  Per key tile j and query tile t:
 //                 O_t += P_t V_j, then (once that product has read P_t out of
 //                 S_t) S_t = Q_t K_{j+1}^T, so the softmax of tile a runs
@@ -164,7 +165,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* s_full = bars + 9;    // [QT]: S_t written
   uint64_t* p_full = bars + 11;   // [QT]: P_t written (4 warps)
   uint64_t* o_done = bars + 13;   // [QT]: O_t += P_t V done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  uint64_t* q_full_b = bars + 15;  // Q_b landed (q_full: Q_a)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -195,6 +197,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_full_b, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
@@ -220,19 +223,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      mbar_expect_tx(q_full, TILE_BYTES * n_tiles);
-      for (int t = 0; t < n_tiles; ++t) {
-        tma_load_2d(sQ + t * TILE_BYTES, &tmQ, q_full, 0, row_base + q0 + t * BQ);
-        tma_load_2d(sQ + t * TILE_BYTES + HALF_BYTES, &tmQ, q_full, 64, row_base + q0 + t * BQ);
+      // Q_a and K_0 first (all that S_a(0) needs), then Q_b, then the rings.
+      mbar_expect_tx(q_full, TILE_BYTES);
+      tma_load_2d(sQ, &tmQ, q_full, 0, row_base + q0);
+      tma_load_2d(sQ + HALF_BYTES, &tmQ, q_full, 64, row_base + q0);
+      mbar_expect_tx(&k_full[0], TILE_BYTES);
+      tma_load_2d(sK, &tmK, &k_full[0], 0, row_base);
+      tma_load_2d(sK + HALF_BYTES, &tmK, &k_full[0], 64, row_base);
+      if (n_tiles == 2) {
+        mbar_expect_tx(q_full_b, TILE_BYTES);
+        tma_load_2d(sQ + TILE_BYTES, &tmQ, q_full_b, 0, row_base + q0 + BQ);
+        tma_load_2d(sQ + TILE_BYTES + HALF_BYTES, &tmQ, q_full_b, 64, row_base + q0 + BQ);
       }
       for (int j = 0; j < n_kv_max && ok; ++j) {
         const int s = j & 1;
         const uint32_t ph = ((j >> 1) & 1) ^ 1;
         const int r = row_base + j * BKV;
-        if (!mbar_wait(&k_empty[s], ph, p.error_flag)) { ok = false; break; }
-        mbar_expect_tx(&k_full[s], TILE_BYTES);
-        tma_load_2d(sK + s * TILE_BYTES, &tmK, &k_full[s], 0, r);
-        tma_load_2d(sK + s * TILE_BYTES + HALF_BYTES, &tmK, &k_full[s], 64, r);
+        if (j > 0) {
+          if (!mbar_wait(&k_empty[s], ph, p.error_flag)) { ok = false; break; }
+          mbar_expect_tx(&k_full[s], TILE_BYTES);
+          tma_load_2d(sK + s * TILE_BYTES, &tmK, &k_full[s], 0, r);
+          tma_load_2d(sK + s * TILE_BYTES + HALF_BYTES, &tmK, &k_full[s], 64, r);
+        }
         if (!mbar_wait(&v_empty[s], ph, p.error_flag)) { ok = false; break; }
         mbar_expect_tx(&v_full[s], TILE_BYTES);
         tma_load_2d(sV + s * TILE_BYTES, &tmV, &v_full[s], 0, r);
@@ -257,7 +269,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(q_full, 0, p.error_flag) || !mbar_wait(&k_full[0], 0, p.error_flag)) ok = false;
       if (ok) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        for (int t = 0; t < n_tiles; ++t) issue_s(t, smem_u32(sK));
+        issue_s(0, smem_u32(sK));
+        if (n_tiles == 2) {
+          if (!mbar_wait(q_full_b, 0, p.error_flag)) ok = false;
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          if (ok) issue_s(1, smem_u32(sK));
+        }
         commit(&k_empty[0]);
       }
       for (int j = 0; j < n_kv_max && ok; ++j) {

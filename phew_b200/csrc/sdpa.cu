@@ -15,9 +15,12 @@
 // released as soon as both S products that read it are done, a value tile
 // after both P V products, so the next loads start early.
 //
-//   warp 0      TMA: Q_a and K_0 first (all that S_a(0) needs), then Q_b,
-//               then K_j and V_j (128B-swizzled, each CTA loading its own
-//               tiles); Q_a and Q_b land on separate barriers
+//   warp 0      TMA: Q_a and K_0 first (all that S_a(0) needs; issued by
+//               the thread that initialises the barriers, before the block
+//               sync and the TMEM allocation), then Q_b, then K_j and V_j
+//               (128B-swizzled, each CTA loading its own tiles); Q_a and Q_b
+//               land on separate barriers; the three tensor maps are
+//               prefetched at entry
 //   warp 1      TMEM owner + MMA issuer.  Per key tile j and query tile t:
 //                 O_t += P_t V_j, then (once that product has read P_t out of
 //                 S_t) S_t = Q_t K_{j+1}^T, so the softmax of tile a runs
@@ -170,6 +173,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmQ)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmK)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmV)) : "memory");
+  }
   const int n_qb = (p.L + BQ * QT - 1) / (BQ * QT);
   // CTA order: heads in groups of 16, so the CTAs running at one time share
   // the K / V of few heads in L2.  With a causal mask later query blocks do
@@ -210,6 +218,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&o_done[t], 1);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    // This thread is also the TMA producer: start Q_a and K_0 now, before
+    // the block-wide sync and the TMEM allocation.
+    mbar_expect_tx(q_full, TILE_BYTES);
+    tma_load_2d(sQ, &tmQ, q_full, 0, row_base + q0);
+    tma_load_2d(sQ + HALF_BYTES, &tmQ, q_full, 64, row_base + q0);
+    mbar_expect_tx(&k_full[0], TILE_BYTES);
+    tma_load_2d(sK, &tmK, &k_full[0], 0, row_base);
+    tma_load_2d(sK + HALF_BYTES, &tmK, &k_full[0], 64, row_base);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -223,13 +239,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      // Q_a and K_0 first (all that S_a(0) needs), then Q_b, then the rings.
-      mbar_expect_tx(q_full, TILE_BYTES);
-      tma_load_2d(sQ, &tmQ, q_full, 0, row_base + q0);
-      tma_load_2d(sQ + HALF_BYTES, &tmQ, q_full, 64, row_base + q0);
-      mbar_expect_tx(&k_full[0], TILE_BYTES);
-      tma_load_2d(sK, &tmK, &k_full[0], 0, row_base);
-      tma_load_2d(sK + HALF_BYTES, &tmK, &k_full[0], 64, row_base);
+      // Q_a and K_0 were issued at set-up (all that S_a(0) needs); now Q_b,
+      // then the rings.
       if (n_tiles == 2) {
         mbar_expect_tx(q_full_b, TILE_BYTES);
         tma_load_2d(sQ + TILE_BYTES, &tmQ, q_full_b, 0, row_base + q0 + BQ);

@@ -1,37 +1,47 @@
 """Benchmark of phew's candidate-evaluation path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl phew|reference]
-                    [--workload gelu_chain|attention|normed_matmul|rms_norm]
+                    [--workload sweep|gelu_chain|attention|normed_matmul|
+                                rms_norm|rms_norm_n256|rms_norm_n1024]
 
-Default workload (gelu_chain): the fused elementwise chain
-z = tanh-GELU(x*a + b) * sigmoid(c) + x on fp16 (4096, 8192) -- the
-fuse->=3-ops path, HBM-bound.  A step is one launch of the fused kernel over
-one batch of inputs.  The other workloads time one launch of the attention
-kernel (bf16 (4, 32, 2048, 128), causal), the normed matmul
-(x bf16 (8192, 4096) @ W (4096, 4096), fused row norm) and rms_norm
-(fp32 (4096, 2048)).
+Default workload (sweep): the verification sweep over a decoder block
+(RMSNorm -> QKV projection (4096 = 32 heads x 128) -> causal attention ->
+output projection -> SwiGLU MLP (hidden 14336), bf16, batch 8): the 16
+candidate graphs the reference's passes emit for it, each verified against
+the baseline over 5 seeds x 3 sizes (seq 512 / 2048 / 8192) x 4 edge
+variants (zeros, N(0,1)*1e4, bf16 subnormals, one-hot rows) -- 960
+candidate units and 60 baseline evaluations.  Processes (one per GPU) take
+(seed, size, variant) groups from one host-side counter; there is no
+data-path collective (strong scaling: the same sweep on 1..N GPUs).
 
 Printed (one JSON line, rank 0):
-  value       the workload's throughput over all ranks (HBM GB/s for the
-              memory-bound kernels, TFLOP/s for the tensor-core ones) with
-              inputs resident in HBM and rotated so no step finds its inputs in
-              the 126 MB L2
-  e2e         the same metric through the public API with pinned host
-              buffers: H2D of the inputs and D2H of the output inside every
-              step (step i+1's H2D overlapping step i's compute and D2H)
-  roofline    achieved vs the measured HBM copy bandwidth / cuBLAS bf16 peak
-  cpu_baseline  the oracle (numpy restatement of the MLX-CPU evaluation)
-              timed on a bounded sample on the host
-  optimized_ms / baseline_ms   (gelu_chain) fused kernel vs the unfused
-              op-by-op evaluation of the same harness function on this backend
+  value       verified candidates / s: the 16 candidates over the device
+              time of the whole sweep (max over ranks); the timed region is
+              one full sweep, and a step is 1/K of it (ms_per_step = region / K)
+  roofline    algorithmic FLOPs of the evaluated units (baselines and the
+              candidates that ran to a comparison) per GPU-second, against
+              the measured sustained bf16 GEMM peak
+  e2e         the same sweep with every group's inputs drawn on the HOST
+              (the counter-based generator on host threads, into pinned
+              memory, one group ahead) and copied in, and every comparison
+              record copied back
+  cpu_baseline  the oracle (numpy restatement of the MLX-CPU evaluation) on a
+              bounded sample of the 64-unit subset (16 candidates x seed 0 x
+              seq 512 x 4 variants), extrapolated by FLOPs to the full sweep
+  configs     (1 GPU) per-kernel figures of the other benchmark configs:
+              rms_norm fp32 n = 256 / 1024 / 4096, the fused fp16 chain, causal
+              SDPA bf16 (4,32,2048,128), normed matmul bf16 8192x4096x4096:
+              value, roofline fraction, clocks and optimized_ms / baseline_ms
+
+The other workloads print the same contract for one kernel: a step is one
+launch over one batch of inputs resident in HBM (rotated past the 126 MB L2),
+K launches captured in a CUDA graph and replayed inside the timed region;
+e2e runs the public API with pinned host buffers (H2D and D2H every step).
 
 ``--impl reference`` times the reference's path on the host CPU (the oracle
 port: MLX, the reference's runtime, is not installable here), using all
-host threads, on the same workload and metric.
-
-Multi-GPU (torchrun): every rank runs its own replica (weak scaling); the
-timed region is bracketed by a barrier and device synchronisation, and the
-max time over ranks is reported.
+host threads, on the same workload and metric.  Under torchrun only rank 0
+runs it.
 """
 
 from __future__ import annotations
@@ -56,21 +66,35 @@ sys.path.insert(0, str(ROOT))
 def parse_args(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["phew", "reference"], default="phew")
-    ap.add_argument("--workload", default="gelu_chain",
-                    choices=["gelu_chain", "attention", "normed_matmul", "rms_norm"])
+    ap.add_argument("--workload", default="sweep", choices=["sweep", *WORKLOADS])
+    # sweep options
+    ap.add_argument("--seeds", type=int, default=5)
+    ap.add_argument("--variants", choices=["edge", "reference"], default="edge")
+    ap.add_argument("--tiny", action="store_true",
+                    help="reduced decoder dimensions (a quick check, not a benchmark number)")
+    ap.add_argument("--journal-dir", default=None)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-configs", action="store_true")
+    ap.add_argument("--cpu-units", type=int, default=3,
+                    help="units of the CPU subset timed for cpu_baseline")
     return ap.parse_args(argv)
 
 
 def load_peaks() -> dict:
+    """HBM copy GB/s and bf16 GEMM TFLOP/s (burst, and sustained for work
+    timed inside a long step) measured on this pool's B200s, or the pool's
+    earlier measurement when the file is absent."""
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
         return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
                 "source": "measured"}
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
 
 
 def load_traffic(name: str | None) -> float | None:
@@ -119,6 +143,13 @@ class Dist:
             return v
         t = self.torch.tensor([v], dtype=self.torch.float64, device="cuda")
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, v: float) -> float:
+        if not self.dist:
+            return v
+        t = self.torch.tensor([float(v)], dtype=self.torch.float64, device="cuda")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
         return float(t.item())
 
     def close(self):
@@ -417,16 +448,24 @@ class NormedMatmul:
 
 
 class RmsNorm:
-    """rms_norm fp32 (4096, 2048): HBM-bound (inputs rotated past the L2)."""
+    """rms_norm fp32 (n, 2048): HBM-bound.  Inputs rotate over enough sets
+    that the launches of one timed graph read more than twice the L2."""
 
-    name = "rms_norm"
     metric, unit, bound, dtype = "rms_norm_hbm_gbs", "GB/s", "hbm", "f32"
-    N, C = 4096, 2048
+    C = 2048
     kernel_regex = "rms_norm"
-    R = 8
+    SIZES = {256: "small", 1024: "typical", 4096: "large"}
+
+    def __init__(self, n: int = 4096) -> None:
+        self.N = n
+        self.name = "rms_norm" if n == 4096 else f"rms_norm_n{n}"
+        per = self.work_per_step()
+        self.R = max(8, -(-2 * L2_BYTES // per) + 1)
+        self.min_steps = 2 * self.R  # one graph reads every set twice
 
     def describe(self):
-        return f"mx.fast.rms_norm fp32 ({self.N},{self.C}), one kernel per step"
+        return (f"mx.fast.rms_norm fp32 ({self.N},{self.C}), one kernel per step; inputs rotated "
+                f"over {self.R} sets ({self.R * self.N * self.C * 4 / 1e6:.0f} MB)")
 
     def work_per_step(self):
         return 2 * self.N * self.C * 4 + self.C * 4
@@ -434,7 +473,7 @@ class RmsNorm:
     def host_inputs(self, seed):
         from phew_b200.workloads import rms_norm_inputs
 
-        return rms_norm_inputs("large", seed)
+        return rms_norm_inputs(self.SIZES[self.N], seed)
 
     def setup(self, mx, host):
         base = [mx.array(h) for h in host]
@@ -464,7 +503,17 @@ class RmsNorm:
         return self.work_per_step() / dt / 1e9, dt, f"full ({self.N},{self.C})"
 
 
-WORKLOADS = {c.name: c for c in (GeluChain, Attention, NormedMatmul, RmsNorm)}
+L2_BYTES = 126 * 1024 * 1024
+
+
+WORKLOADS = {
+    "gelu_chain": GeluChain,
+    "attention": Attention,
+    "normed_matmul": NormedMatmul,
+    "rms_norm": lambda: RmsNorm(4096),
+    "rms_norm_n256": lambda: RmsNorm(256),
+    "rms_norm_n1024": lambda: RmsNorm(1024),
+}
 
 
 # ---------------------------------------------------------------------------
@@ -474,6 +523,9 @@ WORKLOADS = {c.name: c for c in (GeluChain, Attention, NormedMatmul, RmsNorm)}
 
 def run_reference(args) -> None:
     if int(os.environ.get("RANK", "0")) != 0:
+        return
+    if args.workload == "sweep":
+        run_reference_sweep(args)
         return
     w = WORKLOADS[args.workload]()
     threads = os.cpu_count() or 1
@@ -502,34 +554,36 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def run_phew(args) -> None:
+def measure_kernel(w, mx, d, steps: int, warmup: int, e2e: bool = True) -> dict:
+    """Times one workload's kernel: `steps` launches captured in one CUDA
+    graph, replayed inside a region bracketed by barrier + synchronize,
+    CUDA events on the launching stream, clocks sampled during it; then (if
+    `e2e`) the public API with pinned host buffers.  Returns the line's
+    fields (value is the whole-job figure over `d.world` replicas)."""
     import numpy as np
     import torch
 
-    from phew_b200 import mx
+    from phew_b200 import _native
     from phew_b200.ops import check_device_errors
 
-    d = Dist()
     dev = mx.core.device()
     stream = torch.cuda.current_stream()
-    w = WORKLOADS[args.workload]()
     work = w.work_per_step()
     scale = 1e9 if w.unit == "GB/s" else 1e12
     host = w.host_inputs(d.rank)
     w.setup(mx, host)
+    steps = max(steps, getattr(w, "min_steps", 0))
 
-    for i in range(args.warmup):
+    for i in range(warmup):
         w.launch(i)
     torch.cuda.synchronize()
-    # The K timed launches are captured once into a CUDA graph, so the timed
+    # The timed launches are captured once into a CUDA graph, so the timed
     # region measures the device and not the Python host path (which the e2e
     # number below includes).
-    from phew_b200 import _native
-
     graph = torch.cuda.CUDAGraph()
     n0 = _native.launch_count()
     with torch.cuda.graph(graph):
-        for i in range(args.steps):
+        for i in range(steps):
             w.launch(i)
     graph_launches = _native.launch_count() - n0  # the kernels the timed replay runs
     graph.replay()
@@ -547,8 +601,22 @@ def run_phew(args) -> None:
     del graph
     local_ms = ev0.elapsed_time(ev1)
     max_ms = d.max(local_ms)
-    value = work * args.steps * d.world / (max_ms / 1e3) / scale
-    achieved = work / (local_ms / args.steps / 1e3) / scale
+    value = work * steps * d.world / (max_ms / 1e3) / scale
+    achieved = work / (local_ms / steps / 1e3) / scale
+    peaks = load_peaks()
+    peak = peaks["hbm_gbs"] if w.bound == "hbm" else peaks["bf16_tflops"]
+    out = {
+        "metric": w.metric, "value": value, "unit": w.unit, "steps": steps,
+        "ms_per_step": max_ms / steps, "dtype": w.dtype,
+        "workload": w.describe(), "work_per_step": work,
+        "roofline": {"bound": w.bound, "achieved": achieved, "peak": peak, "unit": w.unit,
+                     "frac": achieved / peak, "traffic": load_traffic(getattr(w, "profile", None)),
+                     "peak_source": peaks["source"] + (" (burst)" if w.bound == "tensor" else "")},
+        "gpu_launches": graph_launches,
+        "clocks": clk.summary(),
+    }
+    if not e2e:
+        return out
 
     # e2e through the public API with pinned host buffers.  Every step
     # copies its inputs host -> device, runs the API call and copies the
@@ -598,7 +666,7 @@ def run_phew(args) -> None:
         e2e_step(i)
     join_copies()
     torch.cuda.synchronize()
-    e2e_steps = max(3, min(args.steps, 20))
+    e2e_steps = max(3, min(steps, 20))
     d.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -611,27 +679,29 @@ def run_phew(args) -> None:
     torch.cuda.synchronize()
     d.barrier()
     e2e_ms = d.max(e0.elapsed_time(e1))
-    e2e_val = work * e2e_steps * d.world / (e2e_ms / 1e3) / scale
+    out["e2e"] = {"value": work * e2e_steps * d.world / (e2e_ms / 1e3) / scale, "unit": w.unit,
+                  "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                  "copies": "every step's H2D and D2H inside the timed region; step i+1's H2D "
+                            "overlaps step i's compute and D2H (separate streams)"}
+    return out
 
-    peaks = load_peaks()
-    peak = peaks["hbm_gbs"] if w.bound == "hbm" else peaks["bf16_tflops"]
+
+def run_phew(args) -> None:
+    from phew_b200 import mx
+
+    d = Dist()
+    w = WORKLOADS[args.workload]()
+    m = measure_kernel(w, mx, d, args.steps, args.warmup)
     line = {
-        "metric": w.metric, "value": value, "unit": w.unit, "n_gpus": d.world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": max_ms / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": w.dtype,
+        "metric": m["metric"], "value": m["value"], "unit": m["unit"], "n_gpus": d.world,
+        "steps": m["steps"], "warmup": args.warmup, "ms_per_step": m["ms_per_step"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": m["dtype"],
         "data": "synthetic (np.random.default_rng(rank))",
-        "config": {"workload": w.describe(), "work_per_step": work,
+        "config": {"workload": m["workload"], "work_per_step": m["work_per_step"],
                    "l2": "inputs larger than L2 or rotated across sets larger than L2",
                    "parallelism": f"replicas x{d.world}"},
-        "roofline": {"bound": w.bound, "achieved": achieved, "peak": peak, "unit": w.unit,
-                     "frac": achieved / peak, "traffic": load_traffic(getattr(w, "profile", None)),
-                     "peak_source": peaks["source"] + (" (burst)" if w.bound == "tensor" else "")},
-        "e2e": {"value": e2e_val, "unit": w.unit, "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "steps": e2e_steps,
-                "copies": "every step's H2D and D2H inside the timed region; step i+1's H2D "
-                          "overlaps step i's compute and D2H (separate streams)"},
-        "gpu_launches": graph_launches,
-        "clocks": clk.summary(),
+        "roofline": m["roofline"], "e2e": m["e2e"], "gpu_launches": m["gpu_launches"],
+        "clocks": m["clocks"],
     }
     line.update(w.extras(mx))
     if d.rank == 0 and d.world == 1:
@@ -650,6 +720,7 @@ def run_phew(args) -> None:
 # ---------------------------------------------------------------------------
 
 SOURCES = ROOT / "tests" / "golden" / "sources"
+SIZES = ["small", "typical", "large"]
 
 
 def decoder_specs(dims, seqs):
@@ -688,43 +759,49 @@ def _exception_kinds(verdicts) -> dict:
     return kinds
 
 
-def run_sweep(args) -> None:
-    import torch
+def _sweep_setup(args):
+    from phew_b200 import sweep
+    from phew_b200.workloads import DECODER_FULL, DECODER_SEQ, DECODER_TINY, DECODER_TINY_SEQ
 
-    from phew_b200 import _native, mx, sweep
-    from phew_b200.ops import check_device_errors
-    from phew_b200.workloads import DECODER_FULL, DECODER_SEQ, DECODER_TINY, DECODER_TINY_SEQ, decoder_block_fn
-
-    d = Dist()
-    mx.core.device()
     full = not args.tiny
     dims, seqs = (DECODER_FULL, DECODER_SEQ) if full else (DECODER_TINY, DECODER_TINY_SEQ)
     tag = "decoder_full" if full else "decoder_tiny"
     names = sorted(p.stem for p in SOURCES.glob(f"{tag}__*.py"))
-    cands = sweep.load_candidates({n: (SOURCES / f"{n}.py").read_text() for n in names})
-    baseline = decoder_block_fn(mx, dims)
-    seeds = list(range(args.seeds))
-    sizes = ["small", "typical", "large"]
     variants = sweep.VARIANT_SETS[args.variants]
-    shards = sweep.make_shards(names, seeds)
-    groups = sweep.make_groups(seeds, sizes, variants)
-    store = _sweep_store(d)
-    jdir = Path(args.journal_dir) if args.journal_dir else Path(tempfile.mkdtemp(prefix="sweep_"))
-    if d.dist:  # every rank journals into rank 0's directory
-        obj = [str(jdir)]
-        d.dist.broadcast_object_list(obj, src=0)
-        jdir = Path(obj[0])
-    jdir.mkdir(parents=True, exist_ok=True)
-    journal = jdir / f"journal.rank{d.rank}.jsonl"
-    ev = sweep.DeviceEvaluator(baseline, cands, sweep.DeviceInputs(decoder_specs(dims, seqs)))
+    return dims, seqs, tag, names, variants
 
-    # warm-up: compile every kernel the candidates use (generated kernels
-    # specialise on row length, so each size compiles its own), untimed
-    for size in sizes:
-        for c in names:
-            ev(c, 99, size, variants[0])
-    ev.release()
-    torch.cuda.synchronize()
+
+def _evaluated_flops(jdir: Path, dims, seqs) -> tuple[int, int, int]:
+    """Algorithmic FLOPs of the units a sweep evaluated, from its journals:
+    every group's baseline plus each candidate that ran to a comparison
+    (a candidate that raised did no counted work).  Returns (flops,
+    evaluated candidate units, raising units)."""
+    from phew_b200 import sweep
+    from phew_b200.workloads import decoder_flops
+
+    flops = evaluated = raised = 0
+    for p in sorted(jdir.glob("journal.rank*.jsonl")):
+        for g in sweep.load_groups(p).values():
+            f = decoder_flops(seqs[g.size], dims)
+            # the baseline ran unless every unit of the group raised
+            if any(r is None or "exception=" not in r for r in g.results.values()):
+                flops += f
+            for r in g.results.values():
+                if r is not None and "exception=" in r:
+                    raised += 1
+                else:
+                    evaluated += 1
+                    flops += f
+    return flops, evaluated, raised
+
+
+def _timed_sweep(d, groups, names, ev, store, journal, run_id, prefetch=None):
+    """One sweep over `groups` inside a region bracketed by barrier +
+    synchronize; returns (device seconds on this rank, wall seconds,
+    library launches, clocks)."""
+    import torch
+
+    from phew_b200 import _native, sweep
 
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(torch.cuda.current_device()) as clk:
@@ -733,65 +810,342 @@ def run_sweep(args) -> None:
         t0 = time.perf_counter()
         n0 = _native.launch_count()
         e0.record()
-        recs = sweep.run_groups(groups, names, ev, store, d.rank, journal=journal,
-                                run_id=f"sweep/{jdir.name}")
+        sweep.run_groups(groups, names, ev, store, d.rank, journal=journal, run_id=run_id,
+                         prefetch=prefetch)
         e1.record()
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
         launches = _native.launch_count() - n0
         d.barrier()
+    return e0.elapsed_time(e1) / 1e3, wall, launches, clk.summary()
+
+
+def _shared_dir(d, prefix: str, given: str | None) -> Path:
+    jdir = Path(given) if given else Path(tempfile.mkdtemp(prefix=prefix))
+    if d.dist:  # every rank journals into rank 0's directory
+        obj = [str(jdir)]
+        d.dist.broadcast_object_list(obj, src=0)
+        jdir = Path(obj[0])
+    jdir.mkdir(parents=True, exist_ok=True)
+    return jdir
+
+
+def _host_threads(d) -> int:
+    """Host threads one rank may use for input draws: the cores this
+    process may run on, shared by the ranks of the node, one left for the
+    thread that launches kernels."""
+    try:
+        cores = len(os.sched_getaffinity(0))
+    except AttributeError:
+        cores = os.cpu_count() or 1
+    local = int(os.environ.get("LOCAL_WORLD_SIZE", str(d.world)))
+    return max(1, cores // max(1, local) - 1)
+
+
+def run_sweep(args) -> None:
+    import torch
+
+    from phew_b200 import mx, sweep
+    from phew_b200.ops import check_device_errors
+    from phew_b200.verify import checker as checker_mod
+    from phew_b200.workloads import decoder_block_fn, decoder_flops
+
+    d = Dist()
+    mx.core.device()
+    dims, seqs, tag, names, variants = _sweep_setup(args)
+    cands = sweep.load_candidates({n: (SOURCES / f"{n}.py").read_text() for n in names})
+    baseline = decoder_block_fn(mx, dims)
+    seeds = list(range(args.seeds))
+    shards = sweep.make_shards(names, seeds)
+    groups = sweep.make_groups(seeds, SIZES, variants)
+    store = _sweep_store(d)
+    specs = decoder_specs(dims, seqs)
+    ev = sweep.DeviceEvaluator(baseline, cands, sweep.DeviceInputs(specs))
+
+    # warm-up (untimed): W passes of every candidate at one size, sizes
+    # cycling large -> small, so every size's runtime-compiled kernels are
+    # built (each size compiles its own) before the timed region
+    order = list(reversed(SIZES))
+    for i in range(max(args.warmup, len(SIZES))):
+        for c in names:
+            ev(c, 99, order[i % len(order)], variants[0])
+    ev.release()
+    torch.cuda.synchronize()
+
+    jdir = _shared_dir(d, "sweep_", args.journal_dir)
+    dev_s, wall, launches, clocks = _timed_sweep(
+        d, groups, names, ev, store, jdir / f"journal.rank{d.rank}.jsonl", f"sweep/{jdir.name}")
     check_device_errors()
-    dev_s = e0.elapsed_time(e1) / 1e3
     max_s = d.max(dev_s)
     max_wall = d.max(wall)
+    ev.release()
+
+    # e2e: the same sweep with inputs drawn on the host and copied in
+    e2e = None
+    if not args.no_e2e and args.variants == "edge":
+        host_in = sweep.HostInputs(specs, SIZES, threads=_host_threads(d))
+        ev2 = sweep.DeviceEvaluator(baseline, cands, host_in)
+        rb0 = checker_mod.readback_bytes
+        edir = _shared_dir(d, "sweep_e2e_", None)
+        e2e_s, e2e_wall, _, e2e_clocks = _timed_sweep(
+            d, groups, names, ev2, store, edir / f"journal.rank{d.rank}.jsonl",
+            f"sweep_e2e/{edir.name}", prefetch=host_in.prefetch)
+        check_device_errors()
+        host_in.close()
+        ev2.release()
+        h2d = d.sum(host_in.h2d_bytes)
+        d2h = d.sum(checker_mod.readback_bytes - rb0)
+        e2e_max = d.max(e2e_s)
+        e2e = {"value": len(names) / e2e_max, "unit": "candidates/s", "seconds": e2e_max,
+               "h2d_bytes_per_step": h2d / args.steps, "d2h_bytes_per_step": d2h / args.steps,
+               "h2d_bytes_total": h2d, "d2h_bytes_total": d2h,
+               "copies": "every group's 8 arguments drawn on the host (phew_fill_host, "
+                         f"{_host_threads(d)} threads per rank, one group ahead on a background "
+                         "thread, pinned) and copied host -> device; every comparison record "
+                         "copied device -> host; all inside the timed region",
+               "clocks": e2e_clocks, "journal": str(edir)}
+        del host_in
+    torch.cuda.empty_cache()
+
+    line = None
     if d.rank == 0:
-        verdicts, missing = sweep.merge(jdir, shards, sizes, variants)
-        units = len(shards) * len(sizes) * len(variants)
+        verdicts, missing = sweep.merge(jdir, shards, SIZES, variants)
+        units = len(shards) * len(SIZES) * len(variants)
+        flops, evaluated, raised = _evaluated_flops(jdir, dims, seqs)
+        peaks = load_peaks()
+        achieved = flops / d.world / max_s / 1e12
+        peak = peaks["bf16_tflops_sustained"]
         line = {
             "metric": "verified_candidates_per_s", "value": len(names) / max_s,
-            "unit": "candidates/s", "n_gpus": d.world, "steps": 1, "warmup": 1,
-            "ms_per_step": max_s * 1e3, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (device counter-based RNG)",
-            "config": {"workload": f"{tag} verification sweep: {len(names)} candidates x {len(seeds)} "
-                                   f"seeds x sizes {[seqs[s] for s in sizes]} x variants {list(variants)}",
-                       "dims": vars(dims) if hasattr(dims, "__dict__") else str(dims),
-                       "warmup": "each candidate once at every size (runtime kernel compilation)",
-                       "parallelism": f"(seed, size, variant) groups over {d.world} rank(s) from one "
-                                      "host-side counter, no data-path collective"},
-            "units_per_s": units / max_s, "units": units, "wall_s": max_wall,
+            "unit": "candidates/s", "n_gpus": d.world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": max_s * 1e3 / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (counter-based generator; device draws for value, host draws for e2e)",
+            "config": {
+                "workload": f"{tag} verification sweep: {len(names)} candidates x {len(seeds)} seeds x "
+                            f"seq {[seqs[z] for z in SIZES]} x variants {list(variants)}",
+                "dims": dict(batch=dims.batch, dim=dims.dim, heads=dims.heads, hidden=dims.hidden),
+                "step": f"1/{args.steps} of one full sweep: the timed region is the whole sweep "
+                        f"({len(groups)} groups); ms_per_step = region / steps",
+                "warmup": f"{max(args.warmup, len(SIZES))} untimed passes of every candidate at one "
+                          "size (sizes cycling large -> small; builds every runtime-compiled kernel)",
+                "l2": "every group's inputs (>= 520 MB) exceed the L2",
+                "parallelism": f"(seed, size, variant) groups over {d.world} rank(s) from one "
+                               "host-side counter, no data-path collective"},
+            "units_per_s": units / max_s, "units": units, "evaluated_units": evaluated,
+            "raising_units": raised,
+            "evaluated_tflop": flops / 1e12,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "kernel": "the whole sweep: algorithmic FLOPs of every baseline and every "
+                                   "candidate unit that ran to a comparison, per GPU-second",
+                         "peak_source": peaks["source"] + " (sustained)"},
+            "wall_s": max_wall,
             "passed": sorted(c for c, v in verdicts.items() if v["passed"]),
             "failed": sorted(c for c, v in verdicts.items() if not v["passed"]),
             "missing_shards": len(missing),
             # units that failed by raising, by kind (a device out-of-memory here
             # would be a backend fault, not a verdict)
             "exception_units": _exception_kinds(verdicts),
-            "clocks": clk.summary(), "journal": str(jdir),
+            "clocks": clocks, "journal": str(jdir),
             "gpu_launches": launches,  # rank 0's; every rank launches its own groups' kernels
         }
+        if e2e is not None:
+            e2e_verdicts, _ = sweep.merge(Path(e2e["journal"]), shards, SIZES, variants)
+            e2e["verdicts_match"] = {c: v["passed"] for c, v in e2e_verdicts.items()} == \
+                {c: v["passed"] for c, v in verdicts.items()}
+            line["e2e"] = e2e
+
+    if d.world == 1:
+        # GPU units/s on the CPU subset (seed 0, the small size, 4 variants)
+        sub = [sweep.Group(0, "small", v) for v in variants]
+        sub_s, _, _, _ = _timed_sweep(d, sub, names, ev, _sweep_store(d), None, "subset")
+        ev.release()
+        line["gpu_units_per_s_subset"] = len(sub) * len(names) / sub_s
+        if not args.no_configs and not args.tiny:
+            line["configs"] = measure_configs(mx, d, args)
+        threads = os.cpu_count() or 1
+        cb = cpu_sweep_sample(args, args.cpu_units, 0, threads)
+        line["cpu_baseline"] = {"value": cb["value"], "unit": "candidates/s", "cores": threads,
+                                "kind": "port", "sample": cb["sample"],
+                                "units_per_s_subset": cb["units_per_s_subset"]}
+    if d.rank == 0:
         print(json.dumps(line), flush=True)
-    _ = recs
+    _ = decoder_flops
     d.close()
 
 
+def measure_configs(mx, d, args) -> dict:
+    """Per-kernel figures of benchmark configs 0-3 on this GPU (value,
+    roofline fraction, clocks, optimized/baseline ms)."""
+    import torch
+
+    out = {}
+    for name in ("rms_norm_n256", "rms_norm_n1024", "rms_norm", "gelu_chain", "attention",
+                 "normed_matmul"):
+        w = WORKLOADS[name]()
+        m = measure_kernel(w, mx, d, args.steps, args.warmup, e2e=False)
+        ex = w.extras(mx)
+        out[name if name != "rms_norm" else "rms_norm_n4096"] = {
+            "metric": m["metric"], "value": m["value"], "unit": m["unit"],
+            "frac": m["roofline"]["frac"], "peak": m["roofline"]["peak"],
+            "peak_source": m["roofline"]["peak_source"], "traffic": m["roofline"]["traffic"],
+            "ms_per_launch": m["ms_per_step"], "launches": m["steps"], "workload": m["workload"],
+            "clocks": m["clocks"], **ex}
+        del w
+        torch.cuda.empty_cache()
+    return out
+
+
+# ---------------------------------------------------------------------------
+# the sweep on the CPU (oracle), on the 64-unit subset
+# ---------------------------------------------------------------------------
+
+
+def _oracle_candidates(names):
+    from oracle import mlx_cpu
+
+    mlx_cpu.CUDA_CHAINS.update(json.loads((SOURCES / "cuda_chains.json").read_text()))
+    out = {}
+    for name in names:
+        src = (SOURCES / f"{name}.py").read_text()
+        src = src.replace("import phew_b200.mx as mx", "import oracle.mlx_cpu as mx")
+        src = src.replace("from phew_b200.mx import fast", "from oracle.mlx_cpu import fast")
+        ns: dict = {}
+        exec(compile(src, name, "exec"), ns)
+        out[name] = ns["optimized"]
+    return out
+
+
+def _cpu_variant_inputs(specs, variant: str, seed: int, batch_rows: int, threads: int):
+    """One edge variant's arguments for the CPU sample, drawn on the host
+    with numpy (independent generators per chunk, on `threads` threads):
+    x keeps `batch_rows` of its batch rows, the weights are full size."""
+    import numpy as np
+
+    from oracle import mlx_cpu
+
+    out = []
+    ss = np.random.SeedSequence([seed, hash(variant) & 0xFFFF])
+    for i, spec in enumerate(specs):
+        shape = list(spec.shape)
+        if i == 0:
+            shape[0] = batch_rows
+        n = int(np.prod(shape))
+        a = np.zeros(n, np.float32)
+        if variant in ("pm1e4", "subnormal"):
+            scale = 1e4 if variant == "pm1e4" else 1e-39
+            kids = ss.spawn(threads)
+            per = -(-n // threads)
+
+            def draw(t):
+                lo, hi = t * per, min(n, (t + 1) * per)
+                if lo < hi:
+                    np.random.default_rng(kids[t]).standard_normal(hi - lo, dtype=np.float32,
+                                                                   out=a[lo:hi])
+            with cf.ThreadPoolExecutor(max_workers=threads) as ex:
+                list(ex.map(draw, range(threads)))
+            a *= np.float32(scale)
+        elif variant == "one_hot_rows":
+            rows = a.reshape(-1, shape[-1])
+            hot = np.random.default_rng(ss).integers(0, shape[-1], rows.shape[0])
+            rows[np.arange(rows.shape[0]), hot] = 1.0
+        elif variant != "zeros":
+            raise ValueError(f"CPU sample: variant {variant!r}")
+        out.append(mlx_cpu.array(a.reshape(shape).astype(mlx_cpu.BF16)))
+    return out
+
+
+def cpu_sweep_sample(args, n_units: int, first_unit: int, threads: int) -> dict:
+    """Times the oracle on units of the 64-unit subset (16 candidates x
+    seed 0 x the small size x 4 variants, variant-major), each on
+    `batch_rows` of the decoder's batch rows; a variant's baseline is
+    evaluated (and timed) with its first unit.  Returns the units/s on the
+    subset (in full units: the batch slice is 1/batch of a unit) and the
+    candidates/s it implies for the full sweep, by the algorithmic FLOPs of
+    each size relative to the sampled one."""
+    import numpy as np
+
+    from oracle import mlx_cpu, verdict
+    from phew_b200.workloads import decoder_block_fn, decoder_flops
+
+    dims, seqs, tag, names, variants = _sweep_setup(args)
+    specs = decoder_specs(dims, seqs)("small")
+    ocands = _oracle_candidates(names)
+    base_fn = decoder_block_fn(mlx_cpu, dims)
+    tol = verdict.checker_tolerance({"fp32_to_fp32"})
+    batch_rows = 1
+    frac = batch_rows / dims.batch
+    cache: dict[str, tuple] = {}
+    secs = 0.0
+    for u in range(first_unit, first_unit + n_units):
+        v = variants[(u // len(names)) % len(variants)]
+        c = names[u % len(names)]
+        if v not in cache:
+            host = _cpu_variant_inputs(specs, v, 0, batch_rows, threads)  # untimed draw
+            t0 = time.perf_counter()
+            try:
+                b = base_fn(*host)
+            except Exception:  # noqa: BLE001
+                b = None
+            secs += time.perf_counter() - t0
+            cache.clear()
+            cache[v] = (host, b)
+        host, b = cache[v]
+        t0 = time.perf_counter()
+        try:
+            co = ocands[c](*host)
+            if b is not None:
+                bn = np.asarray(b).astype(np.float32)
+                cn = np.asarray(co).astype(np.float32)
+                verdict.compare_output(bn, cn, tol, True)
+        except Exception:  # noqa: BLE001  (a raising unit is a failed unit)
+            pass
+        secs += time.perf_counter() - t0
+    units_per_s = n_units * frac / secs
+    # one candidate of the full sweep: |seeds| x |variants| units at each size
+    rel = sum(decoder_flops(seqs[z], dims) for z in SIZES) / decoder_flops(seqs["small"], dims)
+    per_candidate_s = args.seeds * len(variants) * rel / units_per_s
+    return {"value": 1.0 / per_candidate_s, "units_per_s_subset": units_per_s, "seconds": secs,
+            "sample": f"{n_units} unit(s) of the 64-unit subset (16 candidates x seed 0 x seq "
+                      f"{seqs['small']} x 4 variants), each on {batch_rows} of {dims.batch} batch "
+                      f"rows, baselines included; numpy restatement of the MLX-CPU evaluation on "
+                      f"{threads} threads; candidates/s of the full sweep extrapolated by "
+                      f"algorithmic FLOPs per size ({secs:.1f} s)"}
+
+
+def run_reference_sweep(args) -> None:
+    """The reference arm for the sweep: the oracle port on the host CPU, a
+    step = one unit of the 64-unit subset (on one batch row), all host
+    threads."""
+    threads = os.cpu_count() or 1
+    warm = cpu_sweep_sample(args, args.warmup, 0, threads) if args.warmup else None
+    res = cpu_sweep_sample(args, args.steps, args.warmup, threads)
+    _ = warm
+    line = {
+        "impl": "reference", "metric": "verified_candidates_per_s", "value": res["value"],
+        "unit": "candidates/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": res["seconds"] * 1e3 / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (numpy default_rng, host)",
+        "config": {"workload": "decoder-block verification sweep on the CPU; a step = one unit of "
+                               "the 64-unit subset on one batch row"},
+        "units_per_s_subset": res["units_per_s_subset"],
+        "cpu_baseline": {"value": res["value"], "unit": "candidates/s", "cores": threads,
+                         "kind": "port", "sample": res["sample"]},
+        "e2e": {"value": res["value"], "unit": "candidates/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "MLX (the reference's runtime) is not installable here; the oracle port is timed",
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main(argv=None) -> int:
-    if argv is None:
-        argv = sys.argv[1:]
-    if "--workload" in argv and "sweep" in argv:
-        ap = argparse.ArgumentParser()
-        ap.add_argument("--gpus", type=int, default=1)
-        ap.add_argument("--steps", type=int, default=1)
-        ap.add_argument("--warmup", type=int, default=1)
-        ap.add_argument("--impl", default="phew")
-        ap.add_argument("--workload", default="sweep")
-        ap.add_argument("--seeds", type=int, default=5)
-        ap.add_argument("--variants", choices=["edge", "reference"], default="edge")
-        ap.add_argument("--tiny", action="store_true")
-        ap.add_argument("--journal-dir", default=None)
-        run_sweep(ap.parse_args(argv))
-        return 0
-    args = parse_args(argv)
+    args = parse_args(sys.argv[1:] if argv is None else argv)
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "sweep":
+        run_sweep(args)
     else:
         run_phew(args)
     return 0

@@ -235,6 +235,15 @@ int phew_dequantize(const void* wq, const void* scales, const void* biases, void
                     int64_t rows, int64_t cols, int group_size, int bits, int dtype,
                     void* stream);
 
+/* The producer of that layout (mx.quantize, which the quantisation rewrite
+ * assumes for the weights it packs, rules/quantization.py:37-71): per group
+ * of g values along a row, scale = T(max((max - min) / (2^bits - 1), 1e-8)),
+ * bias = T(min), q = clamp(rint((w - bias) / scale), 0, 2^bits - 1) in fp32
+ * with IEEE division.  w [rows, cols] in `dtype`; wq [rows, cols * bits / 32]
+ * uint32; scales / biases [rows, cols / g] in `dtype`. */
+int phew_quantize(const void* w, void* wq, void* scales, void* biases, int64_t rows,
+                  int64_t cols, int group_size, int bits, int dtype, void* stream);
+
 /* ---- seeded inputs for the verification sweep -------------------------- */
 
 #define PHEW_FILL_NORMAL 0       /* N(0, 1) * scale (Box-Muller)           */
@@ -249,6 +258,16 @@ int phew_dequantize(const void* wq, const void* scales, const void* biases, void
  * (verify/checker.py:235-263) at sweep scale. */
 int phew_fill(void* out, int64_t n, int64_t cols, int dtype, int kind, uint64_t seed,
               uint64_t stream_id, float scale, void* stream);
+
+/* The same generator on `threads` host threads (<= 0: one per hardware
+ * thread) into HOST memory `out` (pinned or pageable); synchronous.  The
+ * reference's input factories draw on the host
+ * (examples/rms_norm.py:27-31, verify/checker.py:246-263); a caller whose
+ * inputs must start in host memory (an end-to-end sweep that copies them
+ * in) draws here.  Values equal phew_fill's except where the host libm and
+ * the device's logf / cospif round the fp32 value differently. */
+int phew_fill_host(void* out, int64_t n, int64_t cols, int dtype, int kind, uint64_t seed,
+                   uint64_t stream_id, float scale, int threads);
 
 /* ---- equivalence comparison -------------------------------------------- */
 

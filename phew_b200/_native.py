@@ -43,6 +43,7 @@ EXPORTED_SYMBOLS = (
     "phew_softmax",
     "phew_reduce_var",
     "phew_dequantize",
+    "phew_quantize",
     "phew_copy_strided_to",
     "phew_reduce",
     "phew_copy_strided",
@@ -51,6 +52,7 @@ EXPORTED_SYMBOLS = (
     "phew_sdpa_supported",
     "phew_sdpa",
     "phew_fill",
+    "phew_fill_host",
     "phew_compare_scratch_bytes",
     "phew_compare",
     "phew_compare_static",

@@ -9,26 +9,37 @@
 //
 // Generator: SplitMix64 finalizer over (seed, stream, i) -> two 24-bit
 // uniforms -> Box-Muller for normals.
+//
+// phew_fill_host runs the same generator on host threads, for callers whose
+// inputs start in host memory (the sweep's end-to-end leg copies them in):
+// the same bits feed the same transforms, so host and device draws agree
+// except where the host's logf / cosf(2*pi*u) and the device's logf /
+// cospif(2u) differ in the last places of the fp32 value.
 #include <math.h>
+#include <string.h>
+
+#include <algorithm>
+#include <thread>
+#include <vector>
 
 #include "common.cuh"
 
 namespace phew {
 namespace {
 
-__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+__host__ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
   z += 0x9e3779b97f4a7c15ull;
   z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
   z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
   return z ^ (z >> 31);
 }
 
-__device__ __forceinline__ uint64_t draw(uint64_t seed, uint64_t stream, uint64_t i) {
+__host__ __device__ __forceinline__ uint64_t draw(uint64_t seed, uint64_t stream, uint64_t i) {
   return mix64(mix64(mix64(seed) ^ stream) ^ i);
 }
 
 // (0, 1] uniform with 24 bits
-__device__ __forceinline__ float u24(uint64_t bits) {
+__host__ __device__ __forceinline__ float u24(uint64_t bits) {
   return (static_cast<float>(bits & 0xFFFFFFull) + 1.0f) * (1.0f / 16777216.0f);
 }
 
@@ -64,10 +75,109 @@ __global__ void fill_kernel(T* out, int64_t n, int64_t cols, int kind, uint64_t 
   }
 }
 
+// ---- host twin ------------------------------------------------------------
+
+// fp32 -> 16-bit storage, round to nearest even (NaN kept quiet).
+inline uint16_t host_bf16_bits(float v) {
+  uint32_t u;
+  memcpy(&u, &v, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return static_cast<uint16_t>((u >> 16) | 0x40u);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return static_cast<uint16_t>(u >> 16);
+}
+
+inline uint16_t host_f16_bits(float v) {
+  uint32_t u;
+  memcpy(&u, &v, 4);
+  const uint32_t sign = (u >> 16) & 0x8000u;
+  const uint32_t a = u & 0x7fffffffu;
+  if (a > 0x7f800000u) return static_cast<uint16_t>(sign | 0x7e00u);  // NaN
+  if (a >= 0x477ff000u) return static_cast<uint16_t>(sign | 0x7c00u);  // rounds to inf
+  if (a < 0x38800000u) {
+    // half subnormal (or zero): value / 2^-24, rounded to nearest even
+    float f;
+    const uint32_t ab = a;
+    memcpy(&f, &ab, 4);
+    const float scaled = f * 16777216.0f;  // exact: power-of-two scale
+    float r = nearbyintf(scaled);          // current rounding mode: nearest even
+    return static_cast<uint16_t>(sign | static_cast<uint32_t>(r));
+  }
+  // normal: rebias the exponent, round the 13 dropped mantissa bits
+  uint32_t m = a + 0xc8000000u;  // exponent 127 -> 15 (subtract 112 << 23)
+  m += 0xfffu + ((m >> 13) & 1u);
+  return static_cast<uint16_t>(sign | (m >> 13));
+}
+
+inline float host_value(int kind, int64_t i, int64_t cols, uint64_t seed, uint64_t stream,
+                        float scale) {
+  switch (kind) {
+    case PHEW_FILL_NORMAL: {
+      const uint64_t b = draw(seed, stream, static_cast<uint64_t>(i));
+      const float r = sqrtf(-2.0f * logf(u24(b)));
+      const float c = cosf(6.28318530717958647692f * u24(b >> 32));
+      return r * c * scale;
+    }
+    case PHEW_FILL_UNIFORM: {
+      const uint64_t b = draw(seed, stream, static_cast<uint64_t>(i));
+      return (2.0f * u24(b) - 1.0f) * scale;
+    }
+    case PHEW_FILL_ONE_HOT_ROWS: {
+      const int64_t row = i / cols, col = i % cols;
+      const int64_t hot = static_cast<int64_t>(draw(seed, stream, static_cast<uint64_t>(row)) %
+                                               static_cast<uint64_t>(cols));
+      return col == hot ? scale : 0.0f;
+    }
+    default:
+      return scale;
+  }
+}
+
+void host_fill_range(void* out, int64_t lo, int64_t hi, int64_t cols, int dtype, int kind,
+                     uint64_t seed, uint64_t stream, float scale) {
+  if (dtype == PHEW_F32) {
+    float* o = static_cast<float*>(out);
+    for (int64_t i = lo; i < hi; ++i) o[i] = host_value(kind, i, cols, seed, stream, scale);
+  } else if (dtype == PHEW_BF16) {
+    uint16_t* o = static_cast<uint16_t*>(out);
+    for (int64_t i = lo; i < hi; ++i) o[i] = host_bf16_bits(host_value(kind, i, cols, seed, stream, scale));
+  } else {
+    uint16_t* o = static_cast<uint16_t*>(out);
+    for (int64_t i = lo; i < hi; ++i) o[i] = host_f16_bits(host_value(kind, i, cols, seed, stream, scale));
+  }
+}
+
 }  // namespace
 }  // namespace phew
 
 using namespace phew;
+
+extern "C" int phew_fill_host(void* out, int64_t n, int64_t cols, int dtype, int kind,
+                              uint64_t seed, uint64_t stream_id, float scale, int threads) {
+  PHEW_REQUIRE(out != nullptr || n == 0, "phew_fill_host: null output");
+  PHEW_REQUIRE(n >= 0 && cols > 0, "phew_fill_host: bad extent");
+  PHEW_REQUIRE(kind >= PHEW_FILL_NORMAL && kind <= PHEW_FILL_CONSTANT, "phew_fill_host: bad kind");
+  PHEW_REQUIRE(dtype == PHEW_F32 || dtype == PHEW_F16 || dtype == PHEW_BF16,
+               "phew_fill_host: bad dtype");
+  if (n == 0) return PHEW_OK;
+  if (threads <= 0) threads = static_cast<int>(std::max(1u, std::thread::hardware_concurrency()));
+  // at least 1 Mi elements per thread: thread start-up is not free
+  const int64_t max_threads = std::max<int64_t>(1, n >> 20);
+  const int nt = static_cast<int>(std::min<int64_t>(threads, max_threads));
+  if (nt == 1) {
+    host_fill_range(out, 0, n, cols, dtype, kind, seed, stream_id, scale);
+    return PHEW_OK;
+  }
+  std::vector<std::thread> pool;
+  pool.reserve(nt);
+  const int64_t per = (n + nt - 1) / nt;
+  for (int t = 0; t < nt; ++t) {
+    const int64_t lo = t * per, hi = std::min(n, lo + per);
+    if (lo >= hi) break;
+    pool.emplace_back(host_fill_range, out, lo, hi, cols, dtype, kind, seed, stream_id, scale);
+  }
+  for (auto& th : pool) th.join();
+  return PHEW_OK;
+}
 
 extern "C" int phew_fill(void* out, int64_t n, int64_t cols, int dtype, int kind, uint64_t seed,
                          uint64_t stream_id, float scale, void* stream) {

@@ -171,6 +171,146 @@ class DeviceInputs:
                 for i, a in enumerate(base_args)]
 
 
+class HostInputs:
+    """The inputs of `DeviceInputs`, drawn on the HOST and copied in.
+
+    The reference's input factories and edge variants draw on the host
+    (``examples/rms_norm.py:27-31``, ``verify/checker.py:235-263``) and
+    hand the arrays to the device.  This provider does the same at sweep
+    scale: ``phew_fill_host`` runs the counter-based generator of
+    ``phew_fill`` on host threads into pinned buffers, and every group's
+    arguments are copied host -> device before the group is evaluated.
+    With ``prefetch(group)`` the next group is drawn on a background thread
+    while the device evaluates the current one (two pinned slots; a slot is
+    redrawn only after the copies out of it have finished).
+
+    Variants: the edge set (zeros, pm1e4, subnormal, one_hot_rows) and the
+    base draw ("random"), with the arguments `DeviceInputs` gives them.
+    ``h2d_bytes`` counts the bytes copied in."""
+
+    def __init__(self, arg_specs: Callable[[str], list[ArgSpec]], sizes: Sequence[str],
+                 threads: int = 0) -> None:
+        import threading
+
+        import torch
+
+        self.arg_specs = arg_specs
+        self.threads = threads
+        self.h2d_bytes = 0
+        self._lock = threading.Lock()
+        self._pending: dict[tuple, Any] = {}
+        self._slot = 0
+        self._device = torch.cuda.current_device()
+        # one pinned buffer per argument and slot, sized for the largest size
+        cap = [0] * len(arg_specs(sizes[0]))
+        for z in sizes:
+            for j, a in enumerate(arg_specs(z)):
+                cap[j] = max(cap[j], int(np.prod(a.shape)) * _itemsize(a.dtype))
+        self._pinned = [[torch.empty(c, dtype=torch.uint8).pin_memory() for c in cap]
+                        for _ in range(2)]
+        self._copied = [None, None]  # event: copies out of the slot have finished
+        self._pool = None
+
+    # -- host side ---------------------------------------------------------
+    def _draw(self, slot: int, seed: int, size: str, variant: str) -> list:
+        from . import _native
+        from . import dtypes as dt
+
+        ev = self._copied[slot]
+        if ev is not None:
+            ev.synchronize()
+        out = []
+        for i, spec in enumerate(self.arg_specs(size)):
+            n = int(np.prod(spec.shape))
+            d = dt.from_any(spec.dtype)
+            buf = self._pinned[slot][i][: n * _itemsize(spec.dtype)]
+            ptr = ctypes.c_void_p(buf.data_ptr())
+            cols = max(spec.shape[-1] if len(spec.shape) else 1, 1)
+
+            def fill(kind, stream, scale):
+                _native.call("phew_fill_host", ptr, ctypes.c_int64(n), ctypes.c_int64(cols),
+                             d.code, kind, ctypes.c_uint64(seed & (2**64 - 1)),
+                             ctypes.c_uint64(stream), ctypes.c_float(scale), self.threads)
+
+            if variant == "zeros":
+                buf.zero_()
+            elif variant == "random":
+                if spec.kind == "ones":
+                    fill(FILL_CONSTANT, 0, 1.0)
+                elif spec.kind == "causal_mask":
+                    L, S = spec.shape[-2], spec.shape[-1]
+                    m = np.zeros((L, S), np.float32)
+                    m[np.triu_indices(L, S - L + 1, S)] = -np.inf
+                    buf.numpy()[:] = np.frombuffer(m.astype(d.np).tobytes(), np.uint8)
+                else:
+                    fill(FILL_NORMAL, _stream_id("base", size, i), 1.0 / float(np.sqrt(spec.fan_in)))
+            else:
+                kinds = {"pm1e4": (FILL_NORMAL, 1e4), "subnormal": (FILL_NORMAL, 1e-39),
+                         "one_hot_rows": (FILL_ONE_HOT, 1.0)}
+                if variant not in kinds:
+                    raise ValueError(f"HostInputs: variant {variant!r} is not drawn on the host")
+                kind, scale = kinds[variant]
+                fill(kind, _stream_id(variant, size, i), scale)
+            out.append((buf, spec))
+        return out
+
+    def prefetch(self, group: Group) -> None:
+        """Start drawing `group`'s arguments on a background thread."""
+        import concurrent.futures as cf
+
+        if self._pool is None:
+            self._pool = cf.ThreadPoolExecutor(max_workers=1)
+        with self._lock:
+            key = (group.seed, group.size, group.variant)
+            if key in self._pending:
+                return
+            slot = self._slot
+            self._slot ^= 1
+            self._pending[key] = (slot, self._pool.submit(self._draw, slot, *key))
+
+    # -- the DeviceInputs interface ----------------------------------------
+    def base(self, size: str, seed: int) -> list:
+        return list(self.arg_specs(size))
+
+    def variant(self, name: str, base_args: list, size: str, seed: int) -> list:
+        import torch
+
+        from . import dtypes as dt
+        from .mx.core import array
+
+        key = (seed, size, name)
+        with self._lock:
+            hit = self._pending.pop(key, None)
+            if hit is None:
+                slot = self._slot
+                self._slot ^= 1
+        if hit is not None:
+            slot, fut = hit
+            host = fut.result()
+        else:
+            host = self._draw(slot, seed, size, name)
+        args = []
+        for buf, spec in host:
+            d = dt.from_any(spec.dtype)
+            t = torch.empty(spec.shape, dtype=d.torch, device=self._device)
+            t.view(torch.uint8).view(-1).copy_(buf, non_blocking=True)
+            self.h2d_bytes += buf.numel()
+            args.append(array(t))
+        ev = torch.cuda.Event()
+        ev.record()
+        self._copied[slot] = ev
+        return args
+
+    def close(self) -> None:
+        if self._pool is not None:
+            self._pool.shutdown(wait=True)
+            self._pool = None
+
+
+def _itemsize(dtype_name: str) -> int:
+    return {"float32": 4, "float16": 2, "bfloat16": 2}[dtype_name]
+
+
 # ---------------------------------------------------------------------------
 # running shards
 # ---------------------------------------------------------------------------
@@ -285,6 +425,7 @@ def run_groups(
     rank: int = 0,
     journal: Path | None = None,
     run_id: str = "sweep",
+    prefetch: Callable[[Group], None] | None = None,
 ) -> list[GroupRecord]:
     """Evaluate groups taken from one shared counter, in list order, until
     the list is exhausted.
@@ -296,29 +437,48 @@ def run_groups(
     takes the next one, so ranks finish within about one group of each other
     and no baseline is computed twice.  Groups already journalled (by any
     rank: every ``*.jsonl`` beside `journal` is read) are not re-evaluated;
-    each finished group is appended to `journal`."""
+    each finished group is appended to `journal`.
+
+    With `prefetch`, a rank claims its next group before it evaluates the
+    current one and calls ``prefetch(next_group)`` first, so that preparing
+    the next group's inputs (a host-side draw) overlaps this group's device
+    work; each rank then holds at most one claimed group beyond the one it
+    is running."""
     done: dict[tuple, GroupRecord] = {}
     if journal:
         for p in sorted(Path(journal).parent.glob("*.jsonl")):
             done.update(load_groups(p))
     out: list[GroupRecord] = []
     key = f"{run_id}/next"
-    while (i := store.add(key, 1) - 1) < len(groups):
+
+    def claim() -> int:
+        return store.add(key, 1) - 1
+
+    i = claim()
+    while i < len(groups):
+        nxt = None
+        if prefetch is not None:
+            nxt = claim()
+            if nxt < len(groups):
+                g2 = groups[nxt]
+                if (g2.seed, g2.size, g2.variant) not in done:
+                    prefetch(g2)
         g = groups[i]
         k = (g.seed, g.size, g.variant)
         if k in done:
             out.append(done[k])
-            continue
-        t0 = time.perf_counter()
-        rec = GroupRecord(g.seed, g.size, g.variant, rank=rank)
-        for c in candidates:
-            ok, failure = evaluate(c, g.seed, g.size, g.variant)
-            rec.results[c] = None if ok else failure
-        rec.seconds = time.perf_counter() - t0
-        out.append(rec)
-        if journal:
-            with open(journal, "a") as f:
-                f.write(rec.to_json() + "\n")
+        else:
+            t0 = time.perf_counter()
+            rec = GroupRecord(g.seed, g.size, g.variant, rank=rank)
+            for c in candidates:
+                ok, failure = evaluate(c, g.seed, g.size, g.variant)
+                rec.results[c] = None if ok else failure
+            rec.seconds = time.perf_counter() - t0
+            out.append(rec)
+            if journal:
+                with open(journal, "a") as f:
+                    f.write(rec.to_json() + "\n")
+        i = nxt if nxt is not None else claim()
     return out
 
 

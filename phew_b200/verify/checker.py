@@ -62,6 +62,10 @@ class _CompareBuffers:
 
 _buffers: dict[int, _CompareBuffers] = {}
 
+# Bytes of comparison records read back to the host so far (one record per
+# compared output): what a verification run moves device -> host.
+readback_bytes = 0
+
 
 def _bufs(dev: torch.device) -> _CompareBuffers:
     b = _buffers.get(dev.index)
@@ -104,6 +108,8 @@ def compare_arrays(b, c, atol: float, rtol: float) -> _native.CompareStats:
         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream),
     )
     raw = bufs.record.cpu().numpy().tobytes()
+    global readback_bytes
+    readback_bytes += len(raw)
     _ = float32  # keep the import local to the device path
     return _native.CompareStats.from_buffer_copy(raw)
 

@@ -253,3 +253,71 @@ def test_two_rank_gloo_group_sweep(tmp_path, crash_rank):
         # the held group (largest size, seed 0) never ran; its seed's shards were reassigned
         assert len(keys) == n_groups - 1 and (0, "large", VARIANTS[0]) not in keys
         assert res["reassigned"] == len(CANDS)
+
+
+def test_prefetch_claims_one_group_ahead():
+    """With a prefetch hook a rank claims its next group before evaluating
+    the current one and hands it to the hook first; every group still runs
+    exactly once, in list order, and every prefetched group is the one the
+    rank runs next."""
+    from torch.distributed import HashStore
+
+    cands = CANDS[:3]
+    groups = sweep.make_groups(SEEDS[:2], SIZES, VARIANTS)
+    events = []
+    base = fake_eval(set())
+
+    def evaluate(cand, seed, size, variant):
+        events.append(("eval", (seed, size, variant)))
+        return base(cand, seed, size, variant)
+
+    def prefetch(g):
+        events.append(("prefetch", (g.seed, g.size, g.variant)))
+
+    recs = sweep.run_groups(groups, cands, evaluate, HashStore(), prefetch=prefetch)
+    assert [(r.seed, r.size, r.variant) for r in recs] == [(g.seed, g.size, g.variant) for g in groups]
+    pre = [k for e, k in events if e == "prefetch"]
+    assert pre == [(g.seed, g.size, g.variant) for g in groups[1:]]
+    # each prefetch comes before the evaluation of the group it follows
+    for i, k in enumerate(pre):
+        first_eval_of_next = events.index(("eval", k))
+        assert events.index(("prefetch", k)) < first_eval_of_next
+
+
+def _prefetch_worker(rank, world, port, jdir):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    from torch.distributed import distributed_c10d
+
+    store = distributed_c10d._get_default_store()
+    groups = sweep.make_groups(SEEDS[:2], SIZES, VARIANTS)
+    prefetched, evaluated = [], []
+    base = fake_eval(set())
+
+    def evaluate(cand, seed, size, variant):
+        if cand == CANDS[0]:
+            evaluated.append([seed, size, variant])
+        return base(cand, seed, size, variant)
+
+    sweep.run_groups(groups, CANDS[:2], evaluate, store, rank,
+                     journal=Path(jdir) / f"journal.rank{rank}.jsonl", run_id="p",
+                     prefetch=lambda g: prefetched.append([g.seed, g.size, g.variant]))
+    (Path(jdir) / f"rank{rank}.json").write_text(json.dumps({"pre": prefetched, "ev": evaluated}))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_two_rank_gloo_prefetch_sweep(tmp_path):
+    port = _free_port()
+    mp.spawn(_prefetch_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    runs = [json.loads((tmp_path / f"rank{r}.json").read_text()) for r in range(2)]
+    all_ev = [tuple(k) for r in runs for k in r["ev"]]
+    assert len(all_ev) == len(set(all_ev)) == 2 * len(SIZES) * len(VARIANTS)
+    for r in runs:
+        # a rank prefetches only groups it then evaluates itself
+        assert all(k in r["ev"] for k in r["pre"])

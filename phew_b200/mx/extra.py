@@ -7,16 +7,21 @@ on ``phew_reduce_var``; array assembly (concatenate, stack, pad, tile,
 repeat, roll, slice_update) is views plus ``phew_copy_strided_to``.  Ops
 that are data-dependent orderings or gathers (sort, argsort, topk,
 partition, cumulative scans, take / take_along_axis / put_along_axis,
-argmax / argmin, einsum) use torch's CUDA kernels on the same device
-buffers: they are off the candidate hot path (no candidate of the
-verification sweep uses them) and are marked as such in the docstrings.
+argmax / argmin, median, einsum) use torch's CUDA kernels on the same device
+buffers.  They are off the candidate hot path (no candidate of the
+verification sweep or the benchmark harnesses uses them), and because they
+are not this backend's own kernels they raise ``NotImplementedError`` unless
+the caller opts in: ``with allow_torch_kernels(): ...`` or
+``PHEW_ALLOW_TORCH_KERNELS=1`` in the environment.
 """
 
 from __future__ import annotations
 
 import builtins
+import contextlib
 import ctypes
 import math
+import os
 from typing import Any, Sequence
 
 import numpy as np
@@ -53,6 +58,7 @@ __all__ = [
     "concatenate", "concat", "stack", "split", "pad", "tile", "repeat", "roll", "moveaxis",
     "permute_dims", "flatten", "unflatten", "atleast_1d", "atleast_2d", "atleast_3d",
     "contiguous", "view", "as_strided", "slice", "slice_update", "asarray", "einsum",
+    "allow_torch_kernels",
     "hadamard_transform", "bartlett", "blackman", "hamming", "hanning", "quantize", "dequantize",
     "quantized_matmul",
 ]
@@ -75,6 +81,31 @@ def quantized_matmul(x, w, scales=None, biases=None, transpose: bool = True, gro
     from ..ops import quantized_matmul as _qmm
 
     return _qmm(x, w, scales, biases, transpose=transpose, group_size=group_size, bits=bits)
+
+
+# Ops that run on torch's CUDA kernels instead of this library's: refused
+# unless the caller opts in (see the module docstring).
+_TORCH_KERNELS = {"on": os.environ.get("PHEW_ALLOW_TORCH_KERNELS", "") == "1"}
+
+
+@contextlib.contextmanager
+def allow_torch_kernels(flag: bool = True):
+    """Within the block, ops backed by torch's CUDA kernels (sorts, scans,
+    gathers, argmax / argmin, median, einsum) may run."""
+    prev = _TORCH_KERNELS["on"]
+    _TORCH_KERNELS["on"] = bool(flag)
+    try:
+        yield
+    finally:
+        _TORCH_KERNELS["on"] = prev
+
+
+def _torch_kernel_op(name: str) -> None:
+    if not _TORCH_KERNELS["on"]:
+        raise NotImplementedError(
+            f"mx.{name} runs on torch's CUDA kernels, not on this backend's own; it is off the "
+            "candidate path.  Opt in with `with phew_b200.mx.allow_torch_kernels():` or "
+            "PHEW_ALLOW_TORCH_KERNELS=1")
 
 
 def _arr(x) -> array:
@@ -246,6 +277,7 @@ def _axis_arg(a: array, axis):
 
 def argmax(a, axis=None, keepdims: bool = False, **_):
     """Index of the first maximum, uint32 (torch CUDA; off the hot path)."""
+    _torch_kernel_op("argmax")
     a = _arr(a)
     t = a._t.argmax() if axis is None else a._t.argmax(dim=_axis_arg(a, axis), keepdim=keepdims)
     return _wrap(t.to(torch.int32).view(torch.uint32) if hasattr(torch, "uint32") else t.to(torch.int32))
@@ -253,12 +285,14 @@ def argmax(a, axis=None, keepdims: bool = False, **_):
 
 def argmin(a, axis=None, keepdims: bool = False, **_):
     """Index of the first minimum, uint32 (torch CUDA; off the hot path)."""
+    _torch_kernel_op("argmin")
     a = _arr(a)
     t = a._t.argmin() if axis is None else a._t.argmin(dim=_axis_arg(a, axis), keepdim=keepdims)
     return _wrap(t.to(torch.int32).view(torch.uint32) if hasattr(torch, "uint32") else t.to(torch.int32))
 
 
 def _scan(fn, a, axis, reverse, inclusive):
+    _torch_kernel_op(fn.__name__.lstrip("_"))
     a = _arr(a)
     t = a._t.reshape(-1) if axis is None else a._t
     ax = 0 if axis is None else int(axis) % a.ndim
@@ -338,11 +372,13 @@ def _flat_or_axis(a: array, axis):
 
 
 def sort(a, axis=-1, **_):
+    _torch_kernel_op("sort")
     t, ax = _flat_or_axis(_arr(a), axis)
     return _wrap(torch.sort(t, dim=ax, stable=True).values.contiguous())
 
 
 def argsort(a, axis=-1, **_):
+    _torch_kernel_op("argsort")
     t, ax = _flat_or_axis(_arr(a), axis)
     return _wrap(torch.sort(t, dim=ax, stable=True).indices.to(torch.int32).contiguous())
 
@@ -359,6 +395,7 @@ def argpartition(a, kth: int, axis=-1, **_):
 
 def topk(a, k: int, axis=-1, **_):
     """The k largest values along `axis` (ascending, as MLX returns them)."""
+    _torch_kernel_op("topk")
     t, ax = _flat_or_axis(_arr(a), axis)
     v = torch.topk(t, int(k), dim=ax, largest=True, sorted=True).values
     return _wrap(v.flip(ax).contiguous())
@@ -366,6 +403,7 @@ def topk(a, k: int, axis=-1, **_):
 
 def median(a, axis=None, keepdims: bool = False, **_):
     """Mean of the two middle values for even counts (MLX's definition)."""
+    _torch_kernel_op("median")
     a = _arr(a)
     x = astype(a, dt.float32)
     axes = _norm_axes(x, axis)
@@ -380,6 +418,7 @@ def median(a, axis=None, keepdims: bool = False, **_):
 
 
 def take(a, indices, axis=None, **_):
+    _torch_kernel_op("take")
     a = _arr(a)
     idx = _arr(indices)._t.long()
     if axis is None:
@@ -390,6 +429,7 @@ def take(a, indices, axis=None, **_):
 
 
 def take_along_axis(a, indices, axis=None, **_):
+    _torch_kernel_op("take_along_axis")
     a = _arr(a)
     idx = _arr(indices)._t.long()
     if axis is None:
@@ -403,6 +443,7 @@ def take_along_axis(a, indices, axis=None, **_):
 
 
 def put_along_axis(a, indices, values, axis=None, **_):
+    _torch_kernel_op("put_along_axis")
     a = _arr(a)
     out = a._t.clone()
     idx = _arr(indices)._t.long()
@@ -419,6 +460,7 @@ def put_along_axis(a, indices, values, axis=None, **_):
 def einsum(subscripts: str, *operands, **_):
     """torch.einsum on the device buffers (cuBLAS for contractions; no
     candidate on the sweep's hot path emits einsum)."""
+    _torch_kernel_op("einsum")
     ts = [_arr(x)._t for x in operands]
     return _wrap(torch.einsum(subscripts, *ts).contiguous())
 

@@ -168,35 +168,34 @@ def quantized_sdpa(q, k, v, scale_k, biases_k, scale_v, biases_v, *, scale: floa
 
 def quantize(w, group_size: int = 64, bits: int = 4):
     """``mx.quantize``: affine group-wise quantisation along the last axis ->
-    (codes packed 32/bits per uint32, scales, biases).  Per group:
-    scale = (max - min) / (2^bits - 1), bias = min, q = round((w - bias) /
-    scale) clipped to [0, 2^bits - 1].  An input-preparation helper (torch
-    ops on the device buffer), not on the candidate path."""
-    import torch
-
-    from .mx.core import array as _array
+    (codes packed 32/bits per uint32, scales, biases), on ``phew_quantize``.
+    Per group: scale = (max - min) / (2^bits - 1) (at least 1e-8, rounded to
+    w's dtype), bias = min (rounded), q = round((w - bias) / scale) clipped
+    to [0, 2^bits - 1]."""
+    from . import dtypes as dt
 
     w = asarray_device(w)
+    if w.dtype.code is None:
+        raise TypeError(f"quantize: floating-point weights required, got {w.dtype.name}")
     g, nb = int(group_size), int(bits)
     per = 32 // nb
     cols = w.shape[-1]
-    if cols % g or cols % per:
-        raise ValueError("quantize: the last axis must be a multiple of group_size and of 32/bits")
-    t = w._t.float().reshape(-1, cols // g, g)
-    lo = t.amin(-1, keepdim=True)
-    hi = t.amax(-1, keepdim=True)
-    n_bins = (1 << nb) - 1
-    sc = torch.clamp((hi - lo) / n_bins, min=1e-8)
-    sc = sc.to(w._t.dtype).float()
-    bi = lo.to(w._t.dtype).float()
-    qv = torch.clamp(torch.round((t - bi) / sc), 0, n_bins).to(torch.int64).reshape(-1, cols // per, per)
-    shifts = (torch.arange(per, device=qv.device, dtype=torch.int64) * nb)
-    words = (qv << shifts).sum(-1).to(torch.int64)
-    words = torch.where(words >= 2**31, words - 2**32, words).to(torch.int32).view(torch.uint32)
+    if cols % g or g % per:
+        raise ValueError("quantize: the last axis must be a multiple of group_size, and "
+                         "group_size of 32/bits")
+    if not w._t.is_contiguous():
+        from .mx.core import contiguous_copy
+
+        w = contiguous_copy(w)
+    rows = w.size // cols
     shp = tuple(w.shape[:-1])
-    return (_array._wrap(words.reshape(shp + (cols // per,))),
-            _array._wrap(sc.to(w._t.dtype).reshape(shp + (cols // g,))),
-            _array._wrap(bi.to(w._t.dtype).reshape(shp + (cols // g,))))
+    wq = empty(shp + (cols // per,), dt.uint32)
+    sc = empty(shp + (cols // g,), w.dtype)
+    bi = empty(shp + (cols // g,), w.dtype)
+    _native.call("phew_quantize", ctypes.c_void_p(w._t.data_ptr()), ctypes.c_void_p(wq._t.data_ptr()),
+                 ctypes.c_void_p(sc._t.data_ptr()), ctypes.c_void_p(bi._t.data_ptr()),
+                 ctypes.c_int64(rows), ctypes.c_int64(cols), g, nb, w.dtype.code, _stream())
+    return wq, sc, bi
 
 
 _error_flags: dict[int, object] = {}

@@ -89,7 +89,8 @@ def test_all_any_argmax_argmin(mx):
         ref = getattr(mlx_cpu, name)(mlx_cpu.array(x), axis=1)
         assert np.array_equal(np.asarray(got), np.asarray(ref))
     for name in ("argmax", "argmin"):
-        got = getattr(mx, name)(mx.array(x), axis=1)
+        with mx.allow_torch_kernels():
+            got = getattr(mx, name)(mx.array(x), axis=1)
         ref = getattr(mlx_cpu, name)(mlx_cpu.array(x), axis=1)
         assert np.array_equal(np.asarray(got).astype(np.int64), np.asarray(ref).astype(np.int64))
 
@@ -149,7 +150,20 @@ def test_concatenate_stack_split_pad_tile_repeat_roll(mx, dtype):
     assert all(np.array_equal(np.asarray(p), np.asarray(r)) for p, r in zip(parts, refs))
 
 
+def test_torch_kernel_ops_are_refused_without_opt_in(mx):
+    x = mx.array(_rand((5, 30), seed=14))
+    for fn in (lambda: mx.sort(x), lambda: mx.cumsum(x, axis=1), lambda: mx.topk(x, 2),
+               lambda: mx.argmax(x), lambda: mx.einsum("ij->j", x)):
+        with pytest.raises(NotImplementedError, match="torch's CUDA kernels"):
+            fn()
+
+
 def test_cumsum_sort_topk_take(mx):
+    with mx.allow_torch_kernels():
+        _cumsum_sort_topk_take(mx)
+
+
+def _cumsum_sort_topk_take(mx):
     x = _rand((5, 30), seed=14)
     _close(mx.cumsum(mx.array(x), axis=1), mlx_cpu.cumsum(mlx_cpu.array(x), axis=1))
     _close(mx.cumsum(mx.array(x), axis=0, reverse=True, inclusive=False),

@@ -97,3 +97,22 @@ def test_launch_count_is_readable_without_a_device():
 
     n = _native.launch_count()
     assert isinstance(n, int) and n >= 0
+
+
+def test_candidate_sources_use_no_torch_kernel_ops():
+    """No emitted candidate source and no benchmark harness calls an op
+    that runs on torch's CUDA kernels (those raise without an opt-in), so
+    the benchmark and the sweep run on this library's kernels only."""
+    import inspect
+
+    from phew_b200 import workloads
+
+    fenced = ("argmax", "argmin", "cumsum", "cumprod", "cummax", "cummin", "logcumsumexp", "sort",
+              "argsort", "topk", "partition", "argpartition", "median", "take", "take_along_axis",
+              "put_along_axis", "einsum")
+    pat = re.compile(r"\bmx\.(%s)\(" % "|".join(fenced))
+    texts = [p.read_text() for p in (ROOT / "tests" / "golden" / "sources").glob("*.py")]
+    texts.append(inspect.getsource(workloads))
+    assert len(texts) > 40
+    for t in texts:
+        assert not pat.search(t), pat.search(t).group(0)

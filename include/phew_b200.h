@@ -106,6 +106,19 @@ int phew_launch_count(uint64_t* out);
 /* Number of kernels currently held in the compile cache. */
 int phew_compile_cache_size(void);
 
+/* Test hook for the failure path of the tensor-core pipelines, not for
+ * production use.  The NEXT phew_gemm or phew_sdpa call on the calling
+ * thread that launches a tcgen05 kernel leaves one of its producer's tile
+ * loads unissued -- GEMM: ring position `stage` (the stage-th k-block load
+ * of each CTA); attention: the V tile of key tile `stage` -- and bounds
+ * each of its pipeline waits by `wait_limit_ns` (0 < limit <= 1 s) instead
+ * of 1 s.  The consumers' waits then run out: the kernel sets the caller's
+ * error flag to PHEW_ERR_TIMEOUT, lets the loads and MMAs it did issue land,
+ * frees its TMEM and returns, and the device stays usable.  One-shot: the
+ * call that uses it clears it.  No counterpart in the reference (MLX's
+ * kernels have no bounded waits to exercise). */
+int phew_test_inject_stall(int stage, uint64_t wait_limit_ns);
+
 /* ---- hand-written primitives ------------------------------------------- */
 
 /* y[r, :] = w * cast(x[r, :] * rsqrt(mean(x[r, :]^2) + eps)); w may be NULL

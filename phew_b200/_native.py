@@ -37,6 +37,7 @@ EXPORTED_SYMBOLS = (
     "phew_launch",
     "phew_launch_count",
     "phew_compile_cache_size",
+    "phew_test_inject_stall",
     "phew_rms_norm",
     "phew_layer_norm",
     "phew_rope",

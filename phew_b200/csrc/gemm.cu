@@ -82,6 +82,8 @@ struct Params {
   float eps;
   int* error_flag;
   const float* row_vec;  // row_scale != 0: the per-row factor (or sum), [a_batched ? batch : 1][M]
+  unsigned long long wait_ns;  // bound of every pipeline wait
+  int withhold;                // test hook: k-block load left unissued (-1: none)
 };
 
 // Sum of squares of one row of A (K elements) by one warp: 16-byte loads,
@@ -200,6 +202,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   uint64_t* acc_full = empty + C::STAGES;  // [ACC]: accumulator a holds a finished tile
   uint64_t* acc_empty = acc_full + ACC;    // [ACC]: the epilogue has read accumulator a
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + ACC);
+  uint64_t* drain = acc_empty + ACC + 1;   // the MMA thread's last commit (failure path)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -246,6 +249,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], 4);
     }
+    mbar_init(drain, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -256,6 +260,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
+  uint32_t kg_armed = 0;  // producer: k-blocks whose loads were issued (ring positions 0..kg_armed-1)
 
   if (warp == 0) {
     // ---------------- TMA producer: runs ahead across tiles ----------------
@@ -269,10 +274,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         for (int kb = 0; kb < num_kb; ++kb, ++kg) {
           const int s = kg % C::STAGES;
           const uint32_t ph = (kg / C::STAGES) & 1;
-          if (!mbar_wait(&empty[s], ph ^ 1, p.error_flag)) {
+          if (!mbar_wait(&empty[s], ph ^ 1, p.error_flag, p.wait_ns)) {
             ok = false;
             break;
           }
+          kg_armed = kg + 1;
+          if (static_cast<int>(kg) == p.withhold) continue;  // test hook: this stage never fills
           uint8_t* sa = smem + s * C::STAGE_BYTES;
           uint8_t* sb = sa + C::A_BYTES;
           mbar_expect_tx(&full[s], C::STAGE_BYTES);
@@ -298,7 +305,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         work(t, bz, m0, n0, mt);
         const int a = it % ACC;
         // accumulator a is free once the epilogue has read the tile before
-        if (!mbar_wait(&acc_empty[a], ((it / ACC) & 1) ^ 1, p.error_flag)) {
+        if (!mbar_wait(&acc_empty[a], ((it / ACC) & 1) ^ 1, p.error_flag, p.wait_ns)) {
           ok = false;
           break;
         }
@@ -307,7 +314,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         for (int kb = 0; kb < num_kb; ++kb, ++kg) {
           const int s = kg % C::STAGES;
           const uint32_t ph = (kg / C::STAGES) & 1;
-          if (!mbar_wait(&full[s], ph, p.error_flag)) {
+          if (!mbar_wait(&full[s], ph, p.error_flag, p.wait_ns)) {
             ok = false;
             break;
           }
@@ -343,7 +350,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       int bz, m0, n0, mt;
       work(t, bz, m0, n0, mt);
       const int a = it % ACC;
-      if (ok && !mbar_wait(&acc_full[a], (it / ACC) & 1, p.error_flag)) ok = false;
+      if (ok && !mbar_wait(&acc_full[a], (it / ACC) & 1, p.error_flag, p.wait_ns)) ok = false;
       if (!ok) break;
       if (!rows_ready) {
         asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -447,7 +454,24 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   }
   if (!ok && p.error_flag) atomicExch(p.error_flag, PHEW_ERR_TIMEOUT);
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  __syncthreads();
+  if (__syncthreads_or(!ok)) {
+    // A wait ran out somewhere in the CTA: before the shared memory and the
+    // TMEM are given back, let the work this CTA still has in flight land
+    // (each wait bounded again): the tile loads of the ring positions the
+    // producer armed last, and the MMAs the issuer committed.
+    if (warp == 0 && lane == 0) {
+      const uint32_t first = kg_armed > static_cast<uint32_t>(C::STAGES) ? kg_armed - C::STAGES : 0;
+      for (uint32_t i = first; i < kg_armed; ++i) {
+        if (static_cast<int>(i) == p.withhold) continue;
+        mbar_wait(&full[i % C::STAGES], (i / C::STAGES) & 1, nullptr, p.wait_ns);
+      }
+    } else if (warp == 1 && lane == 0) {
+      commit(drain);
+      mbar_wait(drain, 0, nullptr, p.wait_ns);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+  }
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     tmem_dealloc(tmem, C::TMEM_COLS);
@@ -667,6 +691,9 @@ extern "C" int phew_gemm(const void* A, const void* B, void* Cout, int64_t M, in
   p.eps = eps;
   p.error_flag = error_flag;
   p.row_vec = nullptr;
+  const phew::tc::TestStall stall = phew::tc::take_test_stall();
+  p.wait_ns = stall.wait_ns;
+  p.withhold = stall.withhold;
   if (row_scale) {
     // The per-row factor lives in stream-ordered memory allocated here and
     // freed after the GEMM on the same stream: no sharing between streams,

@@ -10,10 +10,24 @@
 #include <vector>
 
 #include "common.cuh"
+#include "tc_common.cuh"
 
 namespace phew {
 
 static thread_local std::string g_last_error;
+
+namespace tc {
+namespace {
+thread_local TestStall g_test_stall{-1, 0};
+}  // namespace
+
+TestStall take_test_stall() {
+  TestStall t = g_test_stall;
+  g_test_stall = TestStall{-1, 0};
+  if (t.wait_ns == 0) t.wait_ns = kWaitLimitNs;
+  return t;
+}
+}  // namespace tc
 
 int set_error(int code, const std::string& msg) {
   g_last_error = msg;
@@ -228,4 +242,12 @@ extern "C" int phew_l2_flush(void* buf, size_t bytes, void* stream) {
   l2_flush_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<uint4*>(buf), n_vec, salt++);
   return launch_status("l2_flush_kernel");
+}
+
+extern "C" int phew_test_inject_stall(int stage, uint64_t wait_limit_ns) {
+  PHEW_REQUIRE(stage >= 0, "phew_test_inject_stall: stage must be >= 0");
+  PHEW_REQUIRE(wait_limit_ns > 0 && wait_limit_ns <= phew::tc::kWaitLimitNs,
+               "phew_test_inject_stall: wait limit must be in (0, 1 s]");
+  phew::tc::g_test_stall = phew::tc::TestStall{stage, static_cast<unsigned long long>(wait_limit_ns)};
+  return PHEW_OK;
 }

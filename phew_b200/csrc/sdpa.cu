@@ -67,6 +67,8 @@ struct Params {
   float scale_log2;  // scale * log2(e), > 0
   void* O;
   int* error_flag;
+  unsigned long long wait_ns;  // bound of every pipeline wait
+  int withhold;                // test hook: the V load of key tile `withhold` is left unissued (-1: none)
 };
 
 // ---- scalar and packed (f32x2) arithmetic helpers ----
@@ -170,6 +172,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* o_done = bars + 13;   // [QT]: O_t += P_t V done
   uint64_t* q_full_b = bars + 15;  // Q_b landed (q_full: Q_a)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* drain = bars + 17;     // the MMA thread's last commit (failure path)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -217,6 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&p_full[t], 4);
       mbar_init(&o_done[t], 1);
     }
+    mbar_init(drain, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     // This thread is also the TMA producer: start Q_a and K_0 now, before
     // the block-wide sync and the TMEM allocation.
@@ -235,6 +239,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
+  // producer: the key tile whose K / V load each ring slot received last (-1: none)
+  int k_last0 = 0, k_last1 = -1, v_last0 = -1, v_last1 = -1;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -251,12 +257,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ph = ((j >> 1) & 1) ^ 1;
         const int r = row_base + j * BKV;
         if (j > 0) {
-          if (!mbar_wait(&k_empty[s], ph, p.error_flag)) { ok = false; break; }
+          if (!mbar_wait(&k_empty[s], ph, p.error_flag, p.wait_ns)) { ok = false; break; }
           mbar_expect_tx(&k_full[s], TILE_BYTES);
           tma_load_2d(sK + s * TILE_BYTES, &tmK, &k_full[s], 0, r);
           tma_load_2d(sK + s * TILE_BYTES + HALF_BYTES, &tmK, &k_full[s], 64, r);
+          if (s) k_last1 = j; else k_last0 = j;
         }
-        if (!mbar_wait(&v_empty[s], ph, p.error_flag)) { ok = false; break; }
+        if (!mbar_wait(&v_empty[s], ph, p.error_flag, p.wait_ns)) { ok = false; break; }
+        if (j == p.withhold) continue;  // test hook: this V tile never lands
+        if (s) v_last1 = j; else v_last0 = j;
         mbar_expect_tx(&v_full[s], TILE_BYTES);
         tma_load_2d(sV + s * TILE_BYTES, &tmV, &v_full[s], 0, r);
         tma_load_2d(sV + s * TILE_BYTES + HALF_BYTES, &tmV, &v_full[s], 64, r);
@@ -277,12 +286,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         commit(&s_full[t]);
       };
-      if (!mbar_wait(q_full, 0, p.error_flag) || !mbar_wait(&k_full[0], 0, p.error_flag)) ok = false;
+      if (!mbar_wait(q_full, 0, p.error_flag, p.wait_ns) || !mbar_wait(&k_full[0], 0, p.error_flag, p.wait_ns)) ok = false;
       if (ok) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         issue_s(0, smem_u32(sK));
         if (n_tiles == 2) {
-          if (!mbar_wait(q_full_b, 0, p.error_flag)) ok = false;
+          if (!mbar_wait(q_full_b, 0, p.error_flag, p.wait_ns)) ok = false;
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           if (ok) issue_s(1, smem_u32(sK));
         }
@@ -291,15 +300,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < n_kv_max && ok; ++j) {
         const int s = j & 1, s1 = (j + 1) & 1;
         const bool more = j + 1 < n_kv_max;
-        if (!mbar_wait(&v_full[s], (j >> 1) & 1, p.error_flag)) { ok = false; break; }
-        if (more && !mbar_wait(&k_full[s1], ((j + 1) >> 1) & 1, p.error_flag)) { ok = false; break; }
+        if (!mbar_wait(&v_full[s], (j >> 1) & 1, p.error_flag, p.wait_ns)) { ok = false; break; }
+        if (more && !mbar_wait(&k_full[s1], ((j + 1) >> 1) & 1, p.error_flag, p.wait_ns)) { ok = false; break; }
         const uint32_t v_addr = smem_u32(sV + s * TILE_BYTES);
         const uint32_t k_addr = smem_u32(sK + s1 * TILE_BYTES);
 #pragma unroll
         for (int t = 0; t < QT; ++t) {
           const int nk = t == 0 ? n_kv_a : n_kv_b;
           if (!ok || j >= nk) continue;
-          if (!mbar_wait(&p_full[t], j & 1, p.error_flag)) { ok = false; continue; }
+          if (!mbar_wait(&p_full[t], j & 1, p.error_flag, p.wait_ns)) { ok = false; continue; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
           for (int kk = 0; kk < BKV / 16; ++kk) {
@@ -311,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           commit(&o_done[t]);
           if (j + 1 < nk) {
             // S_t holds P_t until this product has read it.
-            if (!mbar_wait(&o_done[t], j & 1, p.error_flag)) { ok = false; continue; }
+            if (!mbar_wait(&o_done[t], j & 1, p.error_flag, p.wait_ns)) { ok = false; continue; }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             issue_s(t, k_addr);
           }
@@ -334,7 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float c = p.scale_log2;
     float m_ref = -INFINITY, l = 0.f;
     for (int j = 0; j < nkv && ok; ++j) {
-      if (!mbar_wait(&s_full[t], j & 1, p.error_flag)) { ok = false; break; }
+      if (!mbar_wait(&s_full[t], j & 1, p.error_flag, p.wait_ns)) { ok = false; break; }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       uint32_t raw[128];
 #pragma unroll
@@ -371,7 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // 0..j-1: wait for the last one first.
         tmem_st_wait();
         tile_sum = compute_p<BF16>(raw, c, m_ref, s_addr);
-        if (!mbar_wait(&o_done[t], (j - 1) & 1, p.error_flag)) ok = false;
+        if (!mbar_wait(&o_done[t], (j - 1) & 1, p.error_flag, p.wait_ns)) ok = false;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         if (ok) {
 #pragma unroll
@@ -392,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&p_full[t]);
     }
     // Epilogue: O_t / l after the last product.
-    if (ok && nkv > 0 && !mbar_wait(&o_done[t], (nkv - 1) & 1, p.error_flag)) ok = false;
+    if (ok && nkv > 0 && !mbar_wait(&o_done[t], (nkv - 1) & 1, p.error_flag, p.wait_ns)) ok = false;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (ok && nkv > 0) {
       const float inv = 1.0f / l;
@@ -414,7 +423,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (!ok && p.error_flag) atomicExch(p.error_flag, PHEW_ERR_TIMEOUT);
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  __syncthreads();
+  if (__syncthreads_or(!ok)) {
+    // A wait ran out somewhere in the CTA: before the shared memory and the
+    // TMEM are given back, let the work still in flight land (each wait
+    // bounded again): the Q tiles and the last K / V load of each ring
+    // slot, and the MMAs the issuer committed.
+    if (warp == 0 && lane == 0) {
+      mbar_wait(q_full, 0, nullptr, p.wait_ns);
+      if (n_tiles == 2) mbar_wait(q_full_b, 0, nullptr, p.wait_ns);
+      if (k_last0 >= 0) mbar_wait(&k_full[0], (k_last0 >> 1) & 1, nullptr, p.wait_ns);
+      if (k_last1 >= 0) mbar_wait(&k_full[1], (k_last1 >> 1) & 1, nullptr, p.wait_ns);
+      if (v_last0 >= 0) mbar_wait(&v_full[0], (v_last0 >> 1) & 1, nullptr, p.wait_ns);
+      if (v_last1 >= 0) mbar_wait(&v_full[1], (v_last1 >> 1) & 1, nullptr, p.wait_ns);
+    } else if (warp == 1 && lane == 0) {
+      commit(drain);
+      mbar_wait(drain, 0, nullptr, p.wait_ns);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+  }
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     tmem_dealloc(tmem, TMEM_COLS);
@@ -475,6 +502,9 @@ extern "C" int phew_sdpa(const void* q, const void* k, const void* v, void* o, i
   p.scale_log2 = scale * 1.4426950408889634f;
   p.O = o;
   p.error_flag = error_flag;
+  const tc::TestStall stall = tc::take_test_stall();
+  p.wait_ns = stall.wait_ns;
+  p.withhold = stall.withhold;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return dtype == PHEW_BF16 ? attn::launch<true>(q, k, v, p, st) : attn::launch<false>(q, k, v, p, st);
 }

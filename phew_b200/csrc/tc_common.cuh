@@ -14,6 +14,16 @@
 namespace phew {
 namespace tc {
 
+// One-shot test hook (phew_test_inject_stall): the next tcgen05 launch on the
+// calling thread leaves the producer's load number `withhold` unissued and
+// bounds its waits by `wait_ns`.  take_test_stall() returns and clears it
+// ({-1, kWaitLimitNs} when none is set).
+struct TestStall {
+  int withhold;
+  unsigned long long wait_ns;
+};
+TestStall take_test_stall();
+
 // A pipeline wait gives up after this long (or as soon as another CTA has
 // reported a timeout through the error flag), so a broken pipeline ends the
 // kernel with PHEW_ERR_TIMEOUT instead of hanging the GPU.
@@ -50,14 +60,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Waits for the phase with `parity` to complete.  Returns false when the
-// wait ran past kWaitLimitNs or another CTA already reported a timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const int* error_flag) {
+// wait ran past `limit_ns` or (with an error_flag) another CTA already
+// reported a timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const int* error_flag,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255) == 0) {
-      if (globaltimer() - t0 > kWaitLimitNs) return false;
+      if (globaltimer() - t0 > limit_ns) return false;
       if (error_flag && *reinterpret_cast<const volatile int*>(error_flag) != 0) return false;
     }
   }

@@ -89,9 +89,9 @@ def rope_fn(mx, half: int = 64):
     return fn
 
 
-def rms_norm_inputs(size: str, seed: int):
+def rms_norm_inputs(size: str, seed: int, rows: int | None = None):
     rng = np.random.default_rng(seed)
-    x = rng.standard_normal((RMS_ROWS[size], RMS_COLS)).astype(np.float32)
+    x = rng.standard_normal((rows or RMS_ROWS[size], RMS_COLS)).astype(np.float32)
     w = np.ones((RMS_COLS,), np.float32)
     return [x, w]
 

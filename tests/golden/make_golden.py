@@ -1,7 +1,7 @@
 """Generate the golden fixtures under tests/golden/ from the reference itself.
 
-Run in a checkout that has the phew reference importable (default
-/root/reference, or $PHEW_REFERENCE):
+Run with the phew reference checkout named by $PHEW_REFERENCE (or with its
+``phew`` package importable):
 
     python tests/golden/make_golden.py
 
@@ -27,7 +27,15 @@ Writes
   the chain it was emitted from, so the oracle can evaluate it on the CPU;
 * op_registry.json -- the mlx.core / mlx.core.fast op names the reference's
   tracer records (ir/op_registry.py), which the backend's mx namespace must
-  provide.
+  provide;
+* optimizer_runs.json -- the reference's own ``Optimizer(fn,
+  input_factory).run()`` (optimizer.py:90-353) on the rms_norm and
+  gelu_chain harnesses with elementwise fusion off (the fused kernels' MSL
+  cannot run on the oracle): the rules it applied, its Step-7 verdict, its
+  ``output_source`` and the step names of its search trace.
+
+``python tests/golden/make_golden.py --part optimizer`` regenerates only
+that file.
 """
 
 from __future__ import annotations
@@ -45,7 +53,19 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent.parent
-REF = Path(os.environ.get("PHEW_REFERENCE", "/root/reference"))
+def _reference_root() -> Path:
+    env = os.environ.get("PHEW_REFERENCE")
+    if env:
+        return Path(env)
+    import importlib.util
+
+    spec = importlib.util.find_spec("phew")
+    if spec is None or not spec.origin:
+        raise SystemExit("make_golden: set PHEW_REFERENCE to the phew reference checkout")
+    return Path(spec.origin).resolve().parent.parent
+
+
+REF = _reference_root()
 sys.path.insert(0, str(ROOT))
 sys.path.insert(0, str(REF))
 sys.path.insert(0, str(HERE))
@@ -333,8 +353,64 @@ def make_op_registry():
     return {"IMPLEMENTED": sorted(R.IMPLEMENTED), "FAST_IMPLEMENTED": sorted(R.FAST_IMPLEMENTED)}
 
 
+# Rows per size of the Optimizer runs: the oracle evaluates every op on the
+# CPU, and the reference's benchmark calls each function up to ~850 times in
+# one run, so the runs use fewer rows than the benchmark shapes (the emitted
+# sources do not depend on the row count).
+OPTIMIZER_ROWS = {"rms_norm": {"small": 8, "typical": 32, "large": 128},
+                  "gelu_chain": {"small": 4, "typical": 16, "large": 64}}
+
+
+def optimizer_inputs(name, size, seed):
+    rows = OPTIMIZER_ROWS[name][size]
+    if name == "rms_norm":
+        return W.rms_norm_inputs(size, seed, rows=rows)
+    return W.gelu_chain_inputs(size, seed, rows=rows)
+
+
+def make_optimizer_runs(core):
+    """Run the reference's Optimizer end to end with mlx.core served by the
+    oracle (the reference's own benchmark, passes, codegen and checker; no
+    part of this backend is installed)."""
+    import time
+
+    from phew.optimizer import Optimizer
+
+    if not hasattr(core, "metal"):
+        core.metal = types.SimpleNamespace(is_available=lambda: False)
+    runs = {}
+    for name in ("rms_norm", "gelu_chain"):
+        w = W.WORKLOADS[name]
+
+        def factory(size, seed, name=name):
+            return [core.array(a) for a in optimizer_inputs(name, size, seed)], {}
+
+        t0 = time.perf_counter()
+        res = Optimizer(w.make_fn(core), factory, enable_elementwise_fusion=False).run()
+        print(f"optimizer run {name}: {time.perf_counter() - t0:.1f} s", flush=True)
+        runs[f"{name}__fusion0"] = {
+            "rows": OPTIMIZER_ROWS[name],
+            "applied_rules": list(res.applied_rules),
+            "verification_passed": bool(res.verification_passed),
+            "verification_details": list(res.verification_details),
+            "output_source": res.output_source,
+            "steps": [ln for ln in res.search_trace if ln.startswith("Step")],
+        }
+    return runs
+
+
 def main() -> int:
+    import argparse
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--part", choices=["all", "optimizer"], default="all")
+    args = ap.parse_args()
     core = fake_mlx()
+    # before make_sources, which re-targets phew's codegen to this backend
+    (HERE / "optimizer_runs.json").write_text(json.dumps(make_optimizer_runs(core), indent=1))
+    if args.part == "optimizer":
+        print(f"wrote {HERE / 'optimizer_runs.json'}")
+        return 0
     (HERE / "op_registry.json").write_text(json.dumps(make_op_registry(), indent=1))
     SOURCES.mkdir(exist_ok=True)
     (HERE / "verdicts.json").write_text(json.dumps(make_verdicts(), indent=1))

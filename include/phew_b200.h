@@ -288,7 +288,8 @@ int phew_fill_host(void* out, int64_t n, int64_t cols, int dtype, int kind, uint
 typedef struct phew_compare_stats {
   double sum_abs_base;      /* sum |b| over all elements (fp64, fixed order)   */
   double mean_abs_base;     /* sum_abs_base / n                                */
-  double max_abs_diff;      /* max |b - c| over pairs where both are finite    */
+  double max_abs_diff;      /* max |b - c| over pairs where neither is NaN
+                               (an infinite difference counts: +inf)          */
   double atol_used;         /* tolerance actually applied (after bf16 relax)   */
   double rtol_used;
   int64_t n;                /* elements compared                               */
@@ -326,7 +327,10 @@ int phew_compare(const void* b, const void* c, int64_t n, int dtype,
  * loads the library until the process exits); the call allocates nothing.
  *   - The first call on each device looks up that array's address on the
  *     current device (cudaGetSymbolAddress); make that first call before
- *     any stream capture.
+ *     any stream capture.  The address is kept per device and per context:
+ *     after a device reset (cudaDeviceReset, or a released and re-created
+ *     primary context) the next call looks it up again, so that call too
+ *     belongs before any capture.
  *   - Every call shares the one array: calls that overlap on the GPU (for
  *     instance on two streams at once) race.  Nothing in it needs clearing.
  *   - Comparisons whose scratch need (phew_compare_scratch_bytes) exceeds

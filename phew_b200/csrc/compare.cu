@@ -279,6 +279,8 @@ extern "C" int phew_compare(const void* b, const void* c, int64_t n, int dtype, 
 // per-block partial results live in one array in this library's own device
 // memory instead of a caller-provided scratch buffer.
 // ---------------------------------------------------------------------------
+#include <cuda.h>
+
 #include <mutex>
 
 namespace phew {
@@ -289,7 +291,40 @@ constexpr size_t kStaticScratchBytes =
     sizeof(StatsPartial) * kMaxBlocks + sizeof(ComparePartial) * kMaxBlocks;
 constexpr int kMaxStaticDevices = 256;
 std::mutex g_static_mu;
+// Per device: the array's address and the id of the context it was looked
+// up in.  A device reset (cudaDeviceReset, or a primary context that was
+// released and re-created) reloads the module at a new address in a new
+// context, so an address is reused only while the context id is the same.
 void* g_static_scratch[kMaxStaticDevices] = {};
+unsigned long long g_static_ctx[kMaxStaticDevices] = {};
+
+// Unique id of the calling thread's current context (0 when the driver
+// offers no way to read it; the cache is then kept per device only).
+unsigned long long current_context_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* a = nullptr;
+    void* b = nullptr;
+    cudaDriverEntryPointQueryResult qa, qb;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &a, cudaEnableDefault, &qa) == cudaSuccess &&
+        qa == cudaDriverEntryPointSuccess &&
+        cudaGetDriverEntryPoint("cuCtxGetId", &b, cudaEnableDefault, &qb) == cudaSuccess &&
+        qb == cudaDriverEntryPointSuccess) {
+      get_current = reinterpret_cast<GetCurrent>(a);
+      get_id = reinterpret_cast<GetId>(b);
+    }
+  });
+  if (!get_current || !get_id) return 0;
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
 }  // namespace
 }  // namespace phew
 
@@ -309,17 +344,22 @@ extern "C" int phew_compare_static(const void* b, const void* c, int64_t n, int 
                          std::to_string(kStaticScratchBytes) + "; use phew_compare");
   void* scratch = nullptr;
   {
-    // First call on each device: translate the array's symbol into this
-    // device's address (with the device current).  A host-side reference to
-    // g_compare_static_scratch is only a stand-in, never a device address.
+    // First call on each device (and first call after a device reset):
+    // translate the array's symbol into this device's address (with the
+    // device current).  A host-side reference to g_compare_static_scratch is
+    // only a stand-in, never a device address.
     std::lock_guard<std::mutex> lk(g_static_mu);
-    if (g_static_scratch[dev] == nullptr) {
+    // The context is made current here (runtime calls initialise it), so
+    // its id is read after a runtime call.
+    const unsigned long long ctx = current_context_id();
+    if (g_static_scratch[dev] == nullptr || g_static_ctx[dev] != ctx) {
       void* p = nullptr;
       cudaError_t e = cudaGetSymbolAddress(&p, g_compare_static_scratch);
       if (e != cudaSuccess || p == nullptr)
         return set_error(PHEW_ERR_CUDA, std::string("phew_compare_static: cudaGetSymbolAddress: ") +
                                             cudaGetErrorString(e));
       g_static_scratch[dev] = p;
+      g_static_ctx[dev] = current_context_id();
     }
     scratch = g_static_scratch[dev];
   }

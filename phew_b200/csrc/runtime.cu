@@ -61,7 +61,10 @@ namespace {
 struct CompiledKernel {
   cudaLibrary_t library = nullptr;
   cudaKernel_t kernel = nullptr;
-  size_t smem_attr_set = 48 * 1024;  // largest dynamic smem size already allowed
+  // per device: the largest dynamic shared memory size already allowed
+  // (the attribute is set on the current device; read and written under
+  // g_cache_mu)
+  std::unordered_map<int, size_t> smem_attr_set;
 };
 
 std::mutex g_cache_mu;
@@ -192,18 +195,23 @@ int phew_launch(uint64_t handle, void** args, int nargs, unsigned grid_x, unsign
   PHEW_REQUIRE(block_x > 0 && block_y > 0 && block_z > 0 &&
                    block_x * block_y * block_z <= 1024,
                "phew_launch: block must have 1..1024 threads");
-  CompiledKernel* ck = nullptr;
+  const void* fn = nullptr;
   {
     std::lock_guard<std::mutex> lk(g_cache_mu);
     auto it = g_cache.find(handle);
     if (it == g_cache.end()) return set_error(PHEW_ERR_NOT_FOUND, "phew_launch: unknown handle");
-    ck = &it->second;  // unordered_map nodes are stable
-  }
-  const void* fn = reinterpret_cast<const void*>(ck->kernel);
-  if (dynamic_smem > ck->smem_attr_set) {
-    PHEW_CHECK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(dynamic_smem)));
-    ck->smem_attr_set = dynamic_smem;
+    CompiledKernel& ck = it->second;
+    fn = reinterpret_cast<const void*>(ck.kernel);
+    if (dynamic_smem > 48 * 1024) {
+      int dev = 0;
+      PHEW_CHECK_CUDA(cudaGetDevice(&dev));
+      size_t& allowed = ck.smem_attr_set[dev];
+      if (dynamic_smem > allowed) {
+        PHEW_CHECK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(dynamic_smem)));
+        allowed = dynamic_smem;
+      }
+    }
   }
   PHEW_CHECK_CUDA(cudaLaunchKernel(fn, dim3(grid_x, grid_y, grid_z),
                                    dim3(block_x, block_y, block_z), args, dynamic_smem,

@@ -12,7 +12,22 @@ ROOT = Path(__file__).resolve().parent.parent
 if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
 
-REFERENCE = Path(os.environ.get("PHEW_REFERENCE", "/root/reference"))
+def _reference_root() -> Path | None:
+    """The phew reference checkout: $PHEW_REFERENCE, else wherever an
+    importable ``phew`` package lives; None when neither exists (the tests
+    that drive the reference's own code are then skipped)."""
+    env = os.environ.get("PHEW_REFERENCE")
+    if env:
+        return Path(env)
+    import importlib.util
+
+    spec = importlib.util.find_spec("phew")
+    if spec is not None and spec.origin:
+        return Path(spec.origin).resolve().parent.parent
+    return None
+
+
+REFERENCE = _reference_root()
 
 
 def pytest_configure(config):
@@ -54,4 +69,4 @@ def oracle():
 
 
 def reference_importable() -> bool:
-    return (REFERENCE / "phew" / "__init__.py").exists()
+    return REFERENCE is not None and (REFERENCE / "phew" / "__init__.py").exists()

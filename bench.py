@@ -795,7 +795,12 @@ def _evaluated_flops(jdir: Path, dims, seqs) -> tuple[int, int, int]:
     return flops, evaluated, raised
 
 
-def _timed_sweep(d, groups, names, ev, store, journal, run_id, prefetch=None):
+# Groups whose host-drawn inputs are prepared ahead of the one being
+# evaluated in the e2e sweep (pinned buffers: depth + 1 sets).
+E2E_DEPTH = 2
+
+
+def _timed_sweep(d, groups, names, ev, store, journal, run_id, prefetch=None, prefetch_depth=1):
     """One sweep over `groups` inside a region bracketed by barrier +
     synchronize; returns (device seconds on this rank, wall seconds,
     library launches, clocks)."""
@@ -811,7 +816,7 @@ def _timed_sweep(d, groups, names, ev, store, journal, run_id, prefetch=None):
         n0 = _native.launch_count()
         e0.record()
         sweep.run_groups(groups, names, ev, store, d.rank, journal=journal, run_id=run_id,
-                         prefetch=prefetch)
+                         prefetch=prefetch, prefetch_depth=prefetch_depth)
         e1.record()
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
@@ -883,13 +888,13 @@ def run_sweep(args) -> None:
     # e2e: the same sweep with inputs drawn on the host and copied in
     e2e = None
     if not args.no_e2e and args.variants == "edge":
-        host_in = sweep.HostInputs(specs, SIZES, threads=_host_threads(d))
+        host_in = sweep.HostInputs(specs, SIZES, threads=_host_threads(d), slots=E2E_DEPTH + 1)
         ev2 = sweep.DeviceEvaluator(baseline, cands, host_in)
         rb0 = checker_mod.readback_bytes
         edir = _shared_dir(d, "sweep_e2e_", None)
         e2e_s, e2e_wall, _, e2e_clocks = _timed_sweep(
             d, groups, names, ev2, store, edir / f"journal.rank{d.rank}.jsonl",
-            f"sweep_e2e/{edir.name}", prefetch=host_in.prefetch)
+            f"sweep_e2e/{edir.name}", prefetch=host_in.prefetch, prefetch_depth=E2E_DEPTH)
         check_device_errors()
         host_in.close()
         ev2.release()
@@ -900,9 +905,9 @@ def run_sweep(args) -> None:
                "h2d_bytes_per_step": h2d / args.steps, "d2h_bytes_per_step": d2h / args.steps,
                "h2d_bytes_total": h2d, "d2h_bytes_total": d2h,
                "copies": "every group's 8 arguments drawn on the host (phew_fill_host, "
-                         f"{_host_threads(d)} threads per rank, one group ahead on a background "
-                         "thread, pinned) and copied host -> device; every comparison record "
-                         "copied device -> host; all inside the timed region",
+                         f"{_host_threads(d)} threads per rank, up to {E2E_DEPTH} groups ahead on a "
+                         "background thread, pinned) and copied host -> device; every comparison "
+                         "record copied device -> host; all inside the timed region",
                "clocks": e2e_clocks, "journal": str(edir)}
         del host_in
     torch.cuda.empty_cache()

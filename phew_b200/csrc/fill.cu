@@ -7,14 +7,17 @@
 // (seed, stream_id) is a pure function of those three numbers, independent
 // of the grid, the GPU and the number of GPUs in the sweep.
 //
-// Generator: SplitMix64 finalizer over (seed, stream, i) -> two 24-bit
-// uniforms -> Box-Muller for normals.
+// Generator: SplitMix64 finalizer over (seed, stream, k) -> two 24-bit
+// uniforms (u1, u2).  Normals come in Box-Muller pairs: elements 2k and
+// 2k + 1 are r cos(2 pi u2) and r sin(2 pi u2) with r = sqrt(-2 ln u1), so
+// one draw, one log and one square root serve two elements.  Uniforms use
+// the draw of their own index; one-hot rows the draw of the row index.
 //
 // phew_fill_host runs the same generator on host threads, for callers whose
 // inputs start in host memory (the sweep's end-to-end leg copies them in):
 // the same bits feed the same transforms, so host and device draws agree
-// except where the host's logf / cosf(2*pi*u) and the device's logf /
-// cospif(2u) differ in the last places of the fp32 value.
+// except where the host's logf / sincosf(2*pi*u) and the device's logf /
+// sincospif(2u) differ in the last places of the fp32 value.
 #include <math.h>
 #include <string.h>
 
@@ -47,15 +50,23 @@ template <typename T>
 __global__ void fill_kernel(T* out, int64_t n, int64_t cols, int kind, uint64_t seed,
                             uint64_t stream, float scale) {
   const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += step) {
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (kind == PHEW_FILL_NORMAL) {
+    // one Box-Muller pair (elements 2k, 2k + 1) per iteration
+    const int64_t pairs = (n + 1) / 2;
+    for (int64_t k = first; k < pairs; k += step) {
+      const uint64_t b = draw(seed, stream, static_cast<uint64_t>(k));
+      const float r = sqrtf(-2.0f * logf(u24(b))) * scale;
+      float sn, cs;
+      sincospif(2.0f * u24(b >> 32), &sn, &cs);
+      out[2 * k] = from_f32<T>(r * cs);
+      if (2 * k + 1 < n) out[2 * k + 1] = from_f32<T>(r * sn);
+    }
+    return;
+  }
+  for (int64_t i = first; i < n; i += step) {
     float v;
     switch (kind) {
-      case PHEW_FILL_NORMAL: {
-        const uint64_t b = draw(seed, stream, static_cast<uint64_t>(i));
-        const float r = sqrtf(-2.0f * logf(u24(b)));
-        v = r * cospif(2.0f * u24(b >> 32)) * scale;
-        break;
-      }
       case PHEW_FILL_UNIFORM: {
         const uint64_t b = draw(seed, stream, static_cast<uint64_t>(i));
         v = (2.0f * u24(b) - 1.0f) * scale;
@@ -111,12 +122,6 @@ inline uint16_t host_f16_bits(float v) {
 inline float host_value(int kind, int64_t i, int64_t cols, uint64_t seed, uint64_t stream,
                         float scale) {
   switch (kind) {
-    case PHEW_FILL_NORMAL: {
-      const uint64_t b = draw(seed, stream, static_cast<uint64_t>(i));
-      const float r = sqrtf(-2.0f * logf(u24(b)));
-      const float c = cosf(6.28318530717958647692f * u24(b >> 32));
-      return r * c * scale;
-    }
     case PHEW_FILL_UNIFORM: {
       const uint64_t b = draw(seed, stream, static_cast<uint64_t>(i));
       return (2.0f * u24(b) - 1.0f) * scale;
@@ -132,17 +137,37 @@ inline float host_value(int kind, int64_t i, int64_t cols, uint64_t seed, uint64
   }
 }
 
-void host_fill_range(void* out, int64_t lo, int64_t hi, int64_t cols, int dtype, int kind,
+template <typename Store>
+void host_fill_typed(Store store, int64_t lo, int64_t hi, int64_t n, int64_t cols, int kind,
                      uint64_t seed, uint64_t stream, float scale) {
+  if (kind == PHEW_FILL_NORMAL) {
+    // [lo, hi) starts on an even index (ranges are split on pair boundaries)
+    for (int64_t k = lo / 2; 2 * k < hi; ++k) {
+      const uint64_t b = draw(seed, stream, static_cast<uint64_t>(k));
+      const float r = sqrtf(-2.0f * logf(u24(b))) * scale;
+      float sn, cs;
+      sincosf(6.28318530717958647692f * u24(b >> 32), &sn, &cs);
+      store(2 * k, r * cs);
+      if (2 * k + 1 < n) store(2 * k + 1, r * sn);
+    }
+    return;
+  }
+  for (int64_t i = lo; i < hi; ++i) store(i, host_value(kind, i, cols, seed, stream, scale));
+}
+
+void host_fill_range(void* out, int64_t lo, int64_t hi, int64_t n, int64_t cols, int dtype,
+                     int kind, uint64_t seed, uint64_t stream, float scale) {
   if (dtype == PHEW_F32) {
     float* o = static_cast<float*>(out);
-    for (int64_t i = lo; i < hi; ++i) o[i] = host_value(kind, i, cols, seed, stream, scale);
+    host_fill_typed([o](int64_t i, float v) { o[i] = v; }, lo, hi, n, cols, kind, seed, stream, scale);
   } else if (dtype == PHEW_BF16) {
     uint16_t* o = static_cast<uint16_t*>(out);
-    for (int64_t i = lo; i < hi; ++i) o[i] = host_bf16_bits(host_value(kind, i, cols, seed, stream, scale));
+    host_fill_typed([o](int64_t i, float v) { o[i] = host_bf16_bits(v); }, lo, hi, n, cols, kind,
+                    seed, stream, scale);
   } else {
     uint16_t* o = static_cast<uint16_t*>(out);
-    for (int64_t i = lo; i < hi; ++i) o[i] = host_f16_bits(host_value(kind, i, cols, seed, stream, scale));
+    host_fill_typed([o](int64_t i, float v) { o[i] = host_f16_bits(v); }, lo, hi, n, cols, kind,
+                    seed, stream, scale);
   }
 }
 
@@ -164,16 +189,17 @@ extern "C" int phew_fill_host(void* out, int64_t n, int64_t cols, int dtype, int
   const int64_t max_threads = std::max<int64_t>(1, n >> 20);
   const int nt = static_cast<int>(std::min<int64_t>(threads, max_threads));
   if (nt == 1) {
-    host_fill_range(out, 0, n, cols, dtype, kind, seed, stream_id, scale);
+    host_fill_range(out, 0, n, n, cols, dtype, kind, seed, stream_id, scale);
     return PHEW_OK;
   }
   std::vector<std::thread> pool;
   pool.reserve(nt);
-  const int64_t per = (n + nt - 1) / nt;
+  // even chunk lengths: a normal pair never straddles two threads
+  const int64_t per = ((n + nt - 1) / nt + 1) & ~int64_t(1);
   for (int t = 0; t < nt; ++t) {
     const int64_t lo = t * per, hi = std::min(n, lo + per);
     if (lo >= hi) break;
-    pool.emplace_back(host_fill_range, out, lo, hi, cols, dtype, kind, seed, stream_id, scale);
+    pool.emplace_back(host_fill_range, out, lo, hi, n, cols, dtype, kind, seed, stream_id, scale);
   }
   for (auto& th : pool) th.join();
   return PHEW_OK;

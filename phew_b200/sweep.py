@@ -180,16 +180,17 @@ class HostInputs:
     scale: ``phew_fill_host`` runs the counter-based generator of
     ``phew_fill`` on host threads into pinned buffers, and every group's
     arguments are copied host -> device before the group is evaluated.
-    With ``prefetch(group)`` the next group is drawn on a background thread
-    while the device evaluates the current one (two pinned slots; a slot is
-    redrawn only after the copies out of it have finished).
+    With ``prefetch(group)`` upcoming groups are drawn on a background
+    thread, in order, while the device evaluates earlier ones (`slots`
+    pinned buffers used round robin: a prefetch depth of d needs d + 1; a
+    slot is redrawn only after the copies out of it have finished).
 
     Variants: the edge set (zeros, pm1e4, subnormal, one_hot_rows) and the
     base draw ("random"), with the arguments `DeviceInputs` gives them.
     ``h2d_bytes`` counts the bytes copied in."""
 
     def __init__(self, arg_specs: Callable[[str], list[ArgSpec]], sizes: Sequence[str],
-                 threads: int = 0) -> None:
+                 threads: int = 0, slots: int = 2) -> None:
         import threading
 
         import torch
@@ -206,9 +207,10 @@ class HostInputs:
         for z in sizes:
             for j, a in enumerate(arg_specs(z)):
                 cap[j] = max(cap[j], int(np.prod(a.shape)) * _itemsize(a.dtype))
+        self._slots = max(2, int(slots))
         self._pinned = [[torch.empty(c, dtype=torch.uint8).pin_memory() for c in cap]
-                        for _ in range(2)]
-        self._copied = [None, None]  # event: copies out of the slot have finished
+                        for _ in range(self._slots)]
+        self._copied = [None] * self._slots  # event: copies out of the slot have finished
         self._pool = None
 
     # -- host side ---------------------------------------------------------
@@ -265,7 +267,7 @@ class HostInputs:
             if key in self._pending:
                 return
             slot = self._slot
-            self._slot ^= 1
+            self._slot = (self._slot + 1) % self._slots
             self._pending[key] = (slot, self._pool.submit(self._draw, slot, *key))
 
     # -- the DeviceInputs interface ----------------------------------------
@@ -283,7 +285,7 @@ class HostInputs:
             hit = self._pending.pop(key, None)
             if hit is None:
                 slot = self._slot
-                self._slot ^= 1
+                self._slot = (self._slot + 1) % self._slots
         if hit is not None:
             slot, fut = hit
             host = fut.result()
@@ -426,6 +428,7 @@ def run_groups(
     journal: Path | None = None,
     run_id: str = "sweep",
     prefetch: Callable[[Group], None] | None = None,
+    prefetch_depth: int = 1,
 ) -> list[GroupRecord]:
     """Evaluate groups taken from one shared counter, in list order, until
     the list is exhausted.
@@ -439,30 +442,33 @@ def run_groups(
     rank: every ``*.jsonl`` beside `journal` is read) are not re-evaluated;
     each finished group is appended to `journal`.
 
-    With `prefetch`, a rank claims its next group before it evaluates the
-    current one and calls ``prefetch(next_group)`` first, so that preparing
-    the next group's inputs (a host-side draw) overlaps this group's device
-    work; each rank then holds at most one claimed group beyond the one it
-    is running."""
+    With `prefetch`, a rank keeps `prefetch_depth` groups claimed beyond the
+    one it is evaluating and calls ``prefetch(group)`` as it claims each, so
+    that preparing their inputs (a host-side draw) overlaps the device work
+    of the groups before them."""
+    from collections import deque
+
     done: dict[tuple, GroupRecord] = {}
     if journal:
         for p in sorted(Path(journal).parent.glob("*.jsonl")):
             done.update(load_groups(p))
     out: list[GroupRecord] = []
     key = f"{run_id}/next"
+    ahead = max(1, int(prefetch_depth)) if prefetch is not None else 0
 
     def claim() -> int:
-        return store.add(key, 1) - 1
+        i = store.add(key, 1) - 1
+        if prefetch is not None and i < len(groups):
+            g = groups[i]
+            if (g.seed, g.size, g.variant) not in done:
+                prefetch(g)
+        return i
 
-    i = claim()
-    while i < len(groups):
-        nxt = None
-        if prefetch is not None:
-            nxt = claim()
-            if nxt < len(groups):
-                g2 = groups[nxt]
-                if (g2.seed, g2.size, g2.variant) not in done:
-                    prefetch(g2)
+    queue = deque([claim()])
+    while queue and queue[0] < len(groups):
+        while len(queue) < 1 + ahead and queue[-1] < len(groups):
+            queue.append(claim())
+        i = queue.popleft()
         g = groups[i]
         k = (g.seed, g.size, g.variant)
         if k in done:
@@ -478,7 +484,8 @@ def run_groups(
             if journal:
                 with open(journal, "a") as f:
                     f.write(rec.to_json() + "\n")
-        i = nxt if nxt is not None else claim()
+        if not queue:
+            queue.append(claim())
     return out
 
 

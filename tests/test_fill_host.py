@@ -51,15 +51,17 @@ def _fill(lib, n, cols, dtype, kind, seed, stream, scale, threads=0):
 
 def test_normal_draws_follow_the_generator(lib):
     seed, stream = 11, 0x1234_5678_9ABC
-    got = _fill(lib, 4096, 64, 0, 0, seed, stream, 0.5)
-    for i in (0, 1, 7, 1000, 4095):
-        b = _draw(seed, stream, i)
-        want = np.sqrt(-2.0 * np.log(_u24(b))) * np.cos(2 * np.pi * _u24(b >> 32)) * 0.5
+    got = _fill(lib, 4097, 64, 0, 0, seed, stream, 0.5)
+    # Box-Muller pairs: elements 2k and 2k + 1 share draw k
+    for i in (0, 1, 7, 1000, 4095, 4096):
+        b = _draw(seed, stream, i // 2)
+        trig = np.cos if i % 2 == 0 else np.sin
+        want = np.sqrt(-2.0 * np.log(_u24(b))) * trig(2 * np.pi * _u24(b >> 32)) * 0.5
         assert abs(float(got[i]) - want) <= 2e-6 * max(1.0, abs(want)), (i, got[i], want)
 
 
 def test_thread_count_does_not_change_values(lib):
-    n = 3 * (1 << 20) + 5
+    n = 3 * (1 << 20) + 5  # odd: the last pair has one element
     a = _fill(lib, n, 4096, 2, 0, 3, 99, 1.0, threads=1)
     b = _fill(lib, n, 4096, 2, 0, 3, 99, 1.0, threads=7)
     assert np.array_equal(a.view(np.uint16), b.view(np.uint16))

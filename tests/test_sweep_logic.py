@@ -255,11 +255,11 @@ def test_two_rank_gloo_group_sweep(tmp_path, crash_rank):
         assert res["reassigned"] == len(CANDS)
 
 
-def test_prefetch_claims_one_group_ahead():
-    """With a prefetch hook a rank claims its next group before evaluating
-    the current one and hands it to the hook first; every group still runs
-    exactly once, in list order, and every prefetched group is the one the
-    rank runs next."""
+@pytest.mark.parametrize("depth", [1, 2])
+def test_prefetch_claims_groups_ahead(depth):
+    """With a prefetch hook a rank keeps `depth` groups claimed beyond the
+    one it evaluates and hands each to the hook as it claims it; every
+    group still runs exactly once, in list order."""
     from torch.distributed import HashStore
 
     cands = CANDS[:3]
@@ -274,14 +274,16 @@ def test_prefetch_claims_one_group_ahead():
     def prefetch(g):
         events.append(("prefetch", (g.seed, g.size, g.variant)))
 
-    recs = sweep.run_groups(groups, cands, evaluate, HashStore(), prefetch=prefetch)
-    assert [(r.seed, r.size, r.variant) for r in recs] == [(g.seed, g.size, g.variant) for g in groups]
-    pre = [k for e, k in events if e == "prefetch"]
-    assert pre == [(g.seed, g.size, g.variant) for g in groups[1:]]
-    # each prefetch comes before the evaluation of the group it follows
-    for i, k in enumerate(pre):
-        first_eval_of_next = events.index(("eval", k))
-        assert events.index(("prefetch", k)) < first_eval_of_next
+    recs = sweep.run_groups(groups, cands, evaluate, HashStore(), prefetch=prefetch,
+                            prefetch_depth=depth)
+    keys = [(g.seed, g.size, g.variant) for g in groups]
+    assert [(r.seed, r.size, r.variant) for r in recs] == keys
+    assert [k for e, k in events if e == "prefetch"] == keys
+    # when group n is first evaluated, groups up to n + depth were prefetched
+    for n, k in enumerate(keys):
+        first_eval = events.index(("eval", k))
+        seen = {kk for e, kk in events[:first_eval] if e == "prefetch"}
+        assert set(keys[:min(len(keys), n + depth + 1)]) <= seen
 
 
 def _prefetch_worker(rank, world, port, jdir):

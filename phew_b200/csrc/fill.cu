@@ -21,6 +21,8 @@
 #include <math.h>
 #include <string.h>
 
+#include <cmath>
+
 #include <algorithm>
 #include <thread>
 #include <vector>
@@ -155,8 +157,37 @@ void host_fill_typed(Store store, int64_t lo, int64_t hi, int64_t n, int64_t col
   for (int64_t i = lo; i < hi; ++i) store(i, host_value(kind, i, cols, seed, stream, scale));
 }
 
+// Normals scaled below the fp32 normal range (bf16 subnormals): an fp32
+// multiply with a subnormal result takes a microcode assist on x86 (about a
+// hundred cycles each), so these are scaled in double precision and rounded
+// straight onto bf16's subnormal grid (m * 2^-133, m <= 128) with integer
+// work.  (The device's fp32 products round to 2^-149 first; a value can
+// differ from it only where that first rounding decides a tie.)
+void host_fill_tiny_bf16(uint16_t* o, int64_t lo, int64_t hi, int64_t n, uint64_t seed,
+                         uint64_t stream, float scale) {
+  const double sc = static_cast<double>(scale);
+  auto tiny = [](double v) -> uint16_t {
+    const uint16_t sign = std::signbit(v) ? 0x8000u : 0u;
+    const double a = std::fabs(v);
+    if (a < 0x1p-126) return static_cast<uint16_t>(sign | static_cast<uint16_t>(std::nearbyint(a * 0x1p133)));
+    return host_bf16_bits(static_cast<float>(v));
+  };
+  for (int64_t k = lo / 2; 2 * k < hi; ++k) {
+    const uint64_t b = draw(seed, stream, static_cast<uint64_t>(k));
+    const double r = static_cast<double>(sqrtf(-2.0f * logf(u24(b)))) * sc;
+    float sn, cs;
+    sincosf(6.28318530717958647692f * u24(b >> 32), &sn, &cs);
+    o[2 * k] = tiny(r * cs);
+    if (2 * k + 1 < n) o[2 * k + 1] = tiny(r * sn);
+  }
+}
+
 void host_fill_range(void* out, int64_t lo, int64_t hi, int64_t n, int64_t cols, int dtype,
                      int kind, uint64_t seed, uint64_t stream, float scale) {
+  if (dtype == PHEW_BF16 && kind == PHEW_FILL_NORMAL && std::fabs(scale) < 0x1p-100f) {
+    host_fill_tiny_bf16(static_cast<uint16_t*>(out), lo, hi, n, seed, stream, scale);
+    return;
+  }
   if (dtype == PHEW_F32) {
     float* o = static_cast<float*>(out);
     host_fill_typed([o](int64_t i, float v) { o[i] = v; }, lo, hi, n, cols, kind, seed, stream, scale);

@@ -101,3 +101,16 @@ def test_rejects_bad_arguments(lib):
     buf = np.empty(4, np.float32)
     assert lib.phew_fill_host(ctypes.c_void_p(buf.ctypes.data), ctypes.c_int64(4), ctypes.c_int64(4), 9, 0,
                               ctypes.c_uint64(0), ctypes.c_uint64(0), ctypes.c_float(1.0), 1) == _native.PHEW_ERR_INVALID
+
+
+def test_bf16_subnormal_draws(lib):
+    """Normals scaled to bf16 subnormals (the sweep's subnormal variant) take
+    the double-precision path; they match rounding the fp32 draws scaled in
+    double, except where the order of the two roundings decides a tie."""
+    n = 1 << 20
+    f = _fill(lib, n, 4096, 0, 0, 5, 9, 1.0).astype(np.float64)
+    got = _fill(lib, n, 4096, 2, 0, 5, 9, 1e-39).view(np.uint16)
+    want = (f * np.float64(np.float32(1e-39))).astype(np.float32).astype(BF16).view(np.uint16)
+    assert np.mean(got == want) > 0.9999
+    v = got.view(BF16).astype(np.float32)
+    assert np.all(np.abs(v) < 2.0 ** -126) and np.mean(v != 0) > 0.95

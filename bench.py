@@ -70,7 +70,8 @@ def parse_args(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["phew", "reference"], default="phew")
     ap.add_argument("--workload", default="sweep", choices=["sweep", *WORKLOADS])
-    # sweep options
+    # sweep options (the workload list includes three sweep-internal kernels
+    # measured on their own: softmax, score_softmax, rms_rowmap)
     ap.add_argument("--seeds", type=int, default=5)
     ap.add_argument("--variants", choices=["edge", "reference"], default="edge")
     ap.add_argument("--tiny", action="store_true",
@@ -506,6 +507,130 @@ class RmsNorm:
 L2_BYTES = 126 * 1024 * 1024
 
 
+def _device_normal(mx, shape, dtype, seed, scale=1.0):
+    """A seeded N(0, scale^2) array drawn on the device (phew_fill)."""
+    from phew_b200 import _native
+    from phew_b200.mx.core import _stream, empty
+
+    out = empty(shape, dtype)
+    _native.call("phew_fill", ctypes.c_void_p(out._t.data_ptr()), out.size, shape[-1], out.dtype.code,
+                 0, ctypes.c_uint64(seed), ctypes.c_uint64(17), ctypes.c_float(scale), _stream())
+    return out
+
+
+class _DeviceKernelWorkload:
+    """A sweep-internal kernel measured on its own, on inputs drawn on the
+    device (these arrays are GBs: drawing them on the host would take
+    minutes).  The line carries no e2e: these are kernel measurements that
+    explain the sweep, not a user-facing call."""
+
+    unit, bound, dtype = "GB/s", "hbm", "bf16"
+    e2e = False
+
+    def host_inputs(self, seed):
+        return seed
+
+    def launch(self, i):
+        self.api(self.sets[i % len(self.sets)])
+
+    def extras(self, mx):
+        return {}
+
+    def cpu_sample(self, threads: int):
+        return None
+
+
+class Softmax(_DeviceKernelWorkload):
+    """mx.softmax over the last axis of bf16 rows 8192 wide (the plain row
+    kernel, phew_softmax): the scores of one (8, 32, 8192, 8192) head batch."""
+
+    name, metric = "softmax", "softmax_hbm_gbs"
+    kernel_regex = "softmax"
+    ROWS, COLS = 262144, 8192
+
+    def describe(self):
+        return f"mx.softmax bf16 ({self.ROWS},{self.COLS}) rows, one row kernel per step"
+
+    def work_per_step(self):
+        return 2 * self.ROWS * self.COLS * 2
+
+    def setup(self, mx, seed):
+        self.sets = [[_device_normal(mx, (self.ROWS, self.COLS), mx.bfloat16, seed, 3.0)]]
+        self.api(self.sets[0])
+
+    def api(self, inputs):
+        from phew_b200 import mx
+
+        return mx.softmax(inputs[0], axis=-1)
+
+
+class ScoreSoftmax(_DeviceKernelWorkload):
+    """The fused scale + causal-mask + softmax that mx.compile emits for the
+    unfused-attention candidates: softmax(s * 1/sqrt(128) + mask) over bf16
+    scores (8, 32, 2048, 2048) with an additive (2048, 2048) mask."""
+
+    name, metric = "score_softmax", "score_softmax_hbm_gbs"
+    kernel_regex = "softmax"
+    B, H, L = 8, 32, 2048
+
+    def describe(self):
+        return (f"mx.compile'd softmax(s/sqrt(128) + mask) bf16 s ({self.B},{self.H},{self.L},{self.L}), "
+                "mask (L, L): one fused row kernel per step")
+
+    def work_per_step(self):
+        n = self.B * self.H * self.L * self.L
+        return 2 * n * 2 + self.L * self.L * 2
+
+    def setup(self, mx, seed):
+        from phew_b200.ops import causal_mask
+
+        self.mask = causal_mask(self.L, self.L, mx.bfloat16)
+        self.sets = [[_device_normal(mx, (self.B, self.H, self.L, self.L), mx.bfloat16, seed + k, 10.0)]
+                     for k in range(2)]
+        scale = 1.0 / math.sqrt(128)
+
+        @mx.compile
+        def fn(s, m):
+            return mx.softmax(s * scale + m, axis=-1)
+
+        self.fn = fn
+        self.api(self.sets[0])
+
+    def api(self, inputs):
+        return self.fn(inputs[0], self.mask)
+
+
+class RmsRowMap(_DeviceKernelWorkload):
+    """The RMS norm of the decoder block as mx.compile runs it (reduction and
+    tail in one row kernel): x * rsqrt(mean(x*x, -1) + 1e-5) * w over bf16
+    x (8, 8192, 4096)."""
+
+    name, metric = "rms_rowmap", "rms_rowmap_hbm_gbs"
+    kernel_regex = "row_map|phew_rowmap|kernel"
+    SHAPE = (8, 8192, 4096)
+
+    def describe(self):
+        return f"mx.compile'd x*rsqrt(mean(x*x,-1)+1e-5)*w bf16 x {self.SHAPE}: one row kernel per step"
+
+    def work_per_step(self):
+        n = self.SHAPE[0] * self.SHAPE[1] * self.SHAPE[2]
+        return 2 * n * 2 + self.SHAPE[2] * 2
+
+    def setup(self, mx, seed):
+        self.w = mx.ones((self.SHAPE[2],), mx.bfloat16)
+        self.sets = [[_device_normal(mx, self.SHAPE, mx.bfloat16, seed + k)] for k in range(2)]
+
+        @mx.compile
+        def fn(x, w):
+            return x * mx.rsqrt(mx.mean(x * x, axis=-1, keepdims=True) + 1e-5) * w
+
+        self.fn = fn
+        self.api(self.sets[0])
+
+    def api(self, inputs):
+        return self.fn(inputs[0], self.w)
+
+
 WORKLOADS = {
     "gelu_chain": GeluChain,
     "attention": Attention,
@@ -513,6 +638,9 @@ WORKLOADS = {
     "rms_norm": lambda: RmsNorm(4096),
     "rms_norm_n256": lambda: RmsNorm(256),
     "rms_norm_n1024": lambda: RmsNorm(1024),
+    "softmax": Softmax,
+    "score_softmax": ScoreSoftmax,
+    "rms_rowmap": RmsRowMap,
 }
 
 
@@ -615,7 +743,7 @@ def measure_kernel(w, mx, d, steps: int, warmup: int, e2e: bool = True) -> dict:
         "gpu_launches": graph_launches,
         "clocks": clk.summary(),
     }
-    if not e2e:
+    if not e2e or not getattr(w, "e2e", True):
         return out
 
     # e2e through the public API with pinned host buffers.  Every step
@@ -700,11 +828,12 @@ def run_phew(args) -> None:
         "config": {"workload": m["workload"], "work_per_step": m["work_per_step"],
                    "l2": "inputs larger than L2 or rotated across sets larger than L2",
                    "parallelism": f"replicas x{d.world}"},
-        "roofline": m["roofline"], "e2e": m["e2e"], "gpu_launches": m["gpu_launches"],
-        "clocks": m["clocks"],
+        "roofline": m["roofline"], "gpu_launches": m["gpu_launches"], "clocks": m["clocks"],
     }
+    if "e2e" in m:
+        line["e2e"] = m["e2e"]
     line.update(w.extras(mx))
-    if d.rank == 0 and d.world == 1:
+    if d.rank == 0 and d.world == 1 and not isinstance(w, _DeviceKernelWorkload):
         threads = os.cpu_count() or 1
         v, dt, sample = w.cpu_sample(threads)
         line["cpu_baseline"] = {"value": v, "unit": w.unit, "cores": threads, "kind": "port",

@@ -228,52 +228,79 @@ __device__ __forceinline__ float softmax_exp(float d) {
   return y;
 }
 
+// Persistent row groups: CTA b handles row groups b, b + gridDim.x, ...; the
+// raw 16-byte vectors of its next row group are loaded into registers before
+// the current one's reductions, so loads stay in flight across them (a CTA
+// per row left the loads idle for the two block reductions and the store).
+// Per-element arithmetic and reduction order are those of one row per CTA.
 template <typename T, int VPT>
 __global__ void __launch_bounds__(512) softmax_vec_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t rows,
                                    int64_t cols) {
   __shared__ float smem[32 * 32];
   constexpr int E = Vec<T>::E;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.y + threadIdx.y;
-  const bool active = row < rows;
   const int64_t nvec = cols / E;
-  const T* xr = x + row * cols;
-  float v[VPT][E];
-  float m = -INFINITY;
+  const int64_t groups = (rows + blockDim.y - 1) / blockDim.y;
+  uint4 cur[VPT], nxt[VPT];
+  auto load_group = [&](int64_t g, uint4* buf) {
+    const int64_t row = g * blockDim.y + threadIdx.y;
+    const T* xr = x + row * cols;
 #pragma unroll
-  for (int j = 0; j < VPT; ++j) {
-    const int64_t vi = threadIdx.x + static_cast<int64_t>(j) * blockDim.x;
-    if (active && vi < nvec) {
-      load_vec<T>(xr + vi * E, v[j]);
-#pragma unroll
-      for (int i = 0; i < E; ++i) m = fmaxf(m, v[j][i]);
+    for (int j = 0; j < VPT; ++j) {
+      const int64_t vi = threadIdx.x + static_cast<int64_t>(j) * blockDim.x;
+      if (row < rows && vi < nvec) buf[j] = __ldg(reinterpret_cast<const uint4*>(xr + vi * E));
     }
-  }
-  m = row_allreduce<true>(m, smem);
-  float s = 0.f;
+  };
+  int64_t g = blockIdx.x;
+  if (g < groups) load_group(g, cur);
+  for (; g < groups; g += gridDim.x) {
+    const int64_t gn = g + gridDim.x;
+    if (gn < groups) load_group(gn, nxt);
+    const int64_t row = g * blockDim.y + threadIdx.y;
+    const bool active = row < rows;
+    float v[VPT][E];
+    float m = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < VPT; ++j) {
-    const int64_t vi = threadIdx.x + static_cast<int64_t>(j) * blockDim.x;
-    if (active && vi < nvec) {
+    for (int j = 0; j < VPT; ++j) {
+      const int64_t vi = threadIdx.x + static_cast<int64_t>(j) * blockDim.x;
+      if (active && vi < nvec) {
+        const T* e = reinterpret_cast<const T*>(&cur[j]);
 #pragma unroll
-      for (int i = 0; i < E; ++i) {
-        v[j][i] = softmax_exp<T>(v[j][i] - m);
-        s += v[j][i];
+        for (int i = 0; i < E; ++i) {
+          v[j][i] = to_f32(e[i]);
+          m = fmaxf(m, v[j][i]);
+        }
       }
     }
-  }
-  s = row_allreduce<false>(s, smem);
-  if (!active) return;
-  T* yr = y + row * cols;
-  const float inv = 1.0f / s;
+    m = row_allreduce<true>(m, smem);
+    float s = 0.f;
 #pragma unroll
-  for (int j = 0; j < VPT; ++j) {
-    const int64_t vi = threadIdx.x + static_cast<int64_t>(j) * blockDim.x;
-    if (vi < nvec) {
-      float o[E];
+    for (int j = 0; j < VPT; ++j) {
+      const int64_t vi = threadIdx.x + static_cast<int64_t>(j) * blockDim.x;
+      if (active && vi < nvec) {
 #pragma unroll
-      for (int i = 0; i < E; ++i) o[i] = sizeof(T) == 4 ? __fdiv_rn(v[j][i], s) : v[j][i] * inv;
-      store_vec<T>(yr + vi * E, o);
+        for (int i = 0; i < E; ++i) {
+          v[j][i] = softmax_exp<T>(v[j][i] - m);
+          s += v[j][i];
+        }
+      }
     }
+    s = row_allreduce<false>(s, smem);
+    if (active) {
+      T* yr = y + row * cols;
+      const float inv = 1.0f / s;
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int64_t vi = threadIdx.x + static_cast<int64_t>(j) * blockDim.x;
+        if (vi < nvec) {
+          float o[E];
+#pragma unroll
+          for (int i = 0; i < E; ++i) o[i] = sizeof(T) == 4 ? __fdiv_rn(v[j][i], s) : v[j][i] * inv;
+          store_vec<T>(yr + vi * E, o);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) cur[j] = nxt[j];
   }
 }
 
@@ -449,11 +476,21 @@ int softmax_typed(const void* x, void* y, int64_t rows, int64_t cols, cudaStream
   const T* xp = static_cast<const T*>(x);
   T* yp = static_cast<T*>(y);
   if (aligned && cols % E == 0 && nvec <= static_cast<int64_t>(kMaxTPR) * kMaxVPT) {
-    RowLaunch L = plan_rows(nvec);
-    dim3 block(L.tpr, L.rpb), grid(static_cast<unsigned>((rows + L.rpb - 1) / L.rpb));
+    RowLaunch L = plan_rows(nvec);  // the mapping the emitted fused softmax follows too
+    const int64_t groups = (rows + L.rpb - 1) / L.rpb;
+    dim3 block(L.tpr, L.rpb);
+    // persistent: as many CTAs as fit on the GPU at once (or one per group)
+    auto grid_for = [&](const void* fn) {
+      int per_sm = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, L.tpr * L.rpb, 0) != cudaSuccess ||
+          per_sm < 1)
+        per_sm = 1;
+      const int64_t cap = static_cast<int64_t>(sm_count_current()) * per_sm;
+      return dim3(static_cast<unsigned>(groups < cap ? groups : cap));
+    };
     switch (L.vpt) {
 #define PHEW_CASE(N) \
-  case N: softmax_vec_kernel<T, N><<<grid, block, 0, st>>>(xp, yp, rows, cols); break;
+  case N: softmax_vec_kernel<T, N><<<grid_for(reinterpret_cast<const void*>(softmax_vec_kernel<T, N>)), block, 0, st>>>(xp, yp, rows, cols); break;
       PHEW_CASE(1) PHEW_CASE(2) PHEW_CASE(3) PHEW_CASE(4)
       PHEW_CASE(5) PHEW_CASE(6) PHEW_CASE(7) PHEW_CASE(8)
 #undef PHEW_CASE

@@ -290,7 +290,15 @@ def matmul(a, b, *, row_scale: bool = False, eps: float = 1e-5) -> array:
         layout, ldb = 0, (tb.stride(-2) if K > 1 else N)
     elif (tb.stride(-2) == 1 or K == 1) and (N == 1 or tb.stride(-1) >= K):
         layout, ldb = 1, (tb.stride(-1) if N > 1 else K)
-    if layout is None or _collapse_batch(tb, batch_shape) is None:
+    if layout == 1 and _collapse_batch(tb, batch_shape) is None:
+        # A K-major B (a transposed view, e.g. k.transpose(0, 1, 3, 2) of a
+        # fused qkv projection) whose batch dims do not collapse to one
+        # stride: copy it in its own (N, K) layout -- rows of K contiguous
+        # elements, 16-byte vector copies -- and keep the K-major GEMM form,
+        # instead of materialising the transpose element by element.
+        tb = contiguous_copy(array._wrap(tb.transpose(-1, -2)))._t.transpose(-1, -2)
+        ldb = K
+    elif layout is None or _collapse_batch(tb, batch_shape) is None:
         tb = contiguous_copy(array._wrap(tb))._t
         layout, ldb = 0, N
     sb = _collapse_batch(tb, batch_shape)

@@ -61,6 +61,22 @@ def test_gemm_b_transposed_view(mx, dtype, M, N, K):
     check(got, mlx_cpu.matmul(mlx_cpu.array(a), mlx_cpu.array(bt).T), dtype)
 
 
+def test_gemm_k_transposed_from_fused_qkv(mx):
+    """q @ k^T with q, k sliced out of a fused qkv projection
+    (qkv.reshape(B, T, 3, H, D).transpose(2, 0, 3, 1, 4)): the batch dims of
+    k^T do not collapse to one stride, so k is copied in its own layout and
+    the GEMM reads it K-major."""
+    rng = np.random.default_rng(21)
+    B, T, H, D = 2, 256, 3, 128
+    qkv = _rand(rng, (B, T, 3 * H * D), BF16)
+    x = mx.array(qkv).reshape(B, T, 3, H, D).transpose(2, 0, 3, 1, 4)
+    q, k = x[0], x[1]
+    got = q @ k.transpose(0, 1, 3, 2)
+    o = mlx_cpu.array(qkv).reshape(B, T, 3, H, D).transpose(2, 0, 3, 1, 4)
+    ref = mlx_cpu.matmul(o[0], o[1].transpose(0, 1, 3, 2))
+    check(got, ref, BF16)
+
+
 def test_gemm_batched_attention_shapes(mx):
     rng = np.random.default_rng(3)
     B, H, L, D = 2, 3, 256, 128

@@ -900,33 +900,39 @@ def _sweep_setup(args):
     return dims, seqs, tag, names, variants
 
 
-def _evaluated_flops(jdir: Path, dims, seqs) -> tuple[int, int, int]:
-    """Algorithmic FLOPs of the units a sweep evaluated, from its journals:
+def _evaluated_flops(jdir: Path, dims, seqs) -> tuple[int, int, int, int]:
+    """Algorithmic work of the units a sweep evaluated, from its journals:
     every group's baseline plus each candidate that ran to a comparison
-    (a candidate that raised did no counted work).  Returns (flops,
-    evaluated candidate units, raising units)."""
+    (a candidate that raised did no counted work).  Returns (FLOPs,
+    score-tensor bytes, evaluated candidate units, raising units).
+
+    Score bytes: a graph that computes attention unfused (the baseline and
+    the candidates without the SDPA substitution, ``sdpa0`` in their names)
+    writes the (batch, heads, seq, seq) bf16 scores once (QK^T), reads them
+    and writes P once (the fused scale + mask + softmax) and reads P once
+    (P V): 8 bytes per score."""
     from phew_b200 import sweep
     from phew_b200.workloads import decoder_flops
 
-    flops = evaluated = raised = 0
+    flops = score_bytes = evaluated = raised = 0
     for p in sorted(jdir.glob("journal.rank*.jsonl")):
         for g in sweep.load_groups(p).values():
-            f = decoder_flops(seqs[g.size], dims)
-            # the baseline ran unless every unit of the group raised
+            seq = seqs[g.size]
+            f = decoder_flops(seq, dims)
+            sb = 8 * dims.batch * dims.heads * seq * seq
+            # the baseline (unfused attention) ran unless every unit of the group raised
             if any(r is None or "exception=" not in r for r in g.results.values()):
                 flops += f
-            for r in g.results.values():
+                score_bytes += sb
+            for cand, r in g.results.items():
                 if r is not None and "exception=" in r:
                     raised += 1
                 else:
                     evaluated += 1
                     flops += f
-    return flops, evaluated, raised
-
-
-# Groups whose host-drawn inputs are prepared ahead of the one being
-# evaluated in the e2e sweep (pinned buffers: depth + 1 sets).
-E2E_DEPTH = 2
+                    if "_sdpa0_" in cand:
+                        score_bytes += sb
+    return flops, score_bytes, evaluated, raised
 
 
 def _timed_sweep(d, groups, names, ev, store, journal, run_id, prefetch=None, prefetch_depth=1):
@@ -1045,10 +1051,15 @@ def run_sweep(args) -> None:
     if d.rank == 0:
         verdicts, missing = sweep.merge(jdir, shards, SIZES, variants)
         units = len(shards) * len(SIZES) * len(variants)
-        flops, evaluated, raised = _evaluated_flops(jdir, dims, seqs)
+        flops, score_bytes, evaluated, raised = _evaluated_flops(jdir, dims, seqs)
         peaks = load_peaks()
         achieved = flops / d.world / max_s / 1e12
         peak = peaks["bf16_tflops_sustained"]
+        # the time the evaluated work needs at the measured peaks: its FLOPs
+        # at the sustained GEMM rate plus the unfused graphs' score traffic
+        # at the HBM copy rate (separate kernels, so the two add)
+        flop_s = flops / d.world / (peak * 1e12)
+        byte_s = score_bytes / d.world / (peaks["hbm_gbs"] * 1e9)
         line = {
             "metric": "verified_candidates_per_s", "value": len(names) / max_s,
             "unit": "candidates/s", "n_gpus": d.world, "steps": args.steps,
@@ -1074,6 +1085,12 @@ def run_sweep(args) -> None:
                          "kernel": "the whole sweep: algorithmic FLOPs of every baseline and every "
                                    "candidate unit that ran to a comparison, per GPU-second",
                          "peak_source": peaks["source"] + " (sustained)"},
+            "roofline_model": {
+                "ideal_s": flop_s + byte_s, "frac": (flop_s + byte_s) / max_s,
+                "flop_s": flop_s, "score_bytes": score_bytes, "score_byte_s": byte_s,
+                "model": "per GPU: evaluated FLOPs / sustained bf16 peak + bytes of the "
+                         "(batch, heads, seq, seq) score tensor the unfused-attention graphs "
+                         "write and read (8 B per score) / HBM copy peak"},
             "wall_s": max_wall,
             "passed": sorted(c for c, v in verdicts.items() if v["passed"]),
             "failed": sorted(c for c, v in verdicts.items() if not v["passed"]),

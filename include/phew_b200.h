@@ -106,6 +106,31 @@ int phew_launch_count(uint64_t* out);
 /* Number of kernels currently held in the compile cache. */
 int phew_compile_cache_size(void);
 
+/* Copies the NVRTC log of the last compilation phew_compile ran on the
+ * calling thread (warnings included; a cache hit runs none and leaves it)
+ * into buf, NUL-terminated and truncated to len.  Returns the full length.
+ * The log MLX prints when a metal_kernel source fails to build
+ * (ir/importer.py:55-94 constructs the kernel; the error surfaces at
+ * optimizer.py:293-297). */
+int phew_compile_log(char* buf, size_t len);
+
+/* ---- streams and timing ------------------------------------------------- */
+
+/* A non-blocking CUDA stream (returned as void*), and its release.  The
+ * reference runs everything on MLX's default stream; a binding that does
+ * not own streams of its own gets them here. */
+int phew_stream_create(void** stream);
+int phew_stream_destroy(void* stream);
+
+/* CUDA events for device-side timing: record on a stream, then the elapsed
+ * milliseconds between two recorded events (waits for `stop`).  Replaces the
+ * perf_counter pair around mx.eval / mx.synchronize in the reference's
+ * benchmark loop (bench/harness.py:44-55). */
+int phew_event_create(void** event);
+int phew_event_record(void* event, void* stream);
+int phew_event_elapsed_ms(void* start, void* stop, float* ms);
+int phew_event_destroy(void* event);
+
 /* Test hook for the failure path of the tensor-core pipelines, not for
  * production use.  The NEXT phew_gemm or phew_sdpa call on the calling
  * thread that launches a tcgen05 kernel leaves one of its producer's tile

@@ -37,6 +37,13 @@ EXPORTED_SYMBOLS = (
     "phew_launch",
     "phew_launch_count",
     "phew_compile_cache_size",
+    "phew_compile_log",
+    "phew_stream_create",
+    "phew_stream_destroy",
+    "phew_event_create",
+    "phew_event_record",
+    "phew_event_elapsed_ms",
+    "phew_event_destroy",
     "phew_test_inject_stall",
     "phew_rms_norm",
     "phew_layer_norm",
@@ -113,6 +120,13 @@ _SIGNATURES = {
     "phew_init": ([_int], _int),
     "phew_device_query": ([_int, ctypes.POINTER(DeviceInfo)], _int),
     "phew_compile": ([ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint64)], _int),
+    "phew_compile_log": ([ctypes.c_char_p, ctypes.c_size_t], _int),
+    "phew_stream_create": ([ctypes.POINTER(ctypes.c_void_p)], _int),
+    "phew_stream_destroy": ([ctypes.c_void_p], _int),
+    "phew_event_create": ([ctypes.POINTER(ctypes.c_void_p)], _int),
+    "phew_event_record": ([ctypes.c_void_p, ctypes.c_void_p], _int),
+    "phew_event_elapsed_ms": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_float)], _int),
+    "phew_event_destroy": ([ctypes.c_void_p], _int),
     "phew_launch": (
         [ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p), _int]
         + [ctypes.c_uint] * 6

@@ -15,6 +15,7 @@
 namespace phew {
 
 static thread_local std::string g_last_error;
+static thread_local std::string g_last_compile_log;  // NVRTC log of this thread's last compilation
 
 namespace tc {
 namespace {
@@ -149,8 +150,9 @@ int phew_compile(const char* source, const char* kernel_name, uint64_t* handle) 
       "--generate-line-info",
   };
   nvrtcResult rc = nvrtcCompileProgram(prog, sizeof(opts) / sizeof(opts[0]), opts);
+  phew::g_last_compile_log = nvrtc_log(prog);
   if (rc != NVRTC_SUCCESS) {
-    std::string log = nvrtc_log(prog);
+    std::string log = phew::g_last_compile_log;
     nvrtcDestroyProgram(&prog);
     return set_error(PHEW_ERR_COMPILE, std::string("NVRTC: ") + nvrtcGetErrorString(rc) + "\n" + log);
   }
@@ -179,6 +181,57 @@ int phew_compile(const char* source, const char* kernel_name, uint64_t* handle) 
     g_cache.emplace(key, ck);
   }
   *handle = key;
+  return PHEW_OK;
+}
+
+int phew_compile_log(char* buf, size_t len) {
+  const std::string& m = phew::g_last_compile_log;
+  if (buf && len > 0) {
+    size_t k = m.size() < len - 1 ? m.size() : len - 1;
+    std::memcpy(buf, m.data(), k);
+    buf[k] = '\0';
+  }
+  return static_cast<int>(m.size());
+}
+
+int phew_stream_create(void** stream) {
+  PHEW_REQUIRE(stream != nullptr, "phew_stream_create: null output");
+  cudaStream_t s = nullptr;
+  PHEW_CHECK_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+  *stream = s;
+  return PHEW_OK;
+}
+
+int phew_stream_destroy(void* stream) {
+  PHEW_REQUIRE(stream != nullptr, "phew_stream_destroy: null stream");
+  PHEW_CHECK_CUDA(cudaStreamDestroy(static_cast<cudaStream_t>(stream)));
+  return PHEW_OK;
+}
+
+int phew_event_create(void** event) {
+  PHEW_REQUIRE(event != nullptr, "phew_event_create: null output");
+  cudaEvent_t e = nullptr;
+  PHEW_CHECK_CUDA(cudaEventCreate(&e));
+  *event = e;
+  return PHEW_OK;
+}
+
+int phew_event_record(void* event, void* stream) {
+  PHEW_REQUIRE(event != nullptr, "phew_event_record: null event");
+  PHEW_CHECK_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(event), static_cast<cudaStream_t>(stream)));
+  return PHEW_OK;
+}
+
+int phew_event_elapsed_ms(void* start, void* stop, float* ms) {
+  PHEW_REQUIRE(start && stop && ms, "phew_event_elapsed_ms: null argument");
+  PHEW_CHECK_CUDA(cudaEventSynchronize(static_cast<cudaEvent_t>(stop)));
+  PHEW_CHECK_CUDA(cudaEventElapsedTime(ms, static_cast<cudaEvent_t>(start), static_cast<cudaEvent_t>(stop)));
+  return PHEW_OK;
+}
+
+int phew_event_destroy(void* event) {
+  PHEW_REQUIRE(event != nullptr, "phew_event_destroy: null event");
+  PHEW_CHECK_CUDA(cudaEventDestroy(static_cast<cudaEvent_t>(event)));
   return PHEW_OK;
 }
 

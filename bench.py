@@ -900,11 +900,29 @@ def _sweep_setup(args):
     return dims, seqs, tag, names, variants
 
 
-def _evaluated_flops(jdir: Path, dims, seqs) -> tuple[int, int, int, int]:
-    """Algorithmic work of the units a sweep evaluated, from its journals:
-    every group's baseline plus each candidate that ran to a comparison
-    (a candidate that raised did no counted work).  Returns (FLOPs,
-    score-tensor bytes, evaluated candidate units, raising units).
+def _partial_work(cand: str, failure: str, seq: int, dims) -> tuple[int, int]:
+    """(FLOPs, score bytes) a candidate unit did before it raised.  The
+    reference's emitted sources raise at a known point: an ``rms_norm`` with
+    a full-shape weight (``rms_norm: weight shape``) in the MLP norm, after
+    the QKV projection, the attention and the output projection; an SDPA
+    output fed to a projection of the wrong width (``matmul: inner
+    dimensions differ``) at the output projection, after the QKV projection
+    and the attention.  Any other exception counts no work."""
+    T, C = dims.batch * seq, dims.dim
+    attn = 2 * 2 * dims.batch * dims.heads * seq * seq * dims.head_dim
+    sb = 8 * dims.batch * dims.heads * seq * seq if "_sdpa0_" in cand else 0
+    msg = failure.split("exception=", 1)[1]
+    if msg.startswith("rms_norm: weight shape"):
+        return 2 * T * (C * 3 * C + C * C) + attn, sb
+    if msg.startswith("matmul: inner dimensions differ"):
+        return 2 * T * C * 3 * C + attn, sb
+    return 0, 0
+
+
+def _evaluated_flops(jdir: Path, dims, seqs) -> dict:
+    """Algorithmic work of a sweep, from its journals: every group's
+    baseline, each candidate that ran to a comparison, and the part of each
+    raising candidate that ran before it raised (`_partial_work`).
 
     Score bytes: a graph that computes attention unfused (the baseline and
     the candidates without the SDPA substitution, ``sdpa0`` in their names)
@@ -914,7 +932,8 @@ def _evaluated_flops(jdir: Path, dims, seqs) -> tuple[int, int, int, int]:
     from phew_b200 import sweep
     from phew_b200.workloads import decoder_flops
 
-    flops = score_bytes = evaluated = raised = 0
+    w = {"flops": 0, "score_bytes": 0, "partial_flops": 0, "partial_score_bytes": 0,
+         "evaluated": 0, "raised": 0}
     for p in sorted(jdir.glob("journal.rank*.jsonl")):
         for g in sweep.load_groups(p).values():
             seq = seqs[g.size]
@@ -922,17 +941,20 @@ def _evaluated_flops(jdir: Path, dims, seqs) -> tuple[int, int, int, int]:
             sb = 8 * dims.batch * dims.heads * seq * seq
             # the baseline (unfused attention) ran unless every unit of the group raised
             if any(r is None or "exception=" not in r for r in g.results.values()):
-                flops += f
-                score_bytes += sb
+                w["flops"] += f
+                w["score_bytes"] += sb
             for cand, r in g.results.items():
                 if r is not None and "exception=" in r:
-                    raised += 1
+                    w["raised"] += 1
+                    pf, pb = _partial_work(cand, r, seq, dims)
+                    w["partial_flops"] += pf
+                    w["partial_score_bytes"] += pb
                 else:
-                    evaluated += 1
-                    flops += f
+                    w["evaluated"] += 1
+                    w["flops"] += f
                     if "_sdpa0_" in cand:
-                        score_bytes += sb
-    return flops, score_bytes, evaluated, raised
+                        w["score_bytes"] += sb
+    return w
 
 
 def _timed_sweep(d, groups, names, ev, store, journal, run_id, prefetch=None, prefetch_depth=1):
@@ -1051,14 +1073,18 @@ def run_sweep(args) -> None:
     if d.rank == 0:
         verdicts, missing = sweep.merge(jdir, shards, SIZES, variants)
         units = len(shards) * len(SIZES) * len(variants)
-        flops, score_bytes, evaluated, raised = _evaluated_flops(jdir, dims, seqs)
+        work = _evaluated_flops(jdir, dims, seqs)
+        flops, evaluated, raised = work["flops"], work["evaluated"], work["raised"]
         peaks = load_peaks()
         achieved = flops / d.world / max_s / 1e12
         peak = peaks["bf16_tflops_sustained"]
-        # the time the evaluated work needs at the measured peaks: its FLOPs
-        # at the sustained GEMM rate plus the unfused graphs' score traffic
-        # at the HBM copy rate (separate kernels, so the two add)
-        flop_s = flops / d.world / (peak * 1e12)
+        # the time the sweep's work needs at the measured peaks: its FLOPs
+        # (raising units' partial work included) at the sustained GEMM rate
+        # plus the unfused graphs' score traffic at the HBM copy rate
+        # (separate kernels, so the two add)
+        all_flops = flops + work["partial_flops"]
+        score_bytes = work["score_bytes"] + work["partial_score_bytes"]
+        flop_s = all_flops / d.world / (peak * 1e12)
         byte_s = score_bytes / d.world / (peaks["hbm_gbs"] * 1e9)
         line = {
             "metric": "verified_candidates_per_s", "value": len(names) / max_s,
@@ -1087,10 +1113,13 @@ def run_sweep(args) -> None:
                          "peak_source": peaks["source"] + " (sustained)"},
             "roofline_model": {
                 "ideal_s": flop_s + byte_s, "frac": (flop_s + byte_s) / max_s,
-                "flop_s": flop_s, "score_bytes": score_bytes, "score_byte_s": byte_s,
-                "model": "per GPU: evaluated FLOPs / sustained bf16 peak + bytes of the "
-                         "(batch, heads, seq, seq) score tensor the unfused-attention graphs "
-                         "write and read (8 B per score) / HBM copy peak"},
+                "flop_s": flop_s, "score_byte_s": byte_s,
+                "tflop": all_flops / 1e12, "partial_tflop": work["partial_flops"] / 1e12,
+                "score_gb": score_bytes / 1e9,
+                "model": "per GPU: FLOPs of every unit (the raising units' work up to the op "
+                         "that raised included) / sustained bf16 peak + bytes of the (batch, "
+                         "heads, seq, seq) score tensor the unfused-attention graphs write and "
+                         "read (8 B per score) / HBM copy peak"},
             "wall_s": max_wall,
             "passed": sorted(c for c, v in verdicts.items() if v["passed"]),
             "failed": sorted(c for c, v in verdicts.items() if not v["passed"]),

@@ -153,3 +153,41 @@ def test_device_inputs_are_deterministic(mx):
     for v in one_hot:
         rows = v.reshape(-1, v.shape[-1])
         assert np.all(rows.sum(-1) == 1.0)
+
+
+def test_host_drawn_inputs_reach_the_same_verdicts(mx):
+    """The e2e leg's inputs: the same groups drawn on the host
+    (phew_fill_host into pinned buffers, prefetched two groups ahead) and
+    copied in give the verdicts of the device-drawn run, and the host and
+    device draws of one group agree element for element (up to the last
+    place of the transcendental functions)."""
+    import bench
+    from torch.distributed import HashStore
+
+    from phew_b200 import sweep
+    from phew_b200.workloads import DECODER_TINY, DECODER_TINY_SEQ, decoder_block_fn
+
+    sources = _sources()
+    cands = sweep.load_candidates(sources)
+    names = sorted(sources)
+    specs = bench.decoder_specs(DECODER_TINY, DECODER_TINY_SEQ)
+    base = decoder_block_fn(mx, DECODER_TINY)
+    groups = sweep.make_groups([0, 1], ["small", "typical", "large"], sweep.VARIANT_SETS["edge"])
+    dev = sweep.run_groups(groups, names, sweep.DeviceEvaluator(base, cands, sweep.DeviceInputs(specs)),
+                           HashStore(), run_id="dev")
+    host_in = sweep.HostInputs(specs, ["small", "typical", "large"], threads=4, slots=3)
+    host = sweep.run_groups(groups, names, sweep.DeviceEvaluator(base, cands, host_in), HashStore(),
+                            run_id="host", prefetch=host_in.prefetch, prefetch_depth=2)
+    host_in.close()
+    assert len(dev) == len(host) == len(groups)
+    for a, b in zip(dev, host):
+        assert {c: r is None for c, r in a.results.items()} == {c: r is None for c, r in b.results.items()}
+    # one group's arguments, drawn both ways
+    d_args = sweep.DeviceInputs(specs).variant("pm1e4", sweep.DeviceInputs(specs).base("small", 3), "small", 3)
+    h = sweep.HostInputs(specs, ["small"], threads=2)
+    h_args = h.variant("pm1e4", h.base("small", 3), "small", 3)
+    for x, y in zip(d_args, h_args):
+        xf, yf = np.asarray(x).astype(np.float32), np.asarray(y).astype(np.float32)
+        assert np.mean(xf == yf) > 0.999
+        np.testing.assert_allclose(xf, yf, rtol=1e-2, atol=1e-2 * 1e4)
+    assert h.h2d_bytes == sum(int(np.prod(s.shape)) * 2 for s in specs("small"))

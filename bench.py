@@ -957,6 +957,11 @@ def _evaluated_flops(jdir: Path, dims, seqs) -> dict:
     return w
 
 
+# Groups whose host-drawn inputs are prepared ahead of the one being
+# evaluated in the e2e sweep (pinned buffers: depth + 1 sets).
+E2E_DEPTH = 2
+
+
 def _timed_sweep(d, groups, names, ev, store, journal, run_id, prefetch=None, prefetch_depth=1):
     """One sweep over `groups` inside a region bracketed by barrier +
     synchronize; returns (device seconds on this rank, wall seconds,

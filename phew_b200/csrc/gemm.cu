@@ -52,6 +52,7 @@ using namespace tc;
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 x 16-bit = one 128-byte swizzle row
 constexpr int kNumThreads = 192;
+constexpr int kGroupM = 8;  // row blocks per group of the tile order
 
 // A CTA computes MT x 128 rows by BN columns: MT accumulators of 128 x BN in
 // TMEM that share every B tile (MT = 2 halves the B bytes per MMA).
@@ -210,13 +211,22 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const int n_nb = (p.N + BN - 1) / BN;
   const int n_mb = (p.M + C::ROWS - 1) / C::ROWS;
   const int num_tiles = n_nb * n_mb * p.batch;
-  // Tile t -> (batch, row block, column block), column blocks fastest so
-  // that CTAs running together share their A rows in L2.
+  // Tile t -> (batch, row block, column block) in groups of kGroupM row
+  // blocks: within a group the row blocks go fastest, then the column
+  // blocks, so the ~148 tiles in flight cover about kGroupM row blocks by
+  // 148 / kGroupM column blocks and both their A rows and their B columns
+  // stay in L2 (with column blocks fastest over a wide B, every band of rows
+  // streamed all of B from HBM again).
+  const int tiles_per_batch = n_nb * n_mb;
   auto coords = [&](int t, int& bz, int& m0, int& n0) {
-    n0 = (t % n_nb) * BN;
-    const int r = t / n_nb;
-    m0 = (r % n_mb) * C::ROWS;
-    bz = r / n_mb;
+    bz = t / tiles_per_batch;
+    const int tt = t - bz * tiles_per_batch;
+    const int g = tt / (kGroupM * n_nb);
+    const int first_m = g * kGroupM;
+    const int gsize = n_mb - first_m < kGroupM ? n_mb - first_m : kGroupM;
+    const int within = tt - g * kGroupM * n_nb;
+    m0 = (first_m + within % gsize) * C::ROWS;
+    n0 = (within / gsize) * BN;
   };
   // Wave quantization: with two 128-row halves per tile (MT = 2), the last,
   // partial round of tiles runs as twice as many 128-row half tiles when they

@@ -217,10 +217,19 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   // 148 / kGroupM column blocks and both their A rows and their B columns
   // stay in L2 (with column blocks fastest over a wide B, every band of rows
   // streamed all of B from HBM again).
+  // A GEMM with few k-blocks (q @ k^T, K = 128) is bound by writing C, not
+  // by its operands: it keeps column blocks fastest, so the tiles in flight
+  // write whole rows of C together.
   const int tiles_per_batch = n_nb * n_mb;
+  const bool col_fastest = num_kb < 8;
   auto coords = [&](int t, int& bz, int& m0, int& n0) {
     bz = t / tiles_per_batch;
     const int tt = t - bz * tiles_per_batch;
+    if (col_fastest) {
+      n0 = (tt % n_nb) * BN;
+      m0 = (tt / n_nb) * C::ROWS;
+      return;
+    }
     const int g = tt / (kGroupM * n_nb);
     const int first_m = g * kGroupM;
     const int gsize = n_mb - first_m < kGroupM ? n_mb - first_m : kGroupM;

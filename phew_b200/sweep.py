@@ -183,7 +183,11 @@ class HostInputs:
     With ``prefetch(group)`` upcoming groups are drawn on a background
     thread, in order, while the device evaluates earlier ones (`slots`
     pinned buffers used round robin: a prefetch depth of d needs d + 1; a
-    slot is redrawn only after the copies out of it have finished).
+    slot is redrawn only after the copies out of it have finished).  The
+    thread that draws a group also issues its host -> device copies, on a
+    stream of their own, so they overlap the compute of the groups before
+    it; the compute stream waits for a group's copies only when it reaches
+    that group.
 
     Variants: the edge set (zeros, pm1e4, subnormal, one_hot_rows) and the
     base draw ("random"), with the arguments `DeviceInputs` gives them.
@@ -211,10 +215,16 @@ class HostInputs:
         self._pinned = [[torch.empty(c, dtype=torch.uint8).pin_memory() for c in cap]
                         for _ in range(self._slots)]
         self._copied = [None] * self._slots  # event: copies out of the slot have finished
+        self._copy_stream = torch.cuda.Stream(device=self._device)
         self._pool = None
 
     # -- host side ---------------------------------------------------------
-    def _draw(self, slot: int, seed: int, size: str, variant: str) -> list:
+    def _draw(self, slot: int, seed: int, size: str, variant: str) -> tuple:
+        """Draw one group's arguments into pinned slot `slot` and copy them
+        to the device on the copy stream.  Returns (device tensors, the
+        event that marks the copies done, bytes copied)."""
+        import torch
+
         from . import _native
         from . import dtypes as dt
 
@@ -254,7 +264,17 @@ class HostInputs:
                 kind, scale = kinds[variant]
                 fill(kind, _stream_id(variant, size, i), scale)
             out.append((buf, spec))
-        return out
+        tensors, nbytes = [], 0
+        with torch.cuda.device(self._device), torch.cuda.stream(self._copy_stream):
+            for buf, spec in out:
+                t = torch.empty(spec.shape, dtype=dt.from_any(spec.dtype).torch, device=self._device)
+                t.view(torch.uint8).view(-1).copy_(buf, non_blocking=True)
+                tensors.append(t)
+                nbytes += buf.numel()
+            done = torch.cuda.Event()
+            done.record(self._copy_stream)
+        self._copied[slot] = done  # only this slot's next draw (same thread or caller) reads it
+        return tensors, done, nbytes
 
     def prefetch(self, group: Group) -> None:
         """Start drawing `group`'s arguments on a background thread."""
@@ -277,7 +297,6 @@ class HostInputs:
     def variant(self, name: str, base_args: list, size: str, seed: int) -> list:
         import torch
 
-        from . import dtypes as dt
         from .mx.core import array
 
         key = (seed, size, name)
@@ -288,20 +307,15 @@ class HostInputs:
                 self._slot = (self._slot + 1) % self._slots
         if hit is not None:
             slot, fut = hit
-            host = fut.result()
+            tensors, done, nbytes = fut.result()
         else:
-            host = self._draw(slot, seed, size, name)
-        args = []
-        for buf, spec in host:
-            d = dt.from_any(spec.dtype)
-            t = torch.empty(spec.shape, dtype=d.torch, device=self._device)
-            t.view(torch.uint8).view(-1).copy_(buf, non_blocking=True)
-            self.h2d_bytes += buf.numel()
-            args.append(array(t))
-        ev = torch.cuda.Event()
-        ev.record()
-        self._copied[slot] = ev
-        return args
+            tensors, done, nbytes = self._draw(slot, seed, size, name)
+        cur = torch.cuda.current_stream(self._device)
+        cur.wait_event(done)
+        for t in tensors:
+            t.record_stream(cur)  # allocated on the copy stream, used on this one
+        self.h2d_bytes += nbytes
+        return [array(t) for t in tensors]
 
     def close(self) -> None:
         if self._pool is not None:

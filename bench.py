@@ -1206,12 +1206,14 @@ def _cpu_variant_inputs(specs, variant: str, seed: int, batch_rows: int, threads
     """One edge variant's arguments for the CPU sample, drawn on the host
     with numpy (independent generators per chunk, on `threads` threads):
     x keeps `batch_rows` of its batch rows, the weights are full size."""
+    import zlib
+
     import numpy as np
 
     from oracle import mlx_cpu
 
     out = []
-    ss = np.random.SeedSequence([seed, hash(variant) & 0xFFFF])
+    ss = np.random.SeedSequence([seed, zlib.crc32(variant.encode())])  # stable across processes
     for i, spec in enumerate(specs):
         shape = list(spec.shape)
         if i == 0:

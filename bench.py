@@ -540,6 +540,32 @@ class _DeviceKernelWorkload:
         return None
 
 
+class QkvProjection(_DeviceKernelWorkload):
+    """The decoder's fused QKV projection at the sweep's typical size:
+    x (8 * 2048, 4096) @ W (4096, 12288), bf16, one tcgen05 GEMM per step."""
+
+    name, metric = "qkv_proj", "gemm_tflops"
+    unit, bound = "TFLOP/s", "tensor"
+    kernel_regex = "gemm_tc"
+    profile = "gemm_tc_qkv_proj_bf16_16384x4096x12288"
+    M, K, N = 16384, 4096, 12288
+
+    def describe(self):
+        return f"x ({self.M},{self.K}) @ W ({self.K},{self.N}) bf16: one tcgen05 GEMM per step"
+
+    def work_per_step(self):
+        return 2 * self.M * self.K * self.N
+
+    def setup(self, mx, seed):
+        self.sets = [[_device_normal(mx, (self.M, self.K), mx.bfloat16, seed + k),
+                      _device_normal(mx, (self.K, self.N), mx.bfloat16, seed + 7, 1.0 / 64.0)]
+                     for k in range(2)]
+        self.api(self.sets[0])
+
+    def api(self, inputs):
+        return inputs[0] @ inputs[1]
+
+
 class Softmax(_DeviceKernelWorkload):
     """mx.softmax over the last axis of bf16 rows 8192 wide (the plain row
     kernel, phew_softmax): the scores of one (8, 32, 8192, 8192) head batch."""
@@ -638,6 +664,7 @@ WORKLOADS = {
     "rms_norm": lambda: RmsNorm(4096),
     "rms_norm_n256": lambda: RmsNorm(256),
     "rms_norm_n1024": lambda: RmsNorm(1024),
+    "qkv_proj": QkvProjection,
     "softmax": Softmax,
     "score_softmax": ScoreSoftmax,
     "rms_rowmap": RmsRowMap,

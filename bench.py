@@ -2,7 +2,8 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl phew|reference]
                     [--workload sweep|gelu_chain|attention|normed_matmul|
-                                rms_norm|rms_norm_n256|rms_norm_n1024]
+                                rms_norm|rms_norm_n256|rms_norm_n1024|qkv_proj|
+                                softmax|score_softmax|score_softmax_8k|rms_rowmap]
 
 Default workload (sweep): the verification sweep over a decoder block
 (RMSNorm -> QKV projection (4096 = 32 heads x 128) -> causal attention ->
@@ -70,8 +71,8 @@ def parse_args(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["phew", "reference"], default="phew")
     ap.add_argument("--workload", default="sweep", choices=["sweep", *WORKLOADS])
-    # sweep options (the workload list includes three sweep-internal kernels
-    # measured on their own: softmax, score_softmax, rms_rowmap)
+    # sweep options (the workload list includes sweep-internal kernels measured
+    # on their own: qkv_proj, softmax, score_softmax, score_softmax_8k, rms_rowmap)
     ap.add_argument("--seeds", type=int, default=5)
     ap.add_argument("--variants", choices=["edge", "reference"], default="edge")
     ap.add_argument("--tiny", action="store_true",
@@ -626,6 +627,14 @@ class ScoreSoftmax(_DeviceKernelWorkload):
         return self.fn(inputs[0], self.mask)
 
 
+class ScoreSoftmaxLong(ScoreSoftmax):
+    """The same fused kernel at seq 8192, where the (8192, 8192) bf16 mask
+    (134 MB) no longer fits the L2: s (1, 32, 8192, 8192)."""
+
+    name, metric = "score_softmax_8k", "score_softmax_hbm_gbs"
+    B, H, L = 1, 32, 8192
+
+
 class RmsRowMap(_DeviceKernelWorkload):
     """The RMS norm of the decoder block as mx.compile runs it (reduction and
     tail in one row kernel): x * rsqrt(mean(x*x, -1) + 1e-5) * w over bf16
@@ -666,6 +675,7 @@ WORKLOADS = {
     "rms_norm_n1024": lambda: RmsNorm(1024),
     "qkv_proj": QkvProjection,
     "softmax": Softmax,
+    "score_softmax_8k": ScoreSoftmaxLong,
     "score_softmax": ScoreSoftmax,
     "rms_rowmap": RmsRowMap,
 }

@@ -441,6 +441,27 @@ def classify_input(in_shape, out_shape) -> tuple[str, int]:
 IO_TAG = "// phew-io:"
 
 
+# A broadcast input below this size stays in the L2 (126 MB on B200) between
+# the row groups that re-read it, so its rows need no reordering.
+SHARED_ROWS_MIN_BYTES = 16 << 20
+
+
+def shared_row_groups(classes, out_shape, itemsizes) -> tuple[int, int] | None:
+    """(outer, inner) when a "suffix" input of at least SHARED_ROWS_MIN_BYTES
+    spans several rows of the output (an additive mask (L, L) under scores
+    (B, H, L, L)): the output's ``outer * inner`` rows fall into `outer`
+    groups of `inner` rows that read the same `inner` rows of that input.
+    None when no input does."""
+    cols = int(out_shape[-1])
+    n = _numel(out_shape)
+    ext = max([e for (c, e), size in zip(classes, itemsizes)
+               if c == "suffix" and e > cols and n % e == 0 and e * size >= SHARED_ROWS_MIN_BYTES]
+              or [0])
+    if not ext or n == ext:
+        return None
+    return n // ext, ext // cols
+
+
 def io_contract_line(classes, out_shape, in_shapes, it: str) -> str:
     """Machine-readable launch contract checked by the kernel factory before
     every launch, so a body specialised to traced shapes can never index
@@ -657,6 +678,21 @@ class SubgraphCUDACodegen:
         ct = CTYPE[out_dt]
         st = f"phew_st_{_suffix(out_dt)}"
         div = "__fdiv_rn(phew_sv[j][l], phew_s)" if out_dt == "float32" else "phew_sv[j][l] * phew_inv"
+        # Rows that share a large broadcast input's rows run next to one
+        # another: position p takes row (p % outer) * inner + p / outer, so
+        # the `outer` readers of one mask row are in flight together and that
+        # row is read from HBM once instead of once per head (a seq-8192
+        # mask is 134 MB, more than the L2).  Only which block takes which row
+        # changes, not any row's arithmetic.
+        groups = shared_row_groups(classes, out_shape, [ITEMSIZE[d] for d in in_dts])
+        if groups is None:
+            row_lines = [f"const {it} phew_row = ({it})blockIdx.x * blockDim.y + threadIdx.y;",
+                         "const bool phew_active = phew_row < phew_rows;"]
+        else:
+            outer, inner = groups
+            row_lines = [f"const {it} phew_pos = ({it})blockIdx.x * blockDim.y + threadIdx.y;",
+                         "const bool phew_active = phew_pos < phew_rows;",
+                         f"const {it} phew_row = (phew_pos % {outer}{u}) * {inner}{u} + phew_pos / {outer}{u};"]
         L: list[str] = []
         L.append(
             f"// elementwise prologue ({len(plan.compute_nodes)} ops, {len(external_inputs)} inputs) "
@@ -670,8 +706,7 @@ class SubgraphCUDACodegen:
             f"const {it} phew_cols = {cols}{u};",
             f"const {it} phew_rows = ({it})out0_size / phew_cols;",
             f"const {it} phew_nvec = phew_cols / {V}{u};",
-            f"const {it} phew_row = ({it})blockIdx.x * blockDim.y + threadIdx.y;",
-            "const bool phew_active = phew_row < phew_rows;",
+            *row_lines,
             f"float phew_sv[{vpt}][{V}];",
             "float phew_m = __int_as_float(0xff800000u);",
             "#pragma unroll",

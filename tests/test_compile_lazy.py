@@ -281,3 +281,46 @@ def test_row_map_needs_a_shared_full_size_input(core):
         core.trace_exit()
     i = [k for k, a in enumerate(ext_arrays) if a is m][0]
     assert core._row_map_parts(y, chain, ext_specs, ext_arrays, root, key, i) is None
+
+
+@pytest.mark.parametrize("s_shape,m_shape,groups,min_bytes", [
+    ((3, 7, 256), (7, 256), (3, 7), 0),
+    ((2, 4, 5, 64), (5, 64), (8, 5), 0),
+    ((2, 4, 5, 64), (4, 5, 64), (2, 20), 0),
+    ((3, 7, 256), (7, 256), None, 7 * 256 * 2 + 2),         # mask below the size bound
+    ((3, 7, 256), (256,), None, 0),
+    ((3, 7, 256), (3, 7, 256), None, 0),
+    ((2, 2, 2048, 4096), (2048, 4096), (4, 2048), None),    # 16 MiB mask at the default bound
+])
+def test_fused_softmax_row_order(core, monkeypatch, s_shape, m_shape, groups, min_bytes):
+    """softmax(s * c + mask) over the last axis: rows that read the same rows
+    of a large mask are given to neighbouring blocks (position p -> row
+    (p % outer) * inner + p / outer), a permutation of the rows; the source
+    compiles for sm_100a."""
+    from test_cuda_codegen import nvrtc_compile
+
+    import phew_b200.emit.cuda_codegen as cg
+    from phew_b200.emit.cuda_codegen import SubgraphCUDACodegen, classify_input, shared_row_groups
+    from phew_b200.kernel import full_source
+
+    if min_bytes is not None:
+        monkeypatch.setattr(cg, "SHARED_ROWS_MIN_BYTES", min_bytes)
+
+    s, m = _arr(core, s_shape), _arr(core, m_shape)
+    core.trace_enter()
+    try:
+        chain, ext_specs, ext_arrays, root, key = core._fused_dag(s * 0.125 + m)
+    finally:
+        core.trace_exit()
+    classes = [classify_input(tuple(x.shape), s_shape) for x in ext_specs]
+    assert shared_row_groups(classes, s_shape, [2] * len(classes)) == groups
+    tpr, rpb, vpt = core._softmax_row_plan(s_shape[-1], 2)
+    src, ins, outs = SubgraphCUDACodegen().emit_softmax(chain, ext_specs, root, tpr, rpb, vpt)
+    assert ("phew_pos" in src) == (groups is not None)
+    if groups is not None:
+        outer, inner = groups
+        rows = outer * inner
+        assert sorted((p % outer) * inner + p // outer for p in range(rows)) == list(range(rows))
+    full = full_source("k", ins, outs, src, "", [a.dtype.name for a in ext_arrays], ["bfloat16"])
+    rc, log = nvrtc_compile(full)
+    assert rc == 0, log

@@ -124,6 +124,32 @@ def test_fused_softmax_matches_materialised(mx, dtype, cols):
     _same(mx, f, s, mask)
 
 
+@pytest.mark.parametrize("s_shape,m_shape,min_bytes", [((2, 4, 33, 512), (33, 512), 0),
+                                                       ((2, 4, 5, 8192), (4, 5, 8192), 0),
+                                                       ((3, 2, 9, 40), (9, 40), 0),
+                                                       ((1, 3, 2048, 8192), (2048, 8192), None)])
+def test_fused_softmax_shared_mask_rows(mx, monkeypatch, s_shape, m_shape, min_bytes):
+    """Scores (B, H, L, cols) under a mask broadcast over the leading axes:
+    the kernel hands rows out in mask-row order (every head's row q, then
+    q + 1), with ragged last blocks; bits of materialise-then-softmax.  The
+    small cases lower the mask-size bound so they take that order too; the
+    last one (a 32 MiB mask) takes it at the default bound."""
+    import phew_b200.emit.cuda_codegen as cg
+
+    if min_bytes is not None:
+        monkeypatch.setattr(cg, "SHARED_ROWS_MIN_BYTES", min_bytes)
+    rng = np.random.default_rng(sum(s_shape))
+    s = _rand(mx, rng, s_shape, "bfloat16", 3.0)
+    m = np.triu(np.full(m_shape[-2:], -np.inf, np.float32), k=1)
+    m = np.broadcast_to(m, m_shape) + rng.standard_normal(m_shape).astype(np.float32)
+    mask = mx.array(np.ascontiguousarray(m)).astype(mx.bfloat16)
+
+    def f(s, mask):
+        return mx.softmax(s * 0.0883883 + mask, axis=-1)
+
+    _same(mx, f, s, mask)
+
+
 def test_fused_softmax_of_mixed_width_inputs_falls_back(mx):
     rng = np.random.default_rng(7)
     s = _rand(mx, rng, (4, 64), "float32")

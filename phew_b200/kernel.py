@@ -402,6 +402,11 @@ def check_io_contract(source: str, in_shapes, out_shapes, name: str = "kernel") 
             k = int(tok[len("rowlen="):])
             if not out_shapes or not out_shapes[0] or int(out_shapes[0][-1]) != k:
                 raise ValueError(f"{name}: the kernel maps rows of {k} elements, output {out_shapes}")
+        # A kernel whose row order is baked in serves exactly `rows` rows.
+        if tok.startswith("rows="):
+            k = int(tok[len("rows="):])
+            if not out_shapes or not out_shapes[0] or _numel(out_shapes[0]) != k * int(out_shapes[0][-1]):
+                raise ValueError(f"{name}: the kernel's row order covers {k} rows, output {out_shapes}")
     for tok in line:
         if tok == "idx32" and n >= 2**31 - 2**20:
             raise ValueError(f"{name}: {n} elements overflow the kernel's 32-bit indexing")

@@ -316,7 +316,7 @@ def test_fused_softmax_row_order(core, monkeypatch, s_shape, m_shape, groups, mi
     assert shared_row_groups(classes, s_shape, [2] * len(classes)) == groups
     tpr, rpb, vpt = core._softmax_row_plan(s_shape[-1], 2)
     src, ins, outs = SubgraphCUDACodegen().emit_softmax(chain, ext_specs, root, tpr, rpb, vpt)
-    assert ("phew_pos" in src) == (groups is not None)
+    assert ("phew_p % " in src) == (groups is not None)
     if groups is not None:
         outer, inner = groups
         rows = outer * inner

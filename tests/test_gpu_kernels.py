@@ -122,7 +122,7 @@ def test_binary_broadcast_and_promotion(mx):
 
 
 @pytest.mark.parametrize("dtype", ["float32", "float16", "bfloat16"])
-@pytest.mark.parametrize("rows,cols", [(256, 2048), (3, 100), (5, 8192), (2, 40000)])
+@pytest.mark.parametrize("rows,cols", [(256, 2048), (3, 100), (5, 8192), (2, 40000), (9, 8000)])
 @pytest.mark.parametrize("weighted", [True, False])
 def test_rms_norm(mx, dtype, rows, cols, weighted):
     rng = np.random.default_rng(rows * cols)
@@ -136,7 +136,7 @@ def test_rms_norm(mx, dtype, rows, cols, weighted):
 
 
 @pytest.mark.parametrize("dtype", ["float32", "bfloat16", "float16"])
-@pytest.mark.parametrize("rows,cols", [(64, 2048), (7, 33), (3, 70000), (16, 8192)])
+@pytest.mark.parametrize("rows,cols", [(64, 2048), (7, 33), (3, 70000), (16, 8192), (9, 8000)])
 def test_softmax(mx, dtype, rows, cols):
     rng = np.random.default_rng(cols)
     npd = mlx_cpu._NP[dtype]
@@ -192,7 +192,7 @@ def test_fast_path_full_size_chain_properties(mx):
 
 
 @pytest.mark.parametrize("dtype", ["float32", "float16", "bfloat16"])
-@pytest.mark.parametrize("rows,cols", [(256, 2048), (3, 100), (5, 8192), (2, 40000)])
+@pytest.mark.parametrize("rows,cols", [(256, 2048), (3, 100), (5, 8192), (2, 40000), (9, 8000)])
 @pytest.mark.parametrize("affine", ["none", "weight", "both"])
 def test_layer_norm(mx, dtype, rows, cols, affine):
     rng = np.random.default_rng(rows + cols)

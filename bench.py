@@ -598,6 +598,7 @@ class ScoreSoftmax(_DeviceKernelWorkload):
 
     name, metric = "score_softmax", "score_softmax_hbm_gbs"
     kernel_regex = "softmax"
+    profile = "fused_softmax_score_bf16_8x32x2048x2048"
     B, H, L = 8, 32, 2048
 
     def describe(self):
@@ -632,6 +633,7 @@ class ScoreSoftmaxLong(ScoreSoftmax):
     (134 MB) no longer fits the L2: s (1, 32, 8192, 8192)."""
 
     name, metric = "score_softmax_8k", "score_softmax_hbm_gbs"
+    profile = "fused_softmax_score_bf16_1x32x8192x8192"
     B, H, L = 1, 32, 8192
 
 

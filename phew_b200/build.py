@@ -1,8 +1,9 @@
 """Builds the native library ``phew_b200/libphew_b200.so`` with nvcc for sm_100a.
 
-Every ``csrc/*.cu`` file is compiled to an object under ``phew_b200/_build``
-and linked into one shared library next to this file, so the built library
-travels with the source tree.  NVRTC (used at run time for emitted fused
+Every ``csrc/*.cu`` file is compiled by nvcc, and every ``csrc/*.cpp`` file
+(host-only code) by the host C++ compiler, to an object under
+``phew_b200/_build``; the objects are linked into one shared library next to
+this file, so the built library travels with the source tree.  NVRTC (used at run time for emitted fused
 kernels) is linked dynamically from the CUDA toolkit.
 
 Usage: ``python -m phew_b200.build [--verbose-ptxas] [--force]``.
@@ -66,26 +67,43 @@ def _compile(src: Path, verbose_ptxas: bool) -> tuple[Path, str]:
     return obj, res.stderr
 
 
+def _compile_host(src: Path) -> tuple[Path, str]:
+    """Host-only C++ (no CUDA headers): the host compiler at -O3 with fused
+    multiply-adds off, so every SIMD clone of a function rounds alike, and
+    without errno from math functions, so sqrtf vectorises."""
+    obj = BUILD / (src.stem + ".o")
+    cxx = os.environ.get("CXX") or shutil.which("g++") or "c++"
+    cmd = [cxx, "-O3", "-std=c++17", "-fPIC", "-ffp-contract=off", "-fno-math-errno", "-I", str(INCLUDE),
+           "-c", str(src), "-o", str(obj)]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"{cxx} failed for {src.name}:\n{res.stdout}\n{res.stderr}")
+    return obj, res.stderr
+
+
 def _stale(sources: list[Path]) -> bool:
     if not LIB.exists():
         return True
     lib_mtime = LIB.stat().st_mtime
-    deps = sources + list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
+    deps = sources + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(INCLUDE.glob("*.h"))
     return any(p.stat().st_mtime > lib_mtime for p in deps)
 
 
 def build(force: bool = False, verbose_ptxas: bool = False, jobs: int | None = None) -> Path:
     """Compile and link the library; returns its path.  Raises on failure."""
     sources = sorted(CSRC.glob("*.cu"))
+    host_sources = sorted(CSRC.glob("*.cpp"))
     if not sources:
         raise RuntimeError("no CUDA sources under phew_b200/csrc")
-    if not force and not verbose_ptxas and not _stale(sources):
+    if not force and not verbose_ptxas and not _stale(sources + host_sources):
         return LIB
     BUILD.mkdir(exist_ok=True)
-    jobs = jobs or min(len(sources), os.cpu_count() or 4)
+    jobs = jobs or min(len(sources) + len(host_sources), os.cpu_count() or 4)
     logs = []
     with cf.ThreadPoolExecutor(max_workers=jobs) as ex:
-        results = list(ex.map(lambda s: _compile(s, verbose_ptxas), sources))
+        futs = [ex.submit(_compile, s, verbose_ptxas) for s in sources]
+        futs += [ex.submit(_compile_host, s) for s in host_sources]
+        results = [f.result() for f in futs]
     objs = [o for o, _ in results]
     logs = [log for _, log in results if log.strip()]
     cuda_lib = cuda_home() / "lib64"

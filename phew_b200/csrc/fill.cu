@@ -7,17 +7,16 @@
 // (seed, stream_id) is a pure function of those three numbers, independent
 // of the grid, the GPU and the number of GPUs in the sweep.
 //
-// Generator: SplitMix64 finalizer over (seed, stream, k) -> two 24-bit
-// uniforms (u1, u2).  Normals come in Box-Muller pairs: elements 2k and
-// 2k + 1 are r cos(2 pi u2) and r sin(2 pi u2) with r = sqrt(-2 ln u1), so
-// one draw, one log and one square root serve two elements.  Uniforms use
-// the draw of their own index; one-hot rows the draw of the row index.
+// Generator (fill_host.h): SplitMix64 finalizer over (seed, stream, k) ->
+// two 24-bit uniforms; normals in Box-Muller pairs (elements 2k and 2k + 1
+// share draw k), uniforms from the draw of their own index, one-hot rows from
+// the draw of the row index.
 //
 // phew_fill_host runs the same generator on host threads, for callers whose
 // inputs start in host memory (the sweep's end-to-end leg copies them in):
 // the same bits feed the same transforms, so host and device draws agree
-// except where the host's logf / sincosf(2*pi*u) and the device's logf /
-// sincospif(2u) differ in the last places of the fp32 value.
+// except in the last places of the fp32 value, where the host's vectorised
+// series (fill_host.cpp) and the device's logf / sincospif(2u) round apart.
 #include <math.h>
 #include <string.h>
 
@@ -28,25 +27,10 @@
 #include <vector>
 
 #include "common.cuh"
+#include "fill_host.h"
 
 namespace phew {
 namespace {
-
-__host__ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
-  z += 0x9e3779b97f4a7c15ull;
-  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
-  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
-  return z ^ (z >> 31);
-}
-
-__host__ __device__ __forceinline__ uint64_t draw(uint64_t seed, uint64_t stream, uint64_t i) {
-  return mix64(mix64(mix64(seed) ^ stream) ^ i);
-}
-
-// (0, 1] uniform with 24 bits
-__host__ __device__ __forceinline__ float u24(uint64_t bits) {
-  return (static_cast<float>(bits & 0xFFFFFFull) + 1.0f) * (1.0f / 16777216.0f);
-}
 
 template <typename T>
 __global__ void fill_kernel(T* out, int64_t n, int64_t cols, int kind, uint64_t seed,
@@ -90,37 +74,6 @@ __global__ void fill_kernel(T* out, int64_t n, int64_t cols, int kind, uint64_t 
 
 // ---- host twin ------------------------------------------------------------
 
-// fp32 -> 16-bit storage, round to nearest even (NaN kept quiet).
-inline uint16_t host_bf16_bits(float v) {
-  uint32_t u;
-  memcpy(&u, &v, 4);
-  if ((u & 0x7fffffffu) > 0x7f800000u) return static_cast<uint16_t>((u >> 16) | 0x40u);
-  u += 0x7fffu + ((u >> 16) & 1u);
-  return static_cast<uint16_t>(u >> 16);
-}
-
-inline uint16_t host_f16_bits(float v) {
-  uint32_t u;
-  memcpy(&u, &v, 4);
-  const uint32_t sign = (u >> 16) & 0x8000u;
-  const uint32_t a = u & 0x7fffffffu;
-  if (a > 0x7f800000u) return static_cast<uint16_t>(sign | 0x7e00u);  // NaN
-  if (a >= 0x477ff000u) return static_cast<uint16_t>(sign | 0x7c00u);  // rounds to inf
-  if (a < 0x38800000u) {
-    // half subnormal (or zero): value / 2^-24, rounded to nearest even
-    float f;
-    const uint32_t ab = a;
-    memcpy(&f, &ab, 4);
-    const float scaled = f * 16777216.0f;  // exact: power-of-two scale
-    float r = nearbyintf(scaled);          // current rounding mode: nearest even
-    return static_cast<uint16_t>(sign | static_cast<uint32_t>(r));
-  }
-  // normal: rebias the exponent, round the 13 dropped mantissa bits
-  uint32_t m = a + 0xc8000000u;  // exponent 127 -> 15 (subtract 112 << 23)
-  m += 0xfffu + ((m >> 13) & 1u);
-  return static_cast<uint16_t>(sign | (m >> 13));
-}
-
 inline float host_value(int kind, int64_t i, int64_t cols, uint64_t seed, uint64_t stream,
                         float scale) {
   switch (kind) {
@@ -140,65 +93,32 @@ inline float host_value(int kind, int64_t i, int64_t cols, uint64_t seed, uint64
 }
 
 template <typename Store>
-void host_fill_typed(Store store, int64_t lo, int64_t hi, int64_t n, int64_t cols, int kind,
-                     uint64_t seed, uint64_t stream, float scale) {
-  if (kind == PHEW_FILL_NORMAL) {
-    // [lo, hi) starts on an even index (ranges are split on pair boundaries)
-    for (int64_t k = lo / 2; 2 * k < hi; ++k) {
-      const uint64_t b = draw(seed, stream, static_cast<uint64_t>(k));
-      const float r = sqrtf(-2.0f * logf(u24(b))) * scale;
-      float sn, cs;
-      sincosf(6.28318530717958647692f * u24(b >> 32), &sn, &cs);
-      store(2 * k, r * cs);
-      if (2 * k + 1 < n) store(2 * k + 1, r * sn);
-    }
-    return;
-  }
+void host_fill_typed(Store store, int64_t lo, int64_t hi, int64_t cols, int kind, uint64_t seed,
+                     uint64_t stream, float scale) {
   for (int64_t i = lo; i < hi; ++i) store(i, host_value(kind, i, cols, seed, stream, scale));
-}
-
-// Normals scaled below the fp32 normal range (bf16 subnormals): an fp32
-// multiply with a subnormal result takes a microcode assist on x86 (about a
-// hundred cycles each), so these are scaled in double precision and rounded
-// straight onto bf16's subnormal grid (m * 2^-133, m <= 128) with integer
-// work.  (The device's fp32 products round to 2^-149 first; a value can
-// differ from it only where that first rounding decides a tie.)
-void host_fill_tiny_bf16(uint16_t* o, int64_t lo, int64_t hi, int64_t n, uint64_t seed,
-                         uint64_t stream, float scale) {
-  const double sc = static_cast<double>(scale);
-  auto tiny = [](double v) -> uint16_t {
-    const uint16_t sign = std::signbit(v) ? 0x8000u : 0u;
-    const double a = std::fabs(v);
-    if (a < 0x1p-126) return static_cast<uint16_t>(sign | static_cast<uint16_t>(std::nearbyint(a * 0x1p133)));
-    return host_bf16_bits(static_cast<float>(v));
-  };
-  for (int64_t k = lo / 2; 2 * k < hi; ++k) {
-    const uint64_t b = draw(seed, stream, static_cast<uint64_t>(k));
-    const double r = static_cast<double>(sqrtf(-2.0f * logf(u24(b)))) * sc;
-    float sn, cs;
-    sincosf(6.28318530717958647692f * u24(b >> 32), &sn, &cs);
-    o[2 * k] = tiny(r * cs);
-    if (2 * k + 1 < n) o[2 * k + 1] = tiny(r * sn);
-  }
 }
 
 void host_fill_range(void* out, int64_t lo, int64_t hi, int64_t n, int64_t cols, int dtype,
                      int kind, uint64_t seed, uint64_t stream, float scale) {
-  if (dtype == PHEW_BF16 && kind == PHEW_FILL_NORMAL && std::fabs(scale) < 0x1p-100f) {
-    host_fill_tiny_bf16(static_cast<uint16_t*>(out), lo, hi, n, seed, stream, scale);
+  if (kind == PHEW_FILL_NORMAL) {
+    // [lo, hi) starts on an even index (ranges are split on pair boundaries)
+    if (dtype == PHEW_BF16 && std::fabs(scale) < 0x1p-129f)
+      host_normals_tiny_bf16(static_cast<uint16_t*>(out), lo / 2, (hi + 1) / 2, n, seed, stream, scale);
+    else
+      host_normals(out, dtype, lo / 2, (hi + 1) / 2, n, seed, stream, scale);
     return;
   }
   if (dtype == PHEW_F32) {
     float* o = static_cast<float*>(out);
-    host_fill_typed([o](int64_t i, float v) { o[i] = v; }, lo, hi, n, cols, kind, seed, stream, scale);
+    host_fill_typed([o](int64_t i, float v) { o[i] = v; }, lo, hi, cols, kind, seed, stream, scale);
   } else if (dtype == PHEW_BF16) {
     uint16_t* o = static_cast<uint16_t*>(out);
-    host_fill_typed([o](int64_t i, float v) { o[i] = host_bf16_bits(v); }, lo, hi, n, cols, kind,
-                    seed, stream, scale);
+    host_fill_typed([o](int64_t i, float v) { o[i] = host_bf16_bits(v); }, lo, hi, cols, kind, seed,
+                    stream, scale);
   } else {
     uint16_t* o = static_cast<uint16_t*>(out);
-    host_fill_typed([o](int64_t i, float v) { o[i] = host_f16_bits(v); }, lo, hi, n, cols, kind,
-                    seed, stream, scale);
+    host_fill_typed([o](int64_t i, float v) { o[i] = host_f16_bits(v); }, lo, hi, cols, kind, seed,
+                    stream, scale);
   }
 }
 

@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl phew|reference]
                     [--workload sweep|gelu_chain|attention|normed_matmul|
-                                rms_norm|rms_norm_n256|rms_norm_n1024|qkv_proj|
+                                rms_norm|rms_norm_n256|rms_norm_n1024|qkv_proj|qk_scores|
                                 softmax|score_softmax|score_softmax_8k|rms_rowmap]
 
 Default workload (sweep): the verification sweep over a decoder block
@@ -72,7 +72,8 @@ def parse_args(argv=None):
     ap.add_argument("--impl", choices=["phew", "reference"], default="phew")
     ap.add_argument("--workload", default="sweep", choices=["sweep", *WORKLOADS])
     # sweep options (the workload list includes sweep-internal kernels measured
-    # on their own: qkv_proj, softmax, score_softmax, score_softmax_8k, rms_rowmap)
+    # on their own: qkv_proj, qk_scores, softmax, score_softmax, score_softmax_8k,
+    # rms_rowmap)
     ap.add_argument("--seeds", type=int, default=5)
     ap.add_argument("--variants", choices=["edge", "reference"], default="edge")
     ap.add_argument("--tiny", action="store_true",
@@ -567,6 +568,34 @@ class QkvProjection(_DeviceKernelWorkload):
         return inputs[0] @ inputs[1]
 
 
+class QkScores(_DeviceKernelWorkload):
+    """The unfused-attention candidates' score product at seq 8192:
+    q (1, 32, 8192, 128) @ k^T, bf16, a batched tcgen05 GEMM with K = 128
+    whose (1, 32, 8192, 8192) output makes it bound by HBM writes."""
+
+    name, metric = "qk_scores", "qk_scores_hbm_gbs"
+    kernel_regex = "gemm_tc"
+    profile = "gemm_tc_qk_scores_bf16_1x32x8192x8192x128"
+    B, H, L, D = 1, 32, 8192, 128
+
+    def describe(self):
+        return (f"q ({self.B},{self.H},{self.L},{self.D}) @ k^T bf16 -> ({self.B},{self.H},{self.L},{self.L}): "
+                "one batched tcgen05 GEMM per step")
+
+    def work_per_step(self):
+        # write the scores, read q and k
+        return 2 * self.B * self.H * self.L * self.L + 2 * 2 * self.B * self.H * self.L * self.D
+
+    def setup(self, mx, seed):
+        shp = (self.B, self.H, self.L, self.D)
+        self.sets = [[_device_normal(mx, shp, mx.bfloat16, seed + k),
+                      _device_normal(mx, shp, mx.bfloat16, seed + 7)] for k in range(2)]
+        self.api(self.sets[0])
+
+    def api(self, inputs):
+        return inputs[0] @ inputs[1].transpose(0, 1, 3, 2)
+
+
 class Softmax(_DeviceKernelWorkload):
     """mx.softmax over the last axis of bf16 rows 8192 wide (the plain row
     kernel, phew_softmax): the scores of one (8, 32, 8192, 8192) head batch."""
@@ -676,6 +705,7 @@ WORKLOADS = {
     "rms_norm_n256": lambda: RmsNorm(256),
     "rms_norm_n1024": lambda: RmsNorm(1024),
     "qkv_proj": QkvProjection,
+    "qk_scores": QkScores,
     "softmax": Softmax,
     "score_softmax_8k": ScoreSoftmaxLong,
     "score_softmax": ScoreSoftmax,

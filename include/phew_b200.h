@@ -302,8 +302,10 @@ int phew_fill(void* out, int64_t n, int64_t cols, int dtype, int kind, uint64_t 
  * reference's input factories draw on the host
  * (examples/rms_norm.py:27-31, verify/checker.py:246-263); a caller whose
  * inputs must start in host memory (an end-to-end sweep that copies them
- * in) draws here.  Values equal phew_fill's except where the host libm and
- * the device's logf / cospif round the fp32 value differently. */
+ * in) draws here.  Normals are computed in SIMD loops (series forms of ln
+ * and cos / sin, within 2.6e-7 relative of the exact transform), so they
+ * equal phew_fill's up to the last fp32 places, where those and the
+ * device's logf / sincospif round apart. */
 int phew_fill_host(void* out, int64_t n, int64_t cols, int dtype, int kind, uint64_t seed,
                    uint64_t stream_id, float scale, int threads);
 

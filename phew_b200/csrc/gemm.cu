@@ -56,17 +56,30 @@ constexpr int kGroupM = 8;  // row blocks per group of the tile order
 
 // A CTA computes MT x 128 rows by BN columns: MT accumulators of 128 x BN in
 // TMEM that share every B tile (MT = 2 halves the B bytes per MMA).
-template <int BN, int MT, int ACC> struct Cfg {
+//
+// BRES (resident B, for K <= BRES_KB * 64): the CTA's work is whole column
+// runs (one batch entry and column block, every row block in order); the
+// run's B block stays in shared memory and only A tiles stream through the
+// ring.  With K = 128 the output write is the whole cost, and a tile read
+// its A and B (96 KB) from the L2 for every 64 KB it wrote: the L2 carried
+// 2.7 times the DRAM bytes and bound the kernel.  Resident B reads 32 KB per
+// 64 KB written.
+template <int BN, int MT, int ACC, bool BRES = false> struct Cfg {
   static constexpr int ROWS = BM * MT;
   static constexpr int A_BYTES = ROWS * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES;
+  static constexpr int BRES_KB = 2;
+  static constexpr int BRES_BYTES = BRES ? BRES_KB * B_BYTES : 0;
+  static constexpr int STAGE_BYTES = BRES ? A_BYTES : A_BYTES + B_BYTES;
+  static constexpr int STAGES = BRES ? 6 : (200 * 1024) / STAGE_BYTES;
   // epilogue staging for TMA stores: 4 warps x 2 buffers x (32 rows x 128 B)
   static constexpr int OUT_BYTES = 4 * 2 * 32 * 128;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + OUT_BYTES + 1024 + 256;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + BRES_BYTES + OUT_BYTES + 1024 + 256;
   static constexpr int TMEM_COLS = BN * MT * ACC;
   static_assert(TMEM_COLS <= 512, "accumulators exceed TMEM");
+  static_assert(!BRES || MT == 1, "resident B walks 128-row blocks");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert((2 * STAGES + 2 * ACC + 4) * 8 <= 256, "barrier area");
 };
 
 struct Params {
@@ -190,20 +203,23 @@ __device__ __forceinline__ uint32_t pack_out(float lo, float hi, bool bf16) {
 // RS: the row-scale variant (a separate instantiation, so the plain GEMM's
 // epilogue compiles without the factor read: with it in the same body the
 // write-bound QK^T-shaped GEMM ran 50 % slower).
-template <int BN, int MT, int ACC, bool BF16, bool RS>
+template <int BN, int MT, int ACC, bool BF16, bool RS, bool BRES>
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const Params p) {
-  using C = Cfg<BN, MT, ACC>;
+  using C = Cfg<BN, MT, ACC, BRES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* out_stage = smem + C::STAGES * C::STAGE_BYTES;  // [4 warps][2][32 x 128 B]
+  uint8_t* b_res = smem + C::STAGES * C::STAGE_BYTES;  // [BRES_KB][B tile] (BRES only)
+  uint8_t* out_stage = b_res + C::BRES_BYTES;           // [4 warps][2][32 x 128 B]
   uint64_t* full = reinterpret_cast<uint64_t*>(out_stage + C::OUT_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* acc_full = empty + C::STAGES;  // [ACC]: accumulator a holds a finished tile
   uint64_t* acc_empty = acc_full + ACC;    // [ACC]: the epilogue has read accumulator a
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + ACC);
   uint64_t* drain = acc_empty + ACC + 1;   // the MMA thread's last commit (failure path)
+  uint64_t* b_full = drain + 1;            // BRES: the run's B block landed
+  uint64_t* b_empty = drain + 2;           // BRES: the run's last MMAs completed
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -258,6 +274,28 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     m0 += (u & 1) * BM;
     mt = 1;
   };
+  // The i-th item of this CTA; false past its last.  Tiles: every
+  // gridDim.x-th work item.  BRES: column runs blockIdx.x, blockIdx.x +
+  // gridDim.x, ..., each its n_mb row blocks in order, so that the CTAs
+  // walk the row blocks of neighbouring column blocks together and share
+  // their A rows through the L2.
+  const int num_runs = p.batch * n_nb;
+  auto item = [&](int i, int& bz, int& m0, int& n0, int& mt) -> bool {
+    if constexpr (BRES) {
+      const int run = blockIdx.x + (i / n_mb) * static_cast<int>(gridDim.x);
+      if (run >= num_runs) return false;
+      bz = run / n_nb;
+      n0 = (run - bz * n_nb) * BN;
+      m0 = (i % n_mb) * BM;
+      mt = 1;
+      return true;
+    } else {
+      const int t = blockIdx.x + i * static_cast<int>(gridDim.x);
+      if (t >= num_work) return false;
+      work(t, bz, m0, n0, mt);
+      return true;
+    }
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -269,6 +307,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       mbar_init(&acc_empty[a], 4);
     }
     mbar_init(drain, 1);
+    mbar_init(b_full, 1);
+    mbar_init(b_empty, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -280,16 +320,37 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
   uint32_t kg_armed = 0;  // producer: k-blocks whose loads were issued (ring positions 0..kg_armed-1)
+  uint32_t b_armed = 0;   // producer (BRES): runs whose B block load was issued
 
   if (warp == 0) {
     // ---------------- TMA producer: runs ahead across tiles ----------------
     if (lane == 0) {
       uint32_t kg = 0;  // k-blocks issued so far (ring position)
-      for (int t = blockIdx.x; t < num_work && ok; t += gridDim.x) {
+      for (int i = 0; ok; ++i) {
         int bz, m0, n0, mt;
-        work(t, bz, m0, n0, mt);  // a half tile loads the full box from its own first row
+        if (!item(i, bz, m0, n0, mt)) break;  // a half tile loads the full box from its own first row
         const int ba = p.a_batched ? bz : 0;
         const int bb = p.b_batched ? bz : 0;
+        if (BRES && i % n_mb == 0) {
+          // a new run: its B block replaces the last one once that run's MMAs are done
+          const uint32_t rk = static_cast<uint32_t>(i / n_mb);
+          if (!mbar_wait(b_empty, (rk & 1) ^ 1, p.error_flag, p.wait_ns)) {
+            ok = false;
+            break;
+          }
+          b_armed = rk + 1;
+          mbar_expect_tx(b_full, num_kb * C::B_BYTES);
+          for (int kb = 0; kb < num_kb; ++kb) {
+            uint8_t* sb = b_res + kb * C::B_BYTES;
+            if (p.b_mn_major) {
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j)
+                tma_load_3d(sb + j * (64 * BK * 2), &tmB, b_full, n0 + j * 64, kb * BK, bb);
+            } else {
+              tma_load_3d(sb, &tmB, b_full, kb * BK, n0, bb);
+            }
+          }
+        }
         for (int kb = 0; kb < num_kb; ++kb, ++kg) {
           const int s = kg % C::STAGES;
           const uint32_t ph = (kg / C::STAGES) & 1;
@@ -303,7 +364,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           uint8_t* sb = sa + C::A_BYTES;
           mbar_expect_tx(&full[s], C::STAGE_BYTES);
           tma_load_3d(sa, &tmA, &full[s], kb * BK, m0, ba);
-          if (p.b_mn_major) {
+          if (BRES) {
+            // B is resident for the run
+          } else if (p.b_mn_major) {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
               tma_load_3d(sb + j * (64 * BK * 2), &tmB, &full[s], n0 + j * 64, kb * BK, bb);
@@ -319,9 +382,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       constexpr uint32_t idesc = instr_desc_f16(BF16 ? 1 : 0, 0, BM, BN);
       const uint32_t idesc_b = p.b_mn_major ? instr_desc_f16(BF16 ? 1 : 0, 1, BM, BN) : idesc;
       uint32_t kg = 0, it = 0;
-      for (int t = blockIdx.x; t < num_work && ok; t += gridDim.x, ++it) {
+      for (int i = 0; ok; ++i, ++it) {
         int bz, m0, n0, mt;
-        work(t, bz, m0, n0, mt);
+        if (!item(i, bz, m0, n0, mt)) break;
+        if (BRES && i % n_mb == 0) {
+          // the run's B block
+          if (!mbar_wait(b_full, static_cast<uint32_t>(i / n_mb) & 1, p.error_flag, p.wait_ns)) {
+            ok = false;
+            break;
+          }
+        }
         const int a = it % ACC;
         // accumulator a is free once the epilogue has read the tile before
         if (!mbar_wait(&acc_empty[a], ((it / ACC) & 1) ^ 1, p.error_flag, p.wait_ns)) {
@@ -339,7 +409,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
-          const uint32_t sb = sa + C::A_BYTES;
+          const uint32_t sb = BRES ? smem_u32(b_res + kb * C::B_BYTES) : sa + C::A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint64_t bd = p.b_mn_major ? smem_desc(sb + kk * (16 * 128), 64 * BK * 2, 1024)
@@ -355,6 +425,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           commit(&empty[s]);
         }
         if (ok) commit(&acc_full[a]);
+        // the run's last tile: its B block may be replaced once these MMAs are done
+        if (ok && BRES && i % n_mb == n_mb - 1) commit(b_empty);
       }
     }
   } else {
@@ -365,9 +437,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // (once, before the first epilogue reads them) for it to complete.
     bool rows_ready = !RS;
     uint32_t it = 0, out_idx = 0;
-    for (int t = blockIdx.x; t < num_work && ok; t += gridDim.x, ++it) {
+    for (int i = 0; ok; ++i, ++it) {
       int bz, m0, n0, mt;
-      work(t, bz, m0, n0, mt);
+      if (!item(i, bz, m0, n0, mt)) break;
       const int a = it % ACC;
       if (ok && !mbar_wait(&acc_full[a], (it / ACC) & 1, p.error_flag, p.wait_ns)) ok = false;
       if (!ok) break;
@@ -484,6 +556,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         if (static_cast<int>(i) == p.withhold) continue;
         mbar_wait(&full[i % C::STAGES], (i / C::STAGES) & 1, nullptr, p.wait_ns);
       }
+      // the last B block load (a run's load is issued only after the one before was consumed)
+      if (BRES && b_armed > 0) mbar_wait(b_full, (b_armed - 1) & 1, nullptr, p.wait_ns);
     } else if (warp == 1 && lane == 0) {
       commit(drain);
       mbar_wait(drain, 0, nullptr, p.wait_ns);
@@ -629,11 +703,32 @@ int launch_tc(const void* A, const void* B, const Params& p, long long lda, long
       make_map(&tc, p.C, p.out_dtype == PHEW_BF16, p.N, p.M, p.batch, p.ldc * 2, cbs * 2, 64, 32) != PHEW_OK)
     q.tma_store = 0;
   if (!q.tma_store) tc = ta;  // unused
+  if constexpr (MT == 1) {
+    // K <= 128, enough row blocks per run to amortise loading B once, and
+    // enough runs to keep every SM busy: resident B, one CTA per column run
+    // at a time
+    const int num_kb = (p.K + BK - 1) / BK;
+    const long long n_mb = (p.M + BM - 1) / BM;
+    const long long n_runs = static_cast<long long>((p.N + BN - 1) / BN) * p.batch;
+    using CR = Cfg<BN, MT, ACC, true>;
+    if (!q.row_scale && num_kb <= CR::BRES_KB && n_mb >= 8 && n_runs >= 2LL * sm_count() &&
+        n_runs * n_mb < (1LL << 31)) {
+      static bool attr_res = false;
+      if (!attr_res) {
+        PHEW_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, MT, ACC, BF16, false, true>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, CR::SMEM));
+        attr_res = true;
+      }
+      const unsigned grid = static_cast<unsigned>(sm_count());
+      gemm_tc_kernel<BN, MT, ACC, BF16, false, true><<<grid, kNumThreads, CR::SMEM, st>>>(ta, tb, tc, q);
+      return launch_status("gemm_tc_kernel");
+    }
+  }
   static bool attr_set = false;
   if (!attr_set) {
-    PHEW_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, MT, ACC, BF16, false>,
+    PHEW_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, MT, ACC, BF16, false, false>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    PHEW_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, MT, ACC, BF16, true>,
+    PHEW_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, MT, ACC, BF16, true, false>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr_set = true;
   }
@@ -653,10 +748,10 @@ int launch_tc(const void* A, const void* B, const Params& p, long long lda, long
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    PHEW_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, MT, ACC, BF16, true>, ta, tb, tc, q));
+    PHEW_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, MT, ACC, BF16, true, false>, ta, tb, tc, q));
     return launch_status("gemm_tc_kernel");
   }
-  gemm_tc_kernel<BN, MT, ACC, BF16, false><<<grid, kNumThreads, C::SMEM, st>>>(ta, tb, tc, q);
+  gemm_tc_kernel<BN, MT, ACC, BF16, false, false><<<grid, kNumThreads, C::SMEM, st>>>(ta, tb, tc, q);
   return launch_status("gemm_tc_kernel");
 }
 

@@ -90,6 +90,29 @@ def test_gemm_batched_attention_shapes(mx):
     check(o, mlx_cpu.matmul(mlx_cpu.array(p), mlx_cpu.array(v)), BF16)
 
 
+@pytest.mark.parametrize("dtype", [BF16, np.float16])
+@pytest.mark.parametrize("batch,M,N,K,kmajor", [(80, 1024, 1024, 128, True),    # q @ k^T, as attention
+                                                (40, 1100, 2000, 64, False),    # ragged edges, B row-major
+                                                (300, 1024, 300, 96, True),     # K tail, 2 column blocks
+                                                (400, 1024, 128, 128, False)])  # 128-column tiles
+def test_gemm_resident_b(mx, dtype, batch, M, N, K, kmajor):
+    """K <= 128 with many column runs: each CTA keeps a run's B block in
+    shared memory and walks the run's row blocks (checked on a sample of
+    batch entries, the first and last among them)."""
+    rng = np.random.default_rng(batch + M + K)
+    a = _rand(rng, (batch, M, K), dtype)
+    if kmajor:
+        bt = _rand(rng, (batch, N, K), dtype, 1 / np.sqrt(K))
+        got = mx.array(a) @ mx.array(bt).transpose(0, 2, 1)
+    else:
+        b = _rand(rng, (batch, K, N), dtype, 1 / np.sqrt(K))
+        got = mx.array(a) @ mx.array(b)
+    g = np.asarray(got)
+    for i in sorted({0, 1, batch // 3, batch // 2 + 1, batch - 2, batch - 1}):
+        bi = bt[i].T if kmajor else b[i]
+        check(g[i], mlx_cpu.matmul(mlx_cpu.array(a[i]), mlx_cpu.array(np.ascontiguousarray(bi))), dtype)
+
+
 def test_gemm_broadcast_weight(mx):
     rng = np.random.default_rng(4)
     x = _rand(rng, (3, 100, 256), BF16)

@@ -81,8 +81,9 @@ def parse_args(argv=None):
     ap.add_argument("--journal-dir", default=None)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-configs", action="store_true")
-    ap.add_argument("--cpu-units", type=int, default=3,
-                    help="units of the CPU subset timed for cpu_baseline")
+    ap.add_argument("--cpu-units", type=int, default=32,
+                    help="units of the CPU subset timed for cpu_baseline (32: two variants x "
+                         "16 candidates, 10-20 s of CPU work on a 16-core host)")
     return ap.parse_args(argv)
 
 

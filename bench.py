@@ -597,6 +597,15 @@ class QkScores(_DeviceKernelWorkload):
         return inputs[0] @ inputs[1].transpose(0, 1, 3, 2)
 
 
+class QkScoresFull(QkScores):
+    """The same product at the sweep's full batch: q (8, 32, 8192, 128),
+    34 GB of scores per launch."""
+
+    name, metric = "qk_scores_b8", "qk_scores_hbm_gbs"
+    profile = None
+    B = 8
+
+
 class Softmax(_DeviceKernelWorkload):
     """mx.softmax over the last axis of bf16 rows 8192 wide (the plain row
     kernel, phew_softmax): the scores of one (8, 32, 8192, 8192) head batch."""
@@ -707,6 +716,7 @@ WORKLOADS = {
     "rms_norm_n1024": lambda: RmsNorm(1024),
     "qkv_proj": QkvProjection,
     "qk_scores": QkScores,
+    "qk_scores_b8": QkScoresFull,
     "softmax": Softmax,
     "score_softmax_8k": ScoreSoftmaxLong,
     "score_softmax": ScoreSoftmax,

@@ -242,6 +242,22 @@ int phew_gemm(const void* A, const void* B, void* C, int64_t M, int64_t N, int64
               int64_t stride_b, int64_t stride_c, int b_layout, int in_dtype, int out_dtype,
               int row_scale, float eps, int* error_flag, void* stream);
 
+/* phew_gemm over two batch axes with strides of their own: batch entry
+ * (o, i), o < batch_outer, i < batch_inner, reads A at
+ * o * stride_a_outer + i * stride_a_inner (elements) and B likewise, and
+ * writes C at (o * batch_inner + i) * stride_c.  The attention operands that
+ * an unfused candidate slices out of a fused qkv projection,
+ * qkv.reshape(B, T, 3, H, D).transpose(2, 0, 3, 1, 4), are such views (the
+ * batch stride of q over heads is D, over the batch T * 3 * H * D): the GEMM
+ * reads them in place (4-D TMA maps) instead of after a copy.  An operand is
+ * batched over both axes (both strides non-zero) or over neither (both 0).
+ * No row scale.  Replaces the same `a @ b` call sites as phew_gemm. */
+int phew_gemm_batched2(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                       int64_t batch_outer, int64_t batch_inner, int64_t lda, int64_t ldb,
+                       int64_t ldc, int64_t stride_a_outer, int64_t stride_a_inner,
+                       int64_t stride_b_outer, int64_t stride_b_inner, int64_t stride_c,
+                       int b_layout, int in_dtype, int out_dtype, int* error_flag, void* stream);
+
 /* ---- attention --------------------------------------------------------- */
 
 /* 1 when phew_sdpa's tensor-core kernel handles this shape/dtype

@@ -57,6 +57,7 @@ EXPORTED_SYMBOLS = (
     "phew_copy_strided",
     "phew_l2_flush",
     "phew_gemm",
+    "phew_gemm_batched2",
     "phew_sdpa_supported",
     "phew_sdpa",
     "phew_fill",
@@ -156,6 +157,10 @@ _SIGNATURES = {
     "phew_l2_flush": ([_vp, ctypes.c_size_t, _vp], _int),
     "phew_gemm": (
         [_vp, _vp, _vp] + [_i64] * 10 + [_int, _int, _int, _int, ctypes.c_float, _vp, _vp],
+        _int,
+    ),
+    "phew_gemm_batched2": (
+        [_vp, _vp, _vp] + [_i64] * 13 + [_int, _int, _int, _vp, _vp],
         _int,
     ),
     "phew_sdpa_supported": ([_i64, _i64, _int], _int),

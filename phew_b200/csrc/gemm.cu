@@ -86,6 +86,12 @@ struct Params {
   int M, N, K;
   int b_mn_major;  // 1: B is [K, N] (N contiguous)
   int batch;
+  // Batch entry bz of A / B is (bz / batch_inner, bz % batch_inner) of two
+  // batch axes with their own strides (e.g. (batch, head) of q sliced out of
+  // a fused qkv projection): the operand maps are 4-D, [K or N, rows, inner,
+  // outer].  One strided batch axis: batch_inner = 1.
+  int batch_inner;
+  long long sa_inner, sb_inner;  // strides (elements) of the inner batch axis of A / B
   int a_batched, b_batched;
   void* C;
   long long ldc;
@@ -329,8 +335,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       for (int i = 0; ok; ++i) {
         int bz, m0, n0, mt;
         if (!item(i, bz, m0, n0, mt)) break;  // a half tile loads the full box from its own first row
-        const int ba = p.a_batched ? bz : 0;
-        const int bb = p.b_batched ? bz : 0;
+        const int bi = bz % p.batch_inner, bo = bz / p.batch_inner;
+        const int ba_i = p.a_batched ? bi : 0, ba_o = p.a_batched ? bo : 0;
+        const int bb_i = p.b_batched ? bi : 0, bb_o = p.b_batched ? bo : 0;
         if (BRES && i % n_mb == 0) {
           // a new run: its B block replaces the last one once that run's MMAs are done
           const uint32_t rk = static_cast<uint32_t>(i / n_mb);
@@ -345,9 +352,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             if (p.b_mn_major) {
 #pragma unroll
               for (int j = 0; j < BN / 64; ++j)
-                tma_load_3d(sb + j * (64 * BK * 2), &tmB, b_full, n0 + j * 64, kb * BK, bb);
+                tma_load_4d(sb + j * (64 * BK * 2), &tmB, b_full, n0 + j * 64, kb * BK, bb_i, bb_o);
             } else {
-              tma_load_3d(sb, &tmB, b_full, kb * BK, n0, bb);
+              tma_load_4d(sb, &tmB, b_full, kb * BK, n0, bb_i, bb_o);
             }
           }
         }
@@ -363,15 +370,15 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           uint8_t* sa = smem + s * C::STAGE_BYTES;
           uint8_t* sb = sa + C::A_BYTES;
           mbar_expect_tx(&full[s], C::STAGE_BYTES);
-          tma_load_3d(sa, &tmA, &full[s], kb * BK, m0, ba);
+          tma_load_4d(sa, &tmA, &full[s], kb * BK, m0, ba_i, ba_o);
           if (BRES) {
             // B is resident for the run
           } else if (p.b_mn_major) {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
-              tma_load_3d(sb + j * (64 * BK * 2), &tmB, &full[s], n0 + j * 64, kb * BK, bb);
+              tma_load_4d(sb + j * (64 * BK * 2), &tmB, &full[s], n0 + j * 64, kb * BK, bb_i, bb_o);
           } else {
-            tma_load_3d(sb, &tmB, &full[s], kb * BK, n0, bb);
+            tma_load_4d(sb, &tmB, &full[s], kb * BK, n0, bb_i, bb_o);
           }
         }
       }
@@ -575,14 +582,15 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 // not multiples of 16 bytes): 16 x 16 output tiles, fp32 accumulation.
 template <typename T>
 __global__ void gemm_simt_kernel(const T* A, const T* B, Params p, long long lda, long long ldb,
-                                 long long sa, long long sb) {
+                                 long long sa, long long sb, long long sa_in, long long sb_in) {
   __shared__ float ta[16][17];
   __shared__ float tb[16][17];
   const int bz = blockIdx.z;
+  const int bi = bz % p.batch_inner, bo = bz / p.batch_inner;
   const int row = blockIdx.y * 16 + threadIdx.y;
   const int col = blockIdx.x * 16 + threadIdx.x;
-  const T* Ab = A + (p.a_batched ? bz * sa : 0);
-  const T* Bb = B + (p.b_batched ? bz * sb : 0);
+  const T* Ab = A + (p.a_batched ? bo * sa + bi * sa_in : 0);
+  const T* Bb = B + (p.b_batched ? bo * sb + bi * sb_in : 0);
   float acc = 0.f;
   for (int k0 = 0; k0 < p.K; k0 += 16) {
     const int ka = k0 + threadIdx.x, kb = k0 + threadIdx.y;
@@ -617,6 +625,18 @@ int make_map(CUtensorMap* tm, const void* base, bool bf16, uint64_t d0, uint64_t
   const uint64_t strides[2] = {s1_bytes, s2_bytes};
   const uint32_t box[3] = {b0, b1, 1};
   return make_map_16bit(tm, base, bf16, 3, dims, strides, box);
+}
+
+// An operand [outer][inner][rows][cols] of 16-bit elements: cols contiguous,
+// rows `ld` apart, the two batch axes their own strides (elements).
+int make_operand_map(CUtensorMap* tm, const void* base, bool bf16, uint64_t cols, uint64_t rows,
+                     uint64_t inner, uint64_t outer, long long ld, long long s_inner, long long s_outer,
+                     uint32_t b0, uint32_t b1) {
+  const uint64_t dims[4] = {cols, rows, inner, outer};
+  const uint64_t strides[3] = {static_cast<uint64_t>(ld) * 2, static_cast<uint64_t>(s_inner) * 2,
+                               static_cast<uint64_t>(s_outer) * 2};
+  const uint32_t box[4] = {b0, b1, 1, 1};
+  return make_map_16bit(tm, base, bf16, 4, dims, strides, box);
 }
 
 // A memory pool per device for the row factors that keeps what it has
@@ -684,13 +704,21 @@ int launch_tc(const void* A, const void* B, const Params& p, long long lda, long
               long long sa, long long sb, cudaStream_t st) {
   using C = Cfg<BN, MT, ACC>;
   CUtensorMap ta, tb;
-  const uint64_t nba = p.a_batched ? p.batch : 1, nbb = p.b_batched ? p.batch : 1;
-  int s = make_map(&ta, A, BF16, p.K, p.M, nba, lda * 2, (p.a_batched ? sa : (long long)p.M * lda) * 2, BK, C::ROWS);
+  // [outer][inner][rows][cols] views; an axis of extent 1 gets the stride of
+  // the whole matrix (any multiple of 16 bytes describes it)
+  const uint64_t bi = static_cast<uint64_t>(p.batch_inner), bo = static_cast<uint64_t>(p.batch / p.batch_inner);
+  const long long a_mat = static_cast<long long>(p.M) * lda;
+  const long long b_mat = static_cast<long long>(p.b_mn_major ? p.K : p.N) * ldb;
+  const bool a_in = p.a_batched && bi > 1, b_in = p.b_batched && bi > 1;
+  int s = make_operand_map(&ta, A, BF16, p.K, p.M, a_in ? bi : 1, p.a_batched ? bo : 1, lda,
+                           a_in ? p.sa_inner : a_mat, p.a_batched ? sa : a_mat, BK, C::ROWS);
   if (s) return s;
   if (p.b_mn_major)
-    s = make_map(&tb, B, BF16, p.N, p.K, nbb, ldb * 2, (p.b_batched ? sb : (long long)p.K * ldb) * 2, 64, BK);
+    s = make_operand_map(&tb, B, BF16, p.N, p.K, b_in ? bi : 1, p.b_batched ? bo : 1, ldb,
+                         b_in ? p.sb_inner : b_mat, p.b_batched ? sb : b_mat, 64, BK);
   else
-    s = make_map(&tb, B, BF16, p.K, p.N, nbb, ldb * 2, (p.b_batched ? sb : (long long)p.N * ldb) * 2, BK, BN);
+    s = make_operand_map(&tb, B, BF16, p.K, p.N, b_in ? bi : 1, p.b_batched ? bo : 1, ldb,
+                         b_in ? p.sb_inner : b_mat, p.b_batched ? sb : b_mat, BK, BN);
   if (s) return s;
   // C through TMA stores when it is 16-bit and its layout is describable
   // (16-byte aligned base and row/batch strides); otherwise direct stores.
@@ -761,10 +789,12 @@ int gemm_dispatch(const void* A, const void* B, const Params& p, int64_t lda, in
 // The tensor-core kernels take 16-bit operands whose bases and row / batch
 // strides are 16-byte aligned (TMA); anything else goes to the SIMT kernel.
 inline bool uses_tensor_cores(const void* A, const void* B, int64_t lda, int64_t ldb, int64_t stride_a,
-                              int64_t stride_b, int64_t K, int in_dtype) {
+                              int64_t stride_b, int64_t K, int in_dtype, int64_t sa_inner = 0,
+                              int64_t sb_inner = 0) {
   return in_dtype != PHEW_F32 && K > 0 &&
          ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) == 0 && (lda * 2) % 16 == 0 &&
-         (ldb * 2) % 16 == 0 && (stride_a * 2) % 16 == 0 && (stride_b * 2) % 16 == 0;
+         (ldb * 2) % 16 == 0 && (stride_a * 2) % 16 == 0 && (stride_b * 2) % 16 == 0 &&
+         (sa_inner * 2) % 16 == 0 && (sb_inner * 2) % 16 == 0;
 }
 
 }  // namespace gemm
@@ -773,12 +803,17 @@ inline bool uses_tensor_cores(const void* A, const void* B, int64_t lda, int64_t
 using namespace phew;
 using namespace phew::gemm;
 
-extern "C" int phew_gemm(const void* A, const void* B, void* Cout, int64_t M, int64_t N, int64_t K,
-                         int64_t batch, int64_t lda, int64_t ldb, int64_t ldc, int64_t stride_a,
-                         int64_t stride_b, int64_t stride_c, int b_layout, int in_dtype,
-                         int out_dtype, int row_scale, float eps, int* error_flag, void* stream) {
+namespace {
+int gemm_entry(const void* A, const void* B, void* Cout, int64_t M, int64_t N, int64_t K, int64_t batch,
+               int64_t batch_inner, int64_t lda, int64_t ldb, int64_t ldc, int64_t stride_a, int64_t stride_a_inner,
+               int64_t stride_b, int64_t stride_b_inner, int64_t stride_c, int b_layout, int in_dtype,
+               int out_dtype, int row_scale, float eps, int* error_flag, void* stream) {
   PHEW_REQUIRE(A && B && Cout, "phew_gemm: null operand");
   PHEW_REQUIRE(M >= 0 && N >= 0 && K >= 0 && batch >= 1, "phew_gemm: bad shape");
+  PHEW_REQUIRE(batch_inner >= 1 && batch % batch_inner == 0, "phew_gemm: batch_inner must divide batch");
+  PHEW_REQUIRE(batch_inner == 1 || row_scale == 0, "phew_gemm: the row scale takes one batch axis");
+  PHEW_REQUIRE(batch_inner == 1 || ((stride_a == 0) == (stride_a_inner == 0) && (stride_b == 0) == (stride_b_inner == 0)),
+               "phew_gemm: an operand is batched over both batch axes or over neither");
   PHEW_REQUIRE(in_dtype == PHEW_BF16 || in_dtype == PHEW_F16 || in_dtype == PHEW_F32,
                "phew_gemm: bad input dtype");
   PHEW_REQUIRE(out_dtype == PHEW_BF16 || out_dtype == PHEW_F16 || out_dtype == PHEW_F32,
@@ -794,6 +829,9 @@ extern "C" int phew_gemm(const void* A, const void* B, void* Cout, int64_t M, in
   p.K = static_cast<int>(K);
   p.b_mn_major = b_layout == 0 ? 1 : 0;
   p.batch = static_cast<int>(batch);
+  p.batch_inner = static_cast<int>(batch_inner);
+  p.sa_inner = stride_a_inner;
+  p.sb_inner = stride_b_inner;
   p.a_batched = stride_a != 0;
   p.b_batched = stride_b != 0;
   p.C = Cout;
@@ -830,6 +868,27 @@ extern "C" int phew_gemm(const void* A, const void* B, void* Cout, int64_t M, in
   }
   return gemm_dispatch(A, B, p, lda, ldb, stride_a, stride_b, in_dtype, st);
 }
+}  // namespace
+
+extern "C" int phew_gemm(const void* A, const void* B, void* Cout, int64_t M, int64_t N, int64_t K,
+                         int64_t batch, int64_t lda, int64_t ldb, int64_t ldc, int64_t stride_a,
+                         int64_t stride_b, int64_t stride_c, int b_layout, int in_dtype,
+                         int out_dtype, int row_scale, float eps, int* error_flag, void* stream) {
+  return gemm_entry(A, B, Cout, M, N, K, batch, 1, lda, ldb, ldc, stride_a, 0, stride_b, 0, stride_c, b_layout,
+                    in_dtype, out_dtype, row_scale, eps, error_flag, stream);
+}
+
+extern "C" int phew_gemm_batched2(const void* A, const void* B, void* Cout, int64_t M, int64_t N, int64_t K,
+                                  int64_t batch_outer, int64_t batch_inner, int64_t lda, int64_t ldb,
+                                  int64_t ldc, int64_t stride_a_outer, int64_t stride_a_inner,
+                                  int64_t stride_b_outer, int64_t stride_b_inner, int64_t stride_c,
+                                  int b_layout, int in_dtype, int out_dtype, int* error_flag, void* stream) {
+  PHEW_REQUIRE(batch_outer >= 1 && batch_inner >= 1 && batch_outer * batch_inner < 65536,
+               "phew_gemm_batched2: bad batch extents");
+  return gemm_entry(A, B, Cout, M, N, K, batch_outer * batch_inner, batch_inner, lda, ldb, ldc, stride_a_outer,
+                    stride_a_inner, stride_b_outer, stride_b_inner, stride_c, b_layout, in_dtype, out_dtype, 0,
+                    1e-5f, error_flag, stream);
+}
 
 namespace phew {
 namespace gemm {
@@ -838,7 +897,7 @@ namespace gemm {
 int gemm_dispatch(const void* A, const void* B, const Params& p, int64_t lda, int64_t ldb, int64_t stride_a,
                   int64_t stride_b, int in_dtype, cudaStream_t st) {
   const int64_t K = p.K, M = p.M, N = p.N, batch = p.batch;
-  if (uses_tensor_cores(A, B, lda, ldb, stride_a, stride_b, K, in_dtype)) {
+  if (uses_tensor_cores(A, B, lda, ldb, stride_a, stride_b, K, in_dtype, p.sa_inner, p.sb_inner)) {
     const bool bf = in_dtype == PHEW_BF16;
     // Tile choice (every kernel is persistent: one CTA per SM looping over
     // tiles, TMA running ahead across tile boundaries):
@@ -863,15 +922,15 @@ int gemm_dispatch(const void* A, const void* B, const Params& p, int64_t lda, in
   if (in_dtype == PHEW_F32)
     gemm_simt_kernel<float><<<grid, block, 0, st>>>(static_cast<const float*>(A),
                                                     static_cast<const float*>(B), p, lda, ldb,
-                                                    stride_a, stride_b);
+                                                    stride_a, stride_b, p.sa_inner, p.sb_inner);
   else if (in_dtype == PHEW_BF16)
     gemm_simt_kernel<bf16><<<grid, block, 0, st>>>(static_cast<const bf16*>(A),
                                                    static_cast<const bf16*>(B), p, lda, ldb,
-                                                   stride_a, stride_b);
+                                                   stride_a, stride_b, p.sa_inner, p.sb_inner);
   else
     gemm_simt_kernel<f16><<<grid, block, 0, st>>>(static_cast<const f16*>(A),
                                                   static_cast<const f16*>(B), p, lda, ldb,
-                                                  stride_a, stride_b);
+                                                  stride_a, stride_b, p.sa_inner, p.sb_inner);
   return launch_status("gemm_simt_kernel");
 }
 

@@ -91,6 +91,14 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* tm, ui
       "l"(reinterpret_cast<uint64_t>(tm)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* tm, uint64_t* bar, int c0,
+                                            int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
 
 // tcgen05 shared-memory matrix descriptor for a 1024-byte aligned,
 // 128B-swizzled tile.  K-major operands: lbo = 16 (unused), sbo = 1024 (8-row
@@ -238,8 +246,9 @@ inline int make_map_16bit(CUtensorMap* tm, const void* base, bool bf16, int rank
                           const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box) {
   auto fn = encode_fn();
   if (!fn) return set_error(PHEW_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
-  cuuint64_t d[3], s[2];
-  cuuint32_t b[3], e[3] = {1, 1, 1};
+  if (rank < 1 || rank > 4) return set_error(PHEW_ERR_INVALID, "tensor map rank must be 1..4");
+  cuuint64_t d[4], s[3];
+  cuuint32_t b[4], e[4] = {1, 1, 1, 1};
   for (int i = 0; i < rank; ++i) {
     d[i] = dims[i];
     b[i] = box[i];

@@ -224,6 +224,13 @@ def check_device_errors() -> None:
         raise _native.PhewError(code, "a device-side wait timed out (pipeline stalled)")
 
 
+def _two_axes(t) -> bool:
+    """A 4-D operand whose two batch strides are both non-zero or both zero
+    (batched over both axes or broadcast over both), as phew_gemm_batched2
+    takes them."""
+    return t.ndim == 4 and (t.stride(0) == 0) == (t.stride(1) == 0)
+
+
 def _collapse_batch(t, batch_shape) -> int | None:
     """Single element stride over the flattened batch dims, or None."""
     nb = len(batch_shape)
@@ -279,17 +286,39 @@ def matmul(a, b, *, row_scale: bool = False, eps: float = 1e-5) -> array:
         nbatch *= s
 
     ta = a._t.expand(*batch_shape, M, K)
-    if ta.stride(-1) != 1 and K > 1 or _collapse_batch(ta, batch_shape) is None:
-        ta = contiguous_copy(array._wrap(ta))._t
-    lda = ta.stride(-2) if M > 1 else K
-    sa = _collapse_batch(ta, batch_shape)
-
     tb = b._t.expand(*batch_shape, K, N)
     layout = None
     if (tb.stride(-1) == 1 or N == 1) and (K == 1 or tb.stride(-2) >= N):
         layout, ldb = 0, (tb.stride(-2) if K > 1 else N)
     elif (tb.stride(-2) == 1 or K == 1) and (N == 1 or tb.stride(-1) >= K):
         layout, ldb = 1, (tb.stride(-1) if N > 1 else K)
+    if (not row_scale and len(batch_shape) == 2 and M > 1 and K > 1 and layout is not None
+            and ta.stride(-1) == 1 and ta.stride(-2) >= K
+            and (_collapse_batch(ta, batch_shape) is None or _collapse_batch(tb, batch_shape) is None)
+            and _two_axes(ta) and _two_axes(tb)):
+        # (batch, head) views that no single batch stride describes -- q, k
+        # and v sliced out of a fused qkv projection: read in place
+        out = empty(tuple(batch_shape) + (M, N), res)
+        if out.size:
+            _native.call(
+                "phew_gemm_batched2",
+                ctypes.c_void_p(ta.data_ptr()), ctypes.c_void_p(tb.data_ptr()),
+                ctypes.c_void_p(out._t.data_ptr()),
+                M, N, K, batch_shape[0], batch_shape[1], ta.stride(-2), ldb, N,
+                ta.stride(0), ta.stride(1), tb.stride(0), tb.stride(1), M * N,
+                layout, res.code, res.code,
+                ctypes.c_void_p(error_flag().data_ptr()), _stream(),
+            )
+        if squeeze_a:
+            out = reshape(out, out.shape[:-2] + (N,))
+        if squeeze_b:
+            out = reshape(out, out.shape[:-1])
+        return out
+    if ta.stride(-1) != 1 and K > 1 or _collapse_batch(ta, batch_shape) is None:
+        ta = contiguous_copy(array._wrap(ta))._t
+    lda = ta.stride(-2) if M > 1 else K
+    sa = _collapse_batch(ta, batch_shape)
+
     if layout == 1 and _collapse_batch(tb, batch_shape) is None:
         # A K-major B (a transposed view, e.g. k.transpose(0, 1, 3, 2) of a
         # fused qkv projection) whose batch dims do not collapse to one

@@ -30,6 +30,22 @@ def check(got, ref, dtype):
     assert rel < (1e-5 if dtype == np.float32 else 1.6e-2), rel
 
 
+def check_ulps(got, ref, dtype, max_ulps=1):
+    """16-bit products: both sides round an fp32 sum, so they differ by at
+    most one unit in the last place of the output (fp32 sums in a different
+    order straddle a rounding boundary); more means a wrong element.  Outputs
+    far below the typical magnitude (sums that cancel) are held to the unit
+    of 1/64 of it, where fp32 summation order shows."""
+    g = np.asarray(got).astype(np.float64)
+    r = np.asarray(ref).astype(np.float64)
+    assert g.shape == r.shape, (g.shape, r.shape)
+    mant = 7 if dtype is BF16 else 10
+    floor = np.sqrt(np.mean(r * r)) / 64 + 1e-30
+    ulp = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(r), floor))) - mant)
+    err = np.abs(g - r) / ulp
+    assert err.max() <= max_ulps, (err.max(), np.unravel_index(err.argmax(), err.shape))
+
+
 @pytest.fixture(autouse=True)
 def _no_device_errors(mx):
     from phew_b200.ops import check_device_errors
@@ -75,6 +91,37 @@ def test_gemm_k_transposed_from_fused_qkv(mx):
     o = mlx_cpu.array(qkv).reshape(B, T, 3, H, D).transpose(2, 0, 3, 1, 4)
     ref = mlx_cpu.matmul(o[0], o[1].transpose(0, 1, 3, 2))
     check(got, ref, BF16)
+
+
+@pytest.mark.parametrize("dtype", [BF16, np.float16])
+@pytest.mark.parametrize("B,T,H", [(2, 256, 3), (2, 1024, 80)])
+def test_gemm_reads_fused_qkv_in_place(mx, dtype, B, T, H):
+    """q @ k^T and p @ v with q, k, v (batch, head) views of a fused qkv
+    projection: phew_gemm_batched2 reads them through 4-D maps, no copy (the
+    larger case also takes the resident-B mode); checked on a sample of
+    (batch, head) entries."""
+    from phew_b200 import _native
+
+    D = 128
+    rng = np.random.default_rng(T + H)
+    qkv = _rand(rng, (B, T, 3 * H * D), dtype)
+    x = mx.array(qkv).reshape(B, T, 3, H, D).transpose(2, 0, 3, 1, 4)
+    q, k, v = x[0], x[1], x[2]
+    n0 = _native.launch_count()
+    s = q @ k.transpose(0, 1, 3, 2)
+    p = (s * 0.01).astype(getattr(mx, "bfloat16" if dtype is BF16 else "float16"))
+    o = p @ v
+    mx.synchronize()
+    assert _native.launch_count() - n0 <= 4  # two GEMMs and the scale, no copies
+    o_ref = mlx_cpu.array(qkv).reshape(B, T, 3, H, D).transpose(2, 0, 3, 1, 4)
+    s_np, o_np, p_np = np.asarray(s), np.asarray(o), np.asarray(p)
+    for b, h in sorted({(0, 0), (B - 1, H - 1), (B // 2, H // 2), (0, H - 1)}):
+        qb = np.asarray(o_ref[0])[b, h]
+        kb = np.asarray(o_ref[1])[b, h]
+        vb = np.asarray(o_ref[2])[b, h]
+        check_ulps(s_np[b, h], mlx_cpu.matmul(mlx_cpu.array(qb), mlx_cpu.array(np.ascontiguousarray(kb.T))),
+                   dtype)
+        check_ulps(o_np[b, h], mlx_cpu.matmul(mlx_cpu.array(p_np[b, h]), mlx_cpu.array(vb)), dtype)
 
 
 def test_gemm_batched_attention_shapes(mx):

@@ -737,7 +737,15 @@ def run_reference(args) -> None:
         return
     w = WORKLOADS[args.workload]()
     threads = os.cpu_count() or 1
-    for _ in range(max(1, args.warmup)):
+    if w.cpu_sample(threads) is None:
+        # a sweep-internal kernel measured on its own: the reference has no
+        # CPU path for it apart from the sweep's (the default workload)
+        print(json.dumps({"impl": "reference", "metric": w.metric,
+                          "unavailable": f"{args.workload} is a sweep-internal kernel with no CPU "
+                                         "counterpart of its own; the reference arm times the sweep"}),
+              flush=True)
+        return
+    for _ in range(max(0, args.warmup - 1)):
         w.cpu_sample(threads)
     vals, secs = [], []
     sample = ""

@@ -44,6 +44,19 @@ def test_reference_arm_kernel_line():
     assert d["metric"] == "fused_kernel_hbm_gbs" and d["unit"] == "GB/s"
 
 
+def test_reference_arm_sweep_internal_kernel_is_unavailable():
+    """A sweep-internal kernel timed on its own has no CPU path of its own:
+    the reference arm says so in one line and exits 0."""
+    out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--workload",
+                          "qk_scores", "--steps", "2", "--warmup", "1"],
+                         capture_output=True, text=True, timeout=300, cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and "unavailable" in d
+
+
 def test_peaks_and_traffic_helpers():
     sys.path.insert(0, str(ROOT))
     import bench

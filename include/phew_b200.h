@@ -277,6 +277,16 @@ int phew_sdpa(const void* q, const void* k, const void* v, void* o, int64_t batc
               int64_t L, int64_t D, float scale, int causal, int dtype, int* error_flag,
               void* stream);
 
+/* phew_sdpa on [batch][heads][L][D] views with strides of their own (row,
+ * head, batch; elements, positive multiples of 8): q, k and v sliced out of
+ * a fused qkv projection, qkv.reshape(B, T, 3, H, D).transpose(2, 0, 3, 1, 4),
+ * are read in place.  o is contiguous [batch * heads, L, D].  Replaces
+ * the same call site as phew_sdpa. */
+int phew_sdpa_strided(const void* q, const void* k, const void* v, void* o, int64_t batch,
+                      int64_t heads, int64_t L, int64_t D, const int64_t* q_strides,
+                      const int64_t* k_strides, const int64_t* v_strides, float scale, int causal,
+                      int dtype, int* error_flag, void* stream);
+
 /* ---- group-wise quantised weights --------------------------------------- */
 
 /* out[r, c] = T(scales[r, c / g] * q[r, c] + biases[r, c / g]) for codes q

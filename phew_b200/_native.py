@@ -60,6 +60,7 @@ EXPORTED_SYMBOLS = (
     "phew_gemm_batched2",
     "phew_sdpa_supported",
     "phew_sdpa",
+    "phew_sdpa_strided",
     "phew_fill",
     "phew_fill_host",
     "phew_compare_scratch_bytes",
@@ -166,6 +167,11 @@ _SIGNATURES = {
     "phew_sdpa_supported": ([_i64, _i64, _int], _int),
     "phew_sdpa": (
         [_vp, _vp, _vp, _vp, _i64, _i64, _i64, ctypes.c_float, _int, _int, _vp, _vp],
+        _int,
+    ),
+    "phew_sdpa_strided": (
+        [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, ctypes.POINTER(_i64), ctypes.POINTER(_i64),
+         ctypes.POINTER(_i64), ctypes.c_float, _int, _int, _vp, _vp],
         _int,
     ),
     "phew_fill": (

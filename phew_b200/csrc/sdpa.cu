@@ -63,6 +63,7 @@ constexpr float kRescaleThreshold = 8.0f;     // log2 units
 struct Params {
   int L;           // sequence length (multiple of BQ)
   int bh;          // batch * heads
+  int heads;       // (b, h) = (bh / heads, bh % heads): the q / k / v maps are [b][h][L][D] views
   int causal;
   float scale_log2;  // scale * log2(e), > 0
   void* O;
@@ -199,7 +200,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     bh = static_cast<int>(blockIdx.x / n_qb);
   }
   const int q0 = qb * BQ * QT;
-  const int row_base = bh * p.L;  // first row of this (b, h) in the [B*H*L, D] view
+  const int row_base = bh * p.L;  // first row of this (b, h) in the contiguous [B*H*L, D] output
+  const int hh = bh % p.heads, bb = bh / p.heads;  // operand map coordinates of this (b, h)
   const int n_tiles = (q0 + BQ < p.L) ? 2 : 1;
   // key tiles each query tile needs (0 for a missing tile b)
   const int n_kv_a = p.causal ? q0 / BKV + 1 : p.L / BKV;
@@ -225,11 +227,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // This thread is also the TMA producer: start Q_a and K_0 now, before
     // the block-wide sync and the TMEM allocation.
     mbar_expect_tx(q_full, TILE_BYTES);
-    tma_load_2d(sQ, &tmQ, q_full, 0, row_base + q0);
-    tma_load_2d(sQ + HALF_BYTES, &tmQ, q_full, 64, row_base + q0);
+    tma_load_4d(sQ, &tmQ, q_full, 0, q0, hh, bb);
+    tma_load_4d(sQ + HALF_BYTES, &tmQ, q_full, 64, q0, hh, bb);
     mbar_expect_tx(&k_full[0], TILE_BYTES);
-    tma_load_2d(sK, &tmK, &k_full[0], 0, row_base);
-    tma_load_2d(sK + HALF_BYTES, &tmK, &k_full[0], 64, row_base);
+    tma_load_4d(sK, &tmK, &k_full[0], 0, 0, hh, bb);
+    tma_load_4d(sK + HALF_BYTES, &tmK, &k_full[0], 64, 0, hh, bb);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -249,26 +251,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       // then the rings.
       if (n_tiles == 2) {
         mbar_expect_tx(q_full_b, TILE_BYTES);
-        tma_load_2d(sQ + TILE_BYTES, &tmQ, q_full_b, 0, row_base + q0 + BQ);
-        tma_load_2d(sQ + TILE_BYTES + HALF_BYTES, &tmQ, q_full_b, 64, row_base + q0 + BQ);
+        tma_load_4d(sQ + TILE_BYTES, &tmQ, q_full_b, 0, q0 + BQ, hh, bb);
+        tma_load_4d(sQ + TILE_BYTES + HALF_BYTES, &tmQ, q_full_b, 64, q0 + BQ, hh, bb);
       }
       for (int j = 0; j < n_kv_max && ok; ++j) {
         const int s = j & 1;
         const uint32_t ph = ((j >> 1) & 1) ^ 1;
-        const int r = row_base + j * BKV;
+        const int r = j * BKV;  // key row within this (b, h)
         if (j > 0) {
           if (!mbar_wait(&k_empty[s], ph, p.error_flag, p.wait_ns)) { ok = false; break; }
           mbar_expect_tx(&k_full[s], TILE_BYTES);
-          tma_load_2d(sK + s * TILE_BYTES, &tmK, &k_full[s], 0, r);
-          tma_load_2d(sK + s * TILE_BYTES + HALF_BYTES, &tmK, &k_full[s], 64, r);
+          tma_load_4d(sK + s * TILE_BYTES, &tmK, &k_full[s], 0, r, hh, bb);
+          tma_load_4d(sK + s * TILE_BYTES + HALF_BYTES, &tmK, &k_full[s], 64, r, hh, bb);
           if (s) k_last1 = j; else k_last0 = j;
         }
         if (!mbar_wait(&v_empty[s], ph, p.error_flag, p.wait_ns)) { ok = false; break; }
         if (j == p.withhold) continue;  // test hook: this V tile never lands
         if (s) v_last1 = j; else v_last0 = j;
         mbar_expect_tx(&v_full[s], TILE_BYTES);
-        tma_load_2d(sV + s * TILE_BYTES, &tmV, &v_full[s], 0, r);
-        tma_load_2d(sV + s * TILE_BYTES + HALF_BYTES, &tmV, &v_full[s], 64, r);
+        tma_load_4d(sV + s * TILE_BYTES, &tmV, &v_full[s], 0, r, hh, bb);
+        tma_load_4d(sV + s * TILE_BYTES + HALF_BYTES, &tmV, &v_full[s], 64, r, hh, bb);
       }
     }
   } else if (warp == 1) {
@@ -448,21 +450,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// [rows, 128] row-major 16-bit tensor, box = 64 columns x 128 rows, 128B swizzle.
-int make_map(CUtensorMap* tm, const void* base, bool bf16, uint64_t rows) {
-  const uint64_t dims[2] = {static_cast<uint64_t>(D), rows};
-  const uint64_t strides[1] = {static_cast<uint64_t>(D) * 2};
-  const uint32_t box[2] = {64, 128};
-  return make_map_16bit(tm, base, bf16, 2, dims, strides, box);
+// [batch][heads][L][128] 16-bit view: rows `st[0]` elements apart, heads
+// st[1], batches st[2]; box = 64 columns x 128 rows of one (b, h), 128B
+// swizzle.
+int make_map(CUtensorMap* tm, const void* base, bool bf16, uint64_t L, uint64_t heads, uint64_t batch,
+             const int64_t* st) {
+  const uint64_t dims[4] = {static_cast<uint64_t>(D), L, heads, batch};
+  const uint64_t strides[3] = {static_cast<uint64_t>(st[0]) * 2, static_cast<uint64_t>(st[1]) * 2,
+                               static_cast<uint64_t>(st[2]) * 2};
+  const uint32_t box[4] = {64, 128, 1, 1};
+  return make_map_16bit(tm, base, bf16, 4, dims, strides, box);
 }
 
 template <bool BF16>
-int launch(const void* q, const void* k, const void* v, const Params& p, cudaStream_t st) {
+int launch(const void* q, const void* k, const void* v, const int64_t* qs, const int64_t* ks,
+           const int64_t* vs, const Params& p, cudaStream_t st) {
   CUtensorMap tq, tk, tv;
-  const uint64_t rows = static_cast<uint64_t>(p.bh) * p.L;
-  int s = make_map(&tq, q, BF16, rows);
-  if (!s) s = make_map(&tk, k, BF16, rows);
-  if (!s) s = make_map(&tv, v, BF16, rows);
+  const uint64_t heads = static_cast<uint64_t>(p.heads), batch = static_cast<uint64_t>(p.bh / p.heads);
+  int s = make_map(&tq, q, BF16, p.L, heads, batch, qs);
+  if (!s) s = make_map(&tk, k, BF16, p.L, heads, batch, ks);
+  if (!s) s = make_map(&tv, v, BF16, p.L, heads, batch, vs);
   if (s) return s;
   static bool attr = false;
   if (!attr) {
@@ -484,20 +491,25 @@ extern "C" int phew_sdpa_supported(int64_t L, int64_t D, int dtype) {
   return (L > 0 && L % attn::BQ == 0 && D == attn::D && (dtype == PHEW_BF16 || dtype == PHEW_F16)) ? 1 : 0;
 }
 
-extern "C" int phew_sdpa(const void* q, const void* k, const void* v, void* o, int64_t batch_heads,
-                         int64_t L, int64_t D, float scale, int causal, int dtype, int* error_flag,
-                         void* stream) {
+namespace {
+int sdpa_entry(const void* q, const void* k, const void* v, void* o, int64_t batch, int64_t heads, int64_t L,
+               int64_t D, const int64_t* qs, const int64_t* ks, const int64_t* vs, float scale, int causal,
+               int dtype, int* error_flag, void* stream) {
   PHEW_REQUIRE(q && k && v && o, "phew_sdpa: null pointer");
   PHEW_REQUIRE(phew_sdpa_supported(L, D, dtype), "phew_sdpa: needs D == 128, L % 128 == 0, bf16/f16");
-  PHEW_REQUIRE(batch_heads > 0 && batch_heads * L < (1LL << 31), "phew_sdpa: bad batch");
+  PHEW_REQUIRE(batch > 0 && heads > 0 && batch * heads * L < (1LL << 31), "phew_sdpa: bad batch");
   // The row max is taken over the unscaled scores.
   PHEW_REQUIRE(scale > 0.0f, "phew_sdpa: scale must be positive");
   PHEW_REQUIRE(((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
                  reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(o)) & 15) == 0,
                "phew_sdpa: pointers must be 16-byte aligned");
+  for (const int64_t* st : {qs, ks, vs})
+    for (int i = 0; i < 3; ++i)
+      PHEW_REQUIRE(st[i] > 0 && (st[i] * 2) % 16 == 0, "phew_sdpa: strides must be positive multiples of 16 bytes");
   attn::Params p;
   p.L = static_cast<int>(L);
-  p.bh = static_cast<int>(batch_heads);
+  p.bh = static_cast<int>(batch * heads);
+  p.heads = static_cast<int>(heads);
   p.causal = causal ? 1 : 0;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.O = o;
@@ -506,5 +518,24 @@ extern "C" int phew_sdpa(const void* q, const void* k, const void* v, void* o, i
   p.wait_ns = stall.wait_ns;
   p.withhold = stall.withhold;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return dtype == PHEW_BF16 ? attn::launch<true>(q, k, v, p, st) : attn::launch<false>(q, k, v, p, st);
+  return dtype == PHEW_BF16 ? attn::launch<true>(q, k, v, qs, ks, vs, p, st)
+                            : attn::launch<false>(q, k, v, qs, ks, vs, p, st);
+}
+}  // namespace
+
+extern "C" int phew_sdpa(const void* q, const void* k, const void* v, void* o, int64_t batch_heads,
+                         int64_t L, int64_t D, float scale, int causal, int dtype, int* error_flag,
+                         void* stream) {
+  // contiguous [batch_heads, L, D]: one "head" axis of extent 1
+  const int64_t st[3] = {D, L * D, L * D};
+  return sdpa_entry(q, k, v, o, batch_heads, 1, L, D, st, st, st, scale, causal, dtype, error_flag, stream);
+}
+
+extern "C" int phew_sdpa_strided(const void* q, const void* k, const void* v, void* o, int64_t batch,
+                                 int64_t heads, int64_t L, int64_t D, const int64_t* q_strides,
+                                 const int64_t* k_strides, const int64_t* v_strides, float scale, int causal,
+                                 int dtype, int* error_flag, void* stream) {
+  PHEW_REQUIRE(q_strides && k_strides && v_strides, "phew_sdpa_strided: null strides");
+  return sdpa_entry(q, k, v, o, batch, heads, L, D, q_strides, k_strides, v_strides, scale, causal, dtype,
+                    error_flag, stream);
 }

@@ -383,11 +383,11 @@ def scaled_dot_product_attention(q, k, v, *, scale=1.0, mask=None) -> array:
     scale > 0 and mask None / "causal"; any other case is composed from this backend's GEMM
     and softmax kernels (scores materialised in HBM).
     """
-    from .mx.core import astype, softmax, swapaxes
+    from .mx.core import astype, contiguous_copy, softmax, swapaxes
 
-    q = asarray_device(q)
-    k = asarray_device(k)
-    v = asarray_device(v)
+    q = asarray_device(q, contiguous=False)
+    k = asarray_device(k, contiguous=False)
+    v = asarray_device(v, contiguous=False)
     causal = isinstance(mask, str) and mask == "causal"
     if isinstance(mask, str) and not causal:
         raise ValueError(f"unknown mask mode {mask!r}")
@@ -399,11 +399,23 @@ def scaled_dot_product_attention(q, k, v, *, scale=1.0, mask=None) -> array:
     if fast_ok:
         B, H, L, D = q.shape
         out = empty(q.shape, q.dtype)
+        # [B][H][L][D] views read in place when each has unit column stride
+        # and 16-byte row / head / batch strides (q, k, v of a fused qkv
+        # projection); anything else is copied first
+        ts = []
+        for x in (q, k, v):
+            t = x._t
+            st = (t.stride(2), t.stride(1), t.stride(0))
+            if t.stride(3) != 1 or any(s_ <= 0 or s_ % 8 for s_ in st) or t.data_ptr() % 16:
+                t = contiguous_copy(array._wrap(t))._t
+                st = (D, L * D, H * L * D)
+            ts.append((t, (ctypes.c_int64 * 3)(*st)))
+        (tq, sq), (tk, sk), (tv, sv) = ts
         _native.call(
-            "phew_sdpa",
-            ctypes.c_void_p(q._t.data_ptr()), ctypes.c_void_p(k._t.data_ptr()),
-            ctypes.c_void_p(v._t.data_ptr()), ctypes.c_void_p(out._t.data_ptr()),
-            B * H, L, D, ctypes.c_float(scale), 1 if causal else 0, q.dtype.code,
+            "phew_sdpa_strided",
+            ctypes.c_void_p(tq.data_ptr()), ctypes.c_void_p(tk.data_ptr()),
+            ctypes.c_void_p(tv.data_ptr()), ctypes.c_void_p(out._t.data_ptr()),
+            B, H, L, D, sq, sk, sv, ctypes.c_float(scale), 1 if causal else 0, q.dtype.code,
             ctypes.c_void_p(error_flag().data_ptr()), _stream(),
         )
         return out

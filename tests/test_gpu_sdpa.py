@@ -58,6 +58,31 @@ def test_sdpa_fused(mx, dtype, causal, shape):
     check(got, ref, v)
 
 
+@pytest.mark.parametrize("dtype", [BF16, np.float16])
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("B,T,H", [(2, 256, 3), (1, 512, 5)])
+def test_sdpa_reads_fused_qkv_in_place(mx, dtype, causal, B, T, H):
+    """q, k, v as (batch, head) views of a fused qkv projection
+    (qkv.reshape(B, T, 3, H, D).transpose(2, 0, 3, 1, 4)): phew_sdpa_strided
+    reads them through 4-D maps, with no copy."""
+    from phew_b200 import _native
+
+    D = 128
+    rng = np.random.default_rng(T * H + causal)
+    qkv = rng.standard_normal((B, T, 3 * H * D)).astype(np.float32).astype(dtype)
+    x = mx.array(qkv).reshape(B, T, 3, H, D).transpose(2, 0, 3, 1, 4)
+    q, k, v = x[0], x[1], x[2]
+    mask = "causal" if causal else None
+    n0 = _native.launch_count()
+    got = mx.fast.scaled_dot_product_attention(q, k, v, scale=1 / math.sqrt(D), mask=mask)
+    mx.synchronize()
+    assert _native.launch_count() - n0 == 1  # the attention kernel alone
+    o = qkv.reshape(B, T, 3, H, D).transpose(2, 0, 3, 1, 4)
+    qn, kn, vn = (np.ascontiguousarray(o[i]) for i in range(3))
+    ref = mlx_cpu.sdpa(mlx_cpu.array(qn), mlx_cpu.array(kn), mlx_cpu.array(vn), 1 / math.sqrt(D), mask)
+    check(got, ref, vn)
+
+
 def test_sdpa_large_logits(mx):
     """Rows whose maximum grows late exercise the lazy rescaling path."""
     rng = np.random.default_rng(5)
